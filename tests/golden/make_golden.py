@@ -1,0 +1,121 @@
+"""Regenerate the golden fixtures in this directory from FreeML's own CPU path.
+
+Run (in a container that has the FreeML tree and the built harness):
+
+    make -C oracle all
+    python tests/golden/make_golden.py
+
+Every number below comes from ``oracle/_ref/ref_nanollm`` -- the unmodified
+reference ``Model<float, MatrixCPU<float>>`` and its generic operators -- never
+from the oracle restatement or the CUDA code.  The fixtures are small (a few
+hundred KB) so that the CPU test suite can pin the oracle without the
+reference tree.
+"""
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle import oracle as O  # noqa: E402
+
+# (name, shape, weight seed, prompt seed, prompt length, decode steps)
+GREEDY_CASES = [
+    ("cfg1", O.LMShape(V=256, C=128, d=128, H=4, L=4), 0, 1, 16, 112),
+    ("odd", O.LMShape(V=97, C=48, d=64, H=2, L=2), 11, 12, 8, 40),       # non-power-of-two vocab
+]
+# weight-init hashes only (the tensors are too big to commit)
+HASH_CASES = [
+    ("cfg3", O.LMShape(V=4096, C=512, d=512, H=8, L=8), 3),
+]
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def main():
+    assert O.ref_available(), "build oracle/_ref/ref_nanollm first (make -C oracle all)"
+    meta = {"greedy": {}, "weights_sha256": {}}
+    arrays = {}
+    for name, s, wseed, pseed, plen, nnew in GREEDY_CASES:
+        prompt = np.random.RandomState(pseed).randint(0, s.V, plen).astype(np.uint32)
+        toks, logits = O.ref_greedy(s, wseed, prompt, nnew)
+        w = O.ref_weights(s, wseed)
+        window = np.zeros(s.C, np.uint32)
+        window[:toks.size] = toks
+        full = O.ref_forward(s, wseed, window)
+        arrays[f"{name}_prompt"] = prompt
+        arrays[f"{name}_tokens"] = toks
+        arrays[f"{name}_logits"] = logits
+        arrays[f"{name}_window_logits"] = full
+        meta["greedy"][name] = {"V": s.V, "C": s.C, "d": s.d, "H": s.H, "L": s.L, "wseed": wseed,
+                                "pseed": pseed, "plen": plen, "new": nnew,
+                                "weights_sha256": sha(w), "weights_count": int(w.size)}
+        print(name, "tokens", toks[:8], "...")
+    for name, s, wseed in HASH_CASES:
+        w = O.ref_weights(s, wseed)
+        meta["weights_sha256"][name] = {"V": s.V, "C": s.C, "d": s.d, "H": s.H, "L": s.L, "wseed": wseed,
+                                        "sha256": sha(w), "count": int(w.size),
+                                        "first8": [float(x) for x in w[:8]]}
+        print(name, "weights", w.size)
+
+    # single operators on seeded inputs
+    rs = np.random.RandomState(2)
+    M, K, N = 40, 96, 72
+    A = rs.randn(M, K).astype(np.float32)
+    B = (0.02 * rs.randn(K, N)).astype(np.float32)
+    Bt = (0.02 * rs.randn(N, K)).astype(np.float32)
+    g = (1 + 0.1 * rs.randn(K)).astype(np.float32)
+    beta = (0.1 * rs.randn(K)).astype(np.float32)
+    ops = {"A": A, "B": B, "Bt": Bt, "gamma": g, "beta": beta}
+    ops["mul_none"] = O.ref_op("mul_none", [(N, M, 1), (K, M, 1), (N, K, 1)], [A, B]).reshape(M, N)
+    ops["mul_right"] = O.ref_op("mul_right", [(N, M, 1), (K, M, 1), (K, N, 1)], [A, Bt]).reshape(M, N)
+    small = A[:8, :16].copy()
+    ops["small"] = small
+    ops["small_B"] = B[:16, :8].copy()
+    ops["mul_none_small"] = O.ref_op("mul_none", [(8, 8, 1), (16, 8, 1), (8, 16, 1)], [small, ops["small_B"]]).reshape(8, 8)
+    ops["layernorm"] = O.ref_op("layernorm", [(K, M, 1), (K, M, 1), (K, 1, 1)], [A, g]).reshape(M, K)
+    ops["layernorm_beta"] = O.ref_op("layernorm_beta", [(K, M, 1), (K, M, 1), (K, 1, 1), (K, 1, 1)], [A, g, beta]).reshape(M, K)
+    ops["softmax"] = O.ref_op("softmax", [(K, M, 1), (K, M, 1)], [A]).reshape(M, K)
+    ops["gelu"] = O.ref_op("gelu", [(K, M, 1), (K, M, 1)], [A]).reshape(M, K)
+    ops["add"] = O.ref_op("add", [(K, M, 1), (K, M, 1), (K, M, 1)], [A, A[::-1].copy()]).reshape(M, K)
+    mask = np.where(np.tril(np.ones((M, M))) > 0, 0.0, -np.inf).astype(np.float32)
+    S = rs.randn(M, M).astype(np.float32)
+    ops["S"] = S
+    ops["mask"] = mask
+    ops["scale"] = np.array([1.0 / np.sqrt(np.float32(32))], np.float32)
+    ops["scale_add"] = O.ref_op("scale_add", [(M, M, 1), (M, M, 1), (1, 1, 1), (M, M, 1)], [S, ops["scale"], mask]).reshape(M, M)
+    table = rs.randn(50, K).astype(np.float32)
+    idx = rs.randint(0, 50, M).astype(np.float32)
+    ops["table"], ops["idx"] = table, idx
+    ops["gather_rows"] = O.ref_op("gather_rows", [(K, M, 1), (K, 50, 1), (1, M, 1)], [table, idx]).reshape(M, K)
+    # attention core pieces as CausalSelfAttentionLayer uses them: head h of
+    # width hd at column offset h*hd, row stride d
+    T, d, hd, h = 24, 64, 16, 1
+    Q = rs.randn(T, d).astype(np.float32)
+    Kk = rs.randn(T, d).astype(np.float32)
+    P = rs.rand(T, T).astype(np.float32)
+    ops["attn_Q"], ops["attn_K"], ops["attn_P"] = Q, Kk, P
+    ops["strided_right_h1"] = O.ref_op("matmul_strided_right", [(T, T, 1), (d, T, 1), (d, T, 1)], [Q, Kk],
+                                       hd=hd, off=h * hd).reshape(T, T)
+    ops["strided_none_h1"] = O.ref_op("matmul_strided_none", [(d, T, 1), (T, T, 1), (d, T, 1)], [P, Kk],
+                                      hd=hd, off=h * hd).reshape(T, d)
+    packed = rs.randn(M, 3 * 32).astype(np.float32)
+    ops["packed"] = packed
+    zeros = np.zeros((M, 32), np.float32)
+    qkv = O.ref_op("split_qkv", [(32, M, 1), (32, M, 1), (32, M, 1), (96, M, 1)], [zeros, zeros, packed])
+    ops["split_q"], ops["split_k"], ops["split_v"] = (qkv[i * M * 32:(i + 1) * M * 32].reshape(M, 32) for i in range(3))
+
+    np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)
+    np.savez_compressed(os.path.join(HERE, "ops.npz"), **ops)
+    with open(os.path.join(HERE, "golden.json"), "w") as f:
+        json.dump(meta, f, indent=1, sort_keys=True)
+    print("wrote", os.listdir(HERE))
+
+
+if __name__ == "__main__":
+    main()
