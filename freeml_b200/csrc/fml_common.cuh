@@ -1,0 +1,149 @@
+// Shared helpers for the freeml_b200 CUDA library (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/freeml_cuda.h"
+
+namespace fml {
+
+constexpr unsigned FULL_MASK = 0xffffffffu;
+
+// ---- error reporting -------------------------------------------------------
+
+int set_error(int status, const char* fmt, ...);
+std::atomic<uint64_t>& launch_counter();
+
+#define FML_CUDA_TRY(expr)                                                                     \
+    do {                                                                                       \
+        cudaError_t _e = (expr);                                                               \
+        if (_e != cudaSuccess)                                                                 \
+            return ::fml::set_error(FML_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,               \
+                                    cudaGetErrorString(_e), __FILE__, __LINE__);               \
+    } while (0)
+
+// Checks the launch that was just issued and counts it.
+#define FML_LAUNCH_CHECK()                                                                     \
+    do {                                                                                       \
+        cudaError_t _e = cudaGetLastError();                                                   \
+        if (_e != cudaSuccess)                                                                 \
+            return ::fml::set_error(FML_ERR_CUDA, "kernel launch failed: %s (%s:%d)",           \
+                                    cudaGetErrorString(_e), __FILE__, __LINE__);               \
+        ::fml::launch_counter().fetch_add(1, std::memory_order_relaxed);                       \
+    } while (0)
+
+#define FML_REQUIRE(cond, ...)                                                                 \
+    do {                                                                                       \
+        if (!(cond)) return ::fml::set_error(FML_ERR_INVALID, __VA_ARGS__);                    \
+    } while (0)
+
+inline cudaStream_t as_stream(fml_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline unsigned grid_for(uint64_t n, unsigned block, unsigned cap = 148u * 32u)
+{
+    uint64_t g = (n + block - 1) / block;
+    if (g < 1) g = 1;
+    if (g > cap) g = cap;
+    return (unsigned)g;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- device helpers --------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL_MASK, v, o));
+    return v;
+}
+
+// GeluMat's formula (MatrixBase_Functions.h:989-1000): 0.5 x (1 + erf(x / sqrt 2)).
+__device__ __forceinline__ float gelu_exact(float x)
+{
+    return 0.5f * x * (1.0f + erff(x / 1.41421356237309515f));
+}
+
+// Orders floats as unsigned ints (larger float -> larger key).
+__device__ __forceinline__ uint32_t float_order_key(float f)
+{
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// 64-bit argmax key: value in the high word, (~index) in the low word, so an
+// unsigned max picks the largest value and, among equal values, the smallest
+// index -- the reference's strict '>' scan (NanoLLM.cpp:194-201).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx)
+{
+    return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xffffffffu - idx);
+}
+
+__host__ __device__ __forceinline__ uint32_t argmax_key_index(unsigned long long key)
+{
+    return 0xffffffffu - (uint32_t)(key & 0xffffffffull);
+}
+
+// Sum-reduction of C values per lane across a warp without replicating the
+// work: each step exchanges half of the lane's values with the partner lane,
+// so after log2(min(C,32)) steps lane L holds C/32 complete sums (or one sum,
+// replicated over the low lanes, when C < 32).  The value a[i] that lane L
+// ends with is the sum of the original index i + reduce_base<C>(L).
+template <int C>
+__device__ __forceinline__ void warp_transpose_reduce(float (&a)[C], int lane)
+{
+    constexpr int HALV = C >= 32 ? 5 : (C >= 16 ? 4 : (C >= 8 ? 3 : (C >= 4 ? 2 : (C >= 2 ? 1 : 0))));
+#pragma unroll
+    for (int s = 0; s < HALV; ++s)
+    {
+        const int o = 16 >> s;
+        const int n = C >> (s + 1);
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n; ++i)
+        {
+            const float send = up ? a[i] : a[i + n];
+            const float keep = up ? a[i + n] : a[i];
+            a[i] = keep + __shfl_xor_sync(FULL_MASK, send, o);
+        }
+    }
+#pragma unroll
+    for (int s = HALV; s < 5; ++s)
+    {
+        const int o = 16 >> s;
+        a[0] += __shfl_xor_sync(FULL_MASK, a[0], o);
+    }
+}
+
+template <int C>
+__device__ __forceinline__ int reduce_base(int lane)
+{
+    constexpr int HALV = C >= 32 ? 5 : (C >= 16 ? 4 : (C >= 8 ? 3 : (C >= 4 ? 2 : (C >= 2 ? 1 : 0))));
+    int base = 0;
+#pragma unroll
+    for (int s = 0; s < HALV; ++s)
+        if (lane & (16 >> s)) base += C >> (s + 1);
+    return base;
+}
+
+// True for the one lane of each replica group that should publish its sums.
+template <int C>
+__device__ __forceinline__ bool reduce_owner(int lane)
+{
+    constexpr int HALV = C >= 32 ? 5 : (C >= 16 ? 4 : (C >= 8 ? 3 : (C >= 4 ? 2 : (C >= 2 ? 1 : 0))));
+    return (lane & ((1 << (5 - HALV)) - 1)) == 0;
+}
+
+}  // namespace fml

@@ -1,0 +1,1093 @@
+// The decode engine: FreeML's NanoLLM token loop (Examples/NanoLLM/NanoLLM.cpp:
+// 268-358 graph, Model::Run at ModelLibrary/Model.h:764-788, argmax at
+// NanoLLM.cpp:189-204) rebuilt as a KV-cached, batched greedy loop on B200.
+//
+// Per generated token the reference recomputes the whole block_size window.
+// Causality makes row t of that window depend on tokens 0..t only
+// (CausalSelfAttentionLayer.h:66-67 mask; LayerNorm, Dense, Gelu and Add are
+// row-wise), so the engine keeps each layer's K and V rows and computes only
+// the new row: the logits are the reference's row t up to fp32 rounding.
+//
+// HBM layout (fp32):
+//   weights, K-contiguous ("n-major": row n holds the n-th output's inputs)
+//     tok     [V x d]      token table; also the tied lm_head rows
+//     pos     [C x d]      position table
+//     wqkv_t  [L][3d x d]  transpose of Dense_Weights [d x 3d]
+//     wproj   [L][d x d]   Dense_Weights as stored (out x in)
+//     wfc_t   [L][4d x d]  transpose of [d x 4d]
+//     wmlp_t  [L][d x 4d]  transpose of [4d x d]
+//     ln0, ln1 [L][d], lnf [d]
+//   KV cache  kc, vc [L][B][H][C][hd]: one head's rows are contiguous, so a
+//     split of the attention reads one dense block.
+//   state     pending[B] (token to consume), pos[B] (rows held), keys[B]
+//     (packed argmax), split partials + counters for attention.
+//
+// One decode step (B rows), every kernel reading positions and tokens from
+// device memory so that one captured CUDA graph replays for every step:
+//   embed -> L x { layernorm -> qkv gemv (q + K/V-cache scatter) ->
+//   attention (split-KV, last CTA combines) -> proj gemv (+residual) ->
+//   layernorm -> fc gemv (+gelu) -> mlp gemv (+residual) } -> layernorm ->
+//   lm_head gemv (+argmax keys) -> finalize
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "fml_common.cuh"
+
+namespace fml {
+
+int launch_layernorm(float* out, const float* in, const float* gamma, const float* beta, float* xhat, uint32_t rows,
+                     uint32_t cols, uint64_t in_stride, uint64_t out_stride, float eps, cudaStream_t st);
+int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool trans_b,
+             int batch, uint64_t pa, uint64_t pb, uint64_t pc, cudaStream_t st);
+
+// ---------------------------------------------------------------- kernels --
+
+// Embedding GatherRows x2 + AddLayer (Embedding.h:161-170, AddLayer.h:149):
+// x[r] = tok[id] + pos[t].  Decode: r = sequence b, id = pending[b],
+// t = pos[b].  Prefill: r = b*P + t, id = prompt[r].
+__global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ tok, const float* __restrict__ posemb,
+                             const uint32_t* __restrict__ ids, const uint32_t* __restrict__ pos, uint32_t rows,
+                             uint32_t P, uint32_t d, uint32_t V, uint32_t C)
+{
+    for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x)
+    {
+        const uint32_t t = pos ? pos[r] : r % P;
+        uint32_t id = ids[r];
+        const bool ok = id < V && t < C;
+        if (!ok) id = 0;
+        const float4* a = reinterpret_cast<const float4*>(tok + (uint64_t)id * d);
+        const float4* b = reinterpret_cast<const float4*>(posemb + (uint64_t)(ok ? t : 0) * d);
+        float4* o = reinterpret_cast<float4*>(x + (uint64_t)r * d);
+        for (uint32_t c = threadIdx.x; c < d / 4; c += blockDim.x)
+        {
+            const float4 u = a[c], v = b[c];
+            o[c] = ok ? make_float4(u.x + v.x, u.y + v.y, u.z + v.z, u.w + v.w) : make_float4(0, 0, 0, 0);
+        }
+    }
+}
+
+enum GemvEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_ARGMAX = 4 };
+
+struct GemvArgs
+{
+    const float* x;  // [M x K], row stride ldx
+    const float* w;  // [N x K]
+    uint32_t M, N, K, ldx;
+    float* y;        // [M x N], row stride ldy
+    uint32_t ldy;
+    const float* r;  // residual [M x N], row stride ldr (EPI_RESID)
+    uint32_t ldr;
+    // EPI_QKV: columns [0,d) -> q[m*d + n], [d,2d) -> K cache, [2d,3d) -> V cache
+    float* q;
+    float* kc;
+    float* vc;
+    const uint32_t* pos;
+    uint32_t d, H, hd, C;
+    uint64_t seq_stride;  // H*C*hd: one sequence's block inside a layer
+    // EPI_ARGMAX
+    unsigned long long* keys;
+};
+
+// y[m, n] = sum_k x[m, k] W[n, k] for the small-M (decode) shapes.
+// CTA = 4 warps, 4 output columns n; the warps split K (each lane owns 4
+// consecutive k, a float4 of every W row and x row), so every W element is
+// read once per step.  Partial sums are combined by a warp transpose-reduce
+// (each lane ends up owning distinct outputs) and a 4-way shared-memory sum,
+// then the epilogue runs on one thread per output.
+template <int MT, int EPI>
+__global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
+{
+    constexpr int NW = 4;
+    constexpr int CNT = MT * NW;
+    constexpr int R = CNT >= 32 ? CNT / 32 : 1;
+    __shared__ float red[4][CNT];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // blockIdx.x walks the row chunks of one column group, so the CTAs that
+    // share a W slice run together and the slice comes from HBM once
+    const uint32_t n0 = blockIdx.y * NW;
+    const uint32_t m0 = blockIdx.x * MT;
+
+    float acc[CNT];
+#pragma unroll
+    for (int i = 0; i < CNT; ++i) acc[i] = 0.0f;
+
+    const float* wrow[NW];
+#pragma unroll
+    for (int j = 0; j < NW; ++j) wrow[j] = a.w + (uint64_t)min(n0 + j, a.N - 1) * a.K;
+
+    for (uint32_t k = (uint32_t)warp * 128u + (uint32_t)lane * 4u; k < a.K; k += 512u)
+    {
+        float4 wv[NW];
+#pragma unroll
+        for (int j = 0; j < NW; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(wrow[j] + k));
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+        {
+            if (m0 + m < a.M)
+            {
+                const float4 xv = *reinterpret_cast<const float4*>(a.x + (uint64_t)(m0 + m) * a.ldx + k);
+#pragma unroll
+                for (int j = 0; j < NW; ++j)
+                {
+                    float s = acc[m * NW + j];
+                    s = fmaf(xv.x, wv[j].x, s);
+                    s = fmaf(xv.y, wv[j].y, s);
+                    s = fmaf(xv.z, wv[j].z, s);
+                    s = fmaf(xv.w, wv[j].w, s);
+                    acc[m * NW + j] = s;
+                }
+            }
+        }
+    }
+
+    warp_transpose_reduce<CNT>(acc, lane);
+    if (reduce_owner<CNT>(lane))
+    {
+        const int base = reduce_base<CNT>(lane);
+#pragma unroll
+        for (int i = 0; i < R; ++i) red[warp][base + i] = acc[i];
+    }
+    __syncthreads();
+
+    const int t = threadIdx.x;
+    if (t < CNT || EPI == EPI_ARGMAX)
+    {
+        const int tt = t < CNT ? t : 0;
+        const float v = red[0][tt] + red[1][tt] + red[2][tt] + red[3][tt];
+        const uint32_t m = m0 + tt / NW, n = n0 + tt % NW;
+        const bool valid = t < CNT && m < a.M && n < a.N;
+        if constexpr (EPI == EPI_STORE)
+        {
+            if (valid) a.y[(uint64_t)m * a.ldy + n] = v;
+        }
+        else if constexpr (EPI == EPI_GELU)
+        {
+            if (valid) a.y[(uint64_t)m * a.ldy + n] = gelu_exact(v);
+        }
+        else if constexpr (EPI == EPI_RESID)
+        {
+            if (valid) a.y[(uint64_t)m * a.ldy + n] = a.r[(uint64_t)m * a.ldr + n] + v;
+        }
+        else if constexpr (EPI == EPI_QKV)
+        {
+            if (valid)
+            {
+                if (n < a.d) a.q[(uint64_t)m * a.d + n] = v;
+                else
+                {
+                    const uint32_t c = n % a.d, h = c / a.hd, e = c % a.hd;
+                    float* cache = n < 2 * a.d ? a.kc : a.vc;
+                    cache[(uint64_t)m * a.seq_stride + ((uint64_t)h * a.C + a.pos[m]) * a.hd + e] = v;
+                }
+            }
+        }
+        else if constexpr (EPI == EPI_ARGMAX)
+        {
+            // logits (optional) and the per-row argmax over this CTA's 4
+            // columns, folded into the row's global key with one atomicMax.
+            if (valid && a.y) a.y[(uint64_t)m * a.ldy + n] = v;
+            if (t < 32 * ((CNT + 31) / 32))
+            {
+                unsigned long long key = valid ? argmax_key(v, n) : 0ull;
+                unsigned long long o1 = __shfl_xor_sync(FULL_MASK, key, 1);
+                key = o1 > key ? o1 : key;
+                unsigned long long o2 = __shfl_xor_sync(FULL_MASK, key, 2);
+                key = o2 > key ? o2 : key;
+                if (valid && (t % NW) == 0) atomicMax(a.keys + m, key);
+            }
+        }
+    }
+}
+
+// Prefill: scatter the packed QKV rows of (b, t) into q and the cache.
+__global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restrict__ q, float* __restrict__ kc,
+                                   float* __restrict__ vc, uint32_t rows, uint32_t P, uint32_t d, uint32_t hd,
+                                   uint32_t C, uint64_t seq_stride)
+{
+    const uint64_t n = (uint64_t)rows * 3u * d;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint64_t r = i / (3u * d);
+        const uint32_t c3 = (uint32_t)(i - r * 3u * d);
+        const float v = qkv[i];
+        if (c3 < d) { q[r * d + c3] = v; continue; }
+        const uint32_t b = (uint32_t)(r / P), t = (uint32_t)(r % P);
+        const uint32_t c = c3 % d, h = c / hd, e = c % hd;
+        float* cache = c3 < 2 * d ? kc : vc;
+        cache[(uint64_t)b * seq_stride + ((uint64_t)h * C + t) * hd + e] = v;
+    }
+}
+
+struct AttnArgs
+{
+    const float* q;  // row r, head h at q + r*ldq + h*HD
+    uint32_t ldq;
+    uint32_t row0;   // first row of this launch (rows row0 + blockIdx.y)
+    const float* kc;
+    const float* vc;
+    uint64_t seq_stride;  // H*C*HD
+    uint32_t H, C;
+    float* out;      // row r, head h at out + r*ldo + h*HD
+    uint32_t ldo;
+    const uint32_t* pos;  // decode: b = r, t = pos[r]; prefill (null): b = r / P, t = r % P
+    uint32_t P;
+    uint32_t S, chunk;    // splits over the key range, positions per split
+    float scale;          // 1/sqrt(hd), CausalSelfAttentionLayer.h:73-77
+    float* part;          // [B][H][S][HD + 2] split partials
+    uint32_t* counters;   // [B][H]
+};
+
+// Causal attention for one query row over the cached keys 0..t
+// (CausalSelfAttentionLayer.h:424-499: Q_h K_h^T, * 1/sqrt(hd) + causal
+// mask, Softmax, P V_h), as one pass with an online softmax.
+// grid = (H, rows, S); 4 warps per CTA take 32-key tiles in turn.  Per tile a
+// lane holds HD/32 dims of q; the 32 partial dot products are summed by a
+// transpose-reduce, so lane j ends with key j's score; p_j is then
+// broadcast for the P.V update.  With S > 1 each CTA writes (m, l, acc) and
+// the last CTA of the (row, head) to finish merges the S partials.
+template <int HD>
+__global__ void __launch_bounds__(128) attention_kernel(AttnArgs a)
+{
+    constexpr int DPL = HD / 32;
+    __shared__ float sm_m[4], sm_l[4];
+    __shared__ float sm_acc[4][HD];
+    __shared__ int sm_last;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t h = blockIdx.x, r = a.row0 + blockIdx.y, s = blockIdx.z;
+    uint32_t b, t;
+    if (a.pos) { b = r; t = a.pos[r]; }
+    else { b = r / a.P; t = r % a.P; }
+    const uint32_t len = t + 1;
+    const uint32_t begin = s * a.chunk;
+    const uint32_t end = min(len, begin + a.chunk);
+
+    const float* K = a.kc + (uint64_t)b * a.seq_stride + (uint64_t)h * a.C * HD;
+    const float* Vv = a.vc + (uint64_t)b * a.seq_stride + (uint64_t)h * a.C * HD;
+
+    float qv[DPL];
+    const float* qp = a.q + (uint64_t)r * a.ldq + h * HD + lane * DPL;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) qv[i] = qp[i];
+
+    float m_run = -INFINITY, l_run = 0.0f;
+    float acc[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] = 0.0f;
+
+    for (uint32_t j0 = begin + warp * 32u; j0 < end; j0 += 128u)
+    {
+        float part[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj)
+        {
+            float sdot = 0.0f;
+            if (j0 + jj < end)
+            {
+                const float* kr = K + (uint64_t)(j0 + jj) * HD + lane * DPL;
+                if constexpr (DPL == 4)
+                {
+                    const float4 k4 = *reinterpret_cast<const float4*>(kr);
+                    sdot = qv[0] * k4.x + qv[1] * k4.y + qv[2] * k4.z + qv[3] * k4.w;
+                }
+                else if constexpr (DPL == 2)
+                {
+                    const float2 k2 = *reinterpret_cast<const float2*>(kr);
+                    sdot = qv[0] * k2.x + qv[1] * k2.y;
+                }
+                else
+                {
+                    sdot = qv[0] * kr[0];
+                }
+            }
+            part[jj] = sdot;
+        }
+        warp_transpose_reduce<32>(part, lane);
+        // lane now holds the full dot product of key j0 + lane
+        const bool valid = j0 + lane < end;
+        const float sc = valid ? part[0] * a.scale : -INFINITY;
+        const float tile_max = warp_max(sc);
+        const float m_new = fmaxf(m_run, tile_max);
+        const float p = valid ? expf(sc - m_new) : 0.0f;
+        const float corr = expf(m_run - m_new);
+        l_run = l_run * corr + warp_sum(p);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] *= corr;
+        const uint32_t nvalid = min(32u, end - j0);
+        for (uint32_t jj = 0; jj < nvalid; ++jj)
+        {
+            const float pj = __shfl_sync(FULL_MASK, p, jj);
+            const float* vr = Vv + (uint64_t)(j0 + jj) * HD + lane * DPL;
+            if constexpr (DPL == 4)
+            {
+                const float4 v4 = *reinterpret_cast<const float4*>(vr);
+                acc[0] = fmaf(pj, v4.x, acc[0]);
+                acc[1] = fmaf(pj, v4.y, acc[1]);
+                acc[2] = fmaf(pj, v4.z, acc[2]);
+                acc[3] = fmaf(pj, v4.w, acc[3]);
+            }
+            else if constexpr (DPL == 2)
+            {
+                const float2 v2 = *reinterpret_cast<const float2*>(vr);
+                acc[0] = fmaf(pj, v2.x, acc[0]);
+                acc[1] = fmaf(pj, v2.y, acc[1]);
+            }
+            else
+            {
+                acc[0] = fmaf(pj, vr[0], acc[0]);
+            }
+        }
+        m_run = m_new;
+    }
+
+    if (lane == 0) { sm_m[warp] = m_run; sm_l[warp] = l_run; }
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) sm_acc[warp][lane * DPL + i] = acc[i];
+    __syncthreads();
+
+    // merge the 4 warps
+    const float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
+    float w4[4];
+    float L = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        w4[i] = (M == -INFINITY) ? 0.0f : expf(sm_m[i] - M);
+        L += sm_l[i] * w4[i];
+    }
+    const int e = threadIdx.x;
+    if (a.S == 1)
+    {
+        if (e < HD)
+        {
+            const float A = sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3];
+            a.out[(uint64_t)r * a.ldo + h * HD + e] = A / L;
+        }
+        return;
+    }
+
+    float* mypart = a.part + (((uint64_t)b * a.H + h) * a.S + s) * (HD + 2);
+    if (e < HD)
+        mypart[e] = sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3];
+    if (e == 0) { mypart[HD] = M; mypart[HD + 1] = L; }
+    __threadfence();
+    __syncthreads();
+    if (e == 0)
+    {
+        const uint32_t prev = atomicAdd(a.counters + (uint64_t)b * a.H + h, 1u);
+        sm_last = (prev == a.S - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!sm_last) return;
+    __threadfence();
+    const float* parts = a.part + ((uint64_t)b * a.H + h) * a.S * (HD + 2);
+    float Mg = -INFINITY;
+    for (uint32_t i = 0; i < a.S; ++i) Mg = fmaxf(Mg, __ldcg(parts + i * (HD + 2) + HD));
+    float Lg = 0.0f, Ag = 0.0f;
+    for (uint32_t i = 0; i < a.S; ++i)
+    {
+        const float mi = __ldcg(parts + i * (HD + 2) + HD);
+        const float wi = (mi == -INFINITY) ? 0.0f : expf(mi - Mg);
+        Lg += __ldcg(parts + i * (HD + 2) + HD + 1) * wi;
+        if (e < HD) Ag += __ldcg(parts + i * (HD + 2) + e) * wi;
+    }
+    if (e < HD) a.out[(uint64_t)r * a.ldo + h * HD + e] = Ag / Lg;
+    if (e == 0) a.counters[(uint64_t)b * a.H + h] = 0u;
+}
+
+// After lm_head: pending token = argmax, advance the position, reset keys.
+__global__ void finalize_kernel(unsigned long long* keys, uint32_t* pending, uint32_t* pos, uint32_t* next_out,
+                                uint32_t B, uint32_t set_pos)
+{
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const uint32_t tok = argmax_key_index(keys[b]);
+    pending[b] = tok;
+    if (next_out) next_out[b] = tok;
+    pos[b] = set_pos ? set_pos : pos[b] + 1u;
+    keys[b] = 0ull;
+}
+
+// out[c * rows + r] = in[r * cols + c]: repack a [rows x cols] weight into
+// [cols x rows] (K-contiguous) at bind time.
+__global__ void transpose_kernel(float* __restrict__ out, const float* __restrict__ in, uint32_t rows, uint32_t cols)
+{
+    __shared__ float tile[32][33];
+    const uint32_t c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (uint32_t i = threadIdx.y; i < 32; i += blockDim.y)
+    {
+        const uint32_t r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = in[(uint64_t)r * cols + c];
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.y; i < 32; i += blockDim.y)
+    {
+        const uint32_t c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) out[(uint64_t)c * rows + r] = tile[threadIdx.x][i];
+    }
+}
+
+__global__ void rewind_kernel(uint32_t* pos, uint32_t* pending, const uint32_t* src, uint32_t B, uint32_t p)
+{
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    pos[b] = p;
+    if (src) pending[b] = src[b];
+}
+
+__global__ void gelu_inplace_kernel(float* x, uint64_t n)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        x[i] = gelu_exact(x[i]);
+}
+
+__global__ void add_kernel(float* out, const float* a, const float* b, uint64_t n)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = a[i] + b[i];
+}
+
+}  // namespace fml
+
+using namespace fml;
+
+// ---------------------------------------------------------------- engine --
+
+struct fml_lm
+{
+    fml_lm_config cfg{};
+    int device = 0;
+    uint32_t hd = 0;
+    bool bound = false;
+
+    // weights
+    float* wbuf = nullptr;  // one allocation for every parameter
+    float *tok = nullptr, *pos_emb = nullptr, *lnf = nullptr;
+    std::vector<float*> ln0, ln1, wqkv, wproj, wfc, wmlp;
+
+    // KV cache
+    float *kc = nullptr, *vc = nullptr;
+    uint64_t layer_stride = 0, seq_stride = 0;
+
+    // activations (prefill rows = max_batch * context; decode uses the first rows)
+    float *x = nullptr, *buf = nullptr, *ln = nullptr, *q = nullptr, *att = nullptr, *tmp = nullptr, *hid = nullptr;
+
+    // state
+    uint32_t* pending = nullptr;
+    uint32_t* pos = nullptr;
+    uint32_t* prompt_dev = nullptr;
+    unsigned long long* keys = nullptr;
+    float* part = nullptr;
+    uint32_t* counters = nullptr;
+    uint32_t* host_io = nullptr;  // pinned [2 * max_batch]
+    uint32_t S = 1, chunk = 0;
+
+    uint32_t batch = 0;                // active sequences
+    std::vector<uint32_t> hpos;        // host mirror of positions
+
+    // graph
+    bool use_graph = true;
+    cudaGraphExec_t graph_exec = nullptr;
+    cudaStream_t graph_stream = nullptr;
+    uint32_t* graph_next = nullptr;
+    float* graph_logits = nullptr;
+    uint32_t graph_batch = 0;
+
+    // profiling
+    bool profiling = false;
+    double prof_ms[FML_LM_NCLASS] = {};
+    uint64_t prof_n[FML_LM_NCLASS] = {};
+    std::vector<cudaEvent_t> ev_pool;
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> ev_pending;
+    size_t ev_used = 0;
+};
+
+namespace {
+
+uint64_t param_count(const fml_lm_config& c)
+{
+    const uint64_t d = c.d_model;
+    return (uint64_t)c.vocab * d + (uint64_t)c.context * d + (uint64_t)c.n_layer * (2 * d + 12 * d * d) + d;
+}
+
+void free_all(fml_lm* lm)
+{
+    if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
+    for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
+    void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
+                    lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
+                    lm->counters, lm->prompt_dev};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    if (lm->host_io) cudaFreeHost(lm->host_io);
+}
+
+// Event-pair timing of one kernel class (profiling mode only).
+struct ProfScope
+{
+    fml_lm* lm;
+    int cls;
+    cudaStream_t st;
+    cudaEvent_t b = nullptr, e = nullptr;
+    ProfScope(fml_lm* l, int c, cudaStream_t s) : lm(l), cls(c), st(s)
+    {
+        if (!lm->profiling) return;
+        while (lm->ev_pool.size() < lm->ev_used + 2)
+        {
+            cudaEvent_t ev;
+            cudaEventCreate(&ev);
+            lm->ev_pool.push_back(ev);
+        }
+        b = lm->ev_pool[lm->ev_used++];
+        e = lm->ev_pool[lm->ev_used++];
+        cudaEventRecord(b, st);
+    }
+    ~ProfScope()
+    {
+        if (!b) return;
+        cudaEventRecord(e, st);
+        lm->ev_pending.push_back({cls, {b, e}});
+    }
+};
+
+int collect_profile(fml_lm* lm)
+{
+    if (lm->ev_pending.empty()) return FML_OK;
+    FML_CUDA_TRY(cudaEventSynchronize(lm->ev_pending.back().second.second));
+    for (auto& p : lm->ev_pending)
+    {
+        float ms = 0.0f;
+        FML_CUDA_TRY(cudaEventElapsedTime(&ms, p.second.first, p.second.second));
+        lm->prof_ms[p.first] += ms;
+        lm->prof_n[p.first] += 1;
+    }
+    lm->ev_pending.clear();
+    lm->ev_used = 0;
+    return FML_OK;
+}
+
+template <int EPI>
+int launch_gemv(const GemvArgs& a, cudaStream_t st)
+{
+    FML_REQUIRE(a.K % 4 == 0 && a.ldx % 4 == 0, "gemv: K and ldx must be multiples of 4");
+    const unsigned gy = (a.N + 3) / 4;
+    FML_REQUIRE(gy <= 65535u, "gemv: N = %u too large", a.N);
+    if (a.M <= 4) gemv_kernel<4, EPI><<<dim3(1, gy), 128, 0, st>>>(a);
+    else if (a.M <= 8) gemv_kernel<8, EPI><<<dim3(1, gy), 128, 0, st>>>(a);
+    else gemv_kernel<16, EPI><<<dim3((a.M + 15) / 16, gy), 128, 0, st>>>(a);
+    FML_LAUNCH_CHECK();
+    return FML_OK;
+}
+
+int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, const uint32_t* pos, uint32_t P,
+                     uint32_t S, uint32_t chunk, cudaStream_t st)
+{
+    AttnArgs a{};
+    a.row0 = row0;
+    a.q = lm->q;
+    a.ldq = lm->cfg.d_model;
+    a.kc = lm->kc + (uint64_t)layer * lm->layer_stride;
+    a.vc = lm->vc + (uint64_t)layer * lm->layer_stride;
+    a.seq_stride = lm->seq_stride;
+    a.H = lm->cfg.n_head;
+    a.C = lm->cfg.context;
+    a.out = lm->att;
+    a.ldo = lm->cfg.d_model;
+    a.pos = pos;
+    a.P = P;
+    a.S = S;
+    a.chunk = chunk;
+    a.scale = 1.0f / sqrtf((float)lm->hd);
+    a.part = lm->part;
+    a.counters = lm->counters;
+    dim3 grid(lm->cfg.n_head, rows, S);
+    FML_REQUIRE(rows <= 65535u, "attention: too many rows in one launch (%u)", rows);
+    switch (lm->hd)
+    {
+    case 32: attention_kernel<32><<<grid, 128, 0, st>>>(a); break;
+    case 64: attention_kernel<64><<<grid, 128, 0, st>>>(a); break;
+    case 128: attention_kernel<128><<<grid, 128, 0, st>>>(a); break;
+    default: return set_error(FML_ERR_UNSUPPORTED, "head dim %u not supported (32/64/128)", lm->hd);
+    }
+    FML_LAUNCH_CHECK();
+    return FML_OK;
+}
+
+#define FML_RC(expr)                   \
+    do {                               \
+        int _rc = (expr);              \
+        if (_rc != FML_OK) return _rc; \
+    } while (0)
+
+// Enqueue one decode step for the active batch.
+int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
+{
+    const fml_lm_config& c = lm->cfg;
+    const uint32_t B = lm->batch, d = c.d_model;
+    {
+        ProfScope ps(lm, 0, st);
+        embed_kernel<<<B, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->pending, lm->pos, B, 1, d, c.vocab, c.context);
+        FML_LAUNCH_CHECK();
+    }
+    for (uint32_t l = 0; l < c.n_layer; ++l)
+    {
+        {
+            ProfScope ps(lm, 1, st);
+            FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
+        }
+        {
+            ProfScope ps(lm, 2, st);
+            GemvArgs a{};
+            a.x = lm->ln; a.ldx = d; a.w = lm->wqkv[l]; a.M = B; a.N = 3 * d; a.K = d;
+            a.q = lm->q; a.kc = lm->kc + (uint64_t)l * lm->layer_stride; a.vc = lm->vc + (uint64_t)l * lm->layer_stride;
+            a.pos = lm->pos; a.d = d; a.H = c.n_head; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
+            FML_RC(launch_gemv<EPI_QKV>(a, st));
+        }
+        {
+            ProfScope ps(lm, 3, st);
+            FML_RC(launch_attention(lm, l, 0, B, lm->pos, 1, lm->S, lm->chunk, st));
+        }
+        {
+            ProfScope ps(lm, 4, st);
+            GemvArgs a{};
+            a.x = lm->att; a.ldx = d; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = d;
+            a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
+            FML_RC(launch_gemv<EPI_RESID>(a, st));
+        }
+        {
+            ProfScope ps(lm, 1, st);
+            FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
+        }
+        {
+            ProfScope ps(lm, 5, st);
+            GemvArgs a{};
+            a.x = lm->ln; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = 4 * d; a.K = d;
+            a.y = lm->hid; a.ldy = 4 * d;
+            FML_RC(launch_gemv<EPI_GELU>(a, st));
+        }
+        {
+            ProfScope ps(lm, 6, st);
+            GemvArgs a{};
+            a.x = lm->hid; a.ldx = 4 * d; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = 4 * d;
+            a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
+            FML_RC(launch_gemv<EPI_RESID>(a, st));
+        }
+    }
+    {
+        ProfScope ps(lm, 1, st);
+        FML_RC(launch_layernorm(lm->ln, lm->x, lm->lnf, nullptr, nullptr, B, d, d, d, 1e-5f, st));
+    }
+    {
+        ProfScope ps(lm, 7, st);
+        GemvArgs a{};
+        a.x = lm->ln; a.ldx = d; a.w = lm->tok; a.M = B; a.N = c.vocab; a.K = d;
+        a.y = logits; a.ldy = c.vocab; a.keys = lm->keys;
+        FML_RC(launch_gemv<EPI_ARGMAX>(a, st));
+    }
+    {
+        ProfScope ps(lm, 8, st);
+        finalize_kernel<<<(B + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, next_out, B, 0);
+        FML_LAUNCH_CHECK();
+    }
+    return FML_OK;
+}
+
+uint32_t graph_nodes_per_step(const fml_lm_config& c) { return 1 + c.n_layer * 7 + 3; }
+
+}  // namespace
+
+extern "C" {
+
+uint64_t fml_lm_param_count(const fml_lm_config* cfg) { return cfg ? param_count(*cfg) : 0; }
+
+int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
+{
+    FML_REQUIRE(cfg && out, "fml_lm_create: null argument");
+    const fml_lm_config c = *cfg;
+    FML_REQUIRE(c.vocab && c.context && c.d_model && c.n_head && c.n_layer && c.max_batch,
+                "fml_lm_create: zero-sized dimension");
+    FML_REQUIRE(c.d_model % c.n_head == 0, "fml_lm_create: d_model %% n_head != 0");
+    const uint32_t hd = c.d_model / c.n_head;
+    if (hd != 32 && hd != 64 && hd != 128)
+        return set_error(FML_ERR_UNSUPPORTED, "fml_lm_create: head dim %u (need 32, 64 or 128)", hd);
+    FML_REQUIRE(c.d_model % 4 == 0, "fml_lm_create: d_model must be a multiple of 4");
+    FML_CUDA_TRY(cudaSetDevice(device));
+    fml_lm* lm = new fml_lm();
+    lm->cfg = c;
+    lm->device = device;
+    lm->hd = hd;
+    lm->hpos.assign(c.max_batch, 0);
+
+    const uint64_t d = c.d_model, B = c.max_batch, Ctx = c.context, L = c.n_layer, H = c.n_head;
+    lm->seq_stride = H * Ctx * hd;
+    lm->layer_stride = B * lm->seq_stride;
+    const uint64_t rows = B * Ctx;
+
+    // attention split: enough CTAs for ~2 waves of 148 SMs at full batch,
+    // each split a multiple of 32 keys
+    {
+        const uint64_t pairs = B * H;
+        uint64_t S = (2 * 148 + pairs - 1) / pairs;
+        const uint64_t max_s = (Ctx + 31) / 32;
+        if (S > max_s) S = max_s;
+        if (S < 1) S = 1;
+        uint64_t chunk = (Ctx + S - 1) / S;
+        chunk = (chunk + 31) / 32 * 32;
+        S = (Ctx + chunk - 1) / chunk;
+        lm->S = (uint32_t)S;
+        lm->chunk = (uint32_t)chunk;
+    }
+
+    auto alloc = [&](void** p, uint64_t bytes) -> int {
+        cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+        if (e != cudaSuccess)
+        {
+            cudaGetLastError();
+            return set_error(FML_ERR_NOMEM, "cudaMalloc(%llu bytes) failed: %s", (unsigned long long)bytes,
+                             cudaGetErrorString(e));
+        }
+        return FML_OK;
+    };
+    int rc = FML_OK;
+    const uint64_t f = sizeof(float);
+    if (!rc) rc = alloc((void**)&lm->wbuf, param_count(c) * f);
+    if (!rc) rc = alloc((void**)&lm->kc, L * lm->layer_stride * f);
+    if (!rc) rc = alloc((void**)&lm->vc, L * lm->layer_stride * f);
+    if (!rc) rc = alloc((void**)&lm->x, rows * d * f);
+    if (!rc) rc = alloc((void**)&lm->buf, rows * d * f);
+    if (!rc) rc = alloc((void**)&lm->ln, rows * d * f);
+    if (!rc) rc = alloc((void**)&lm->q, rows * d * f);
+    if (!rc) rc = alloc((void**)&lm->att, rows * d * f);
+    if (!rc) rc = alloc((void**)&lm->tmp, rows * 3 * d * f);
+    if (!rc) rc = alloc((void**)&lm->hid, rows * 4 * d * f);
+    if (!rc) rc = alloc((void**)&lm->pending, B * 4);
+    if (!rc) rc = alloc((void**)&lm->pos, B * 4);
+    if (!rc) rc = alloc((void**)&lm->prompt_dev, rows * 4);
+    if (!rc) rc = alloc((void**)&lm->keys, B * 8);
+    if (!rc) rc = alloc((void**)&lm->part, B * H * lm->S * (hd + 2) * f);
+    if (!rc) rc = alloc((void**)&lm->counters, B * H * 4);
+    if (!rc && cudaMallocHost((void**)&lm->host_io, 2 * B * 4) != cudaSuccess)
+        rc = set_error(FML_ERR_NOMEM, "cudaMallocHost failed");
+    if (rc)
+    {
+        free_all(lm);
+        delete lm;
+        return rc;
+    }
+    cudaMemset(lm->pending, 0, B * 4);
+    cudaMemset(lm->pos, 0, B * 4);
+    cudaMemset(lm->keys, 0, B * 8);
+    cudaMemset(lm->counters, 0, B * H * 4);
+
+    // carve the weight buffer
+    float* p = lm->wbuf;
+    lm->tok = p; p += (uint64_t)c.vocab * d;
+    lm->pos_emb = p; p += Ctx * d;
+    for (uint32_t l = 0; l < L; ++l)
+    {
+        lm->ln0.push_back(p); p += d;
+        lm->wqkv.push_back(p); p += 3 * d * d;
+        lm->wproj.push_back(p); p += d * d;
+        lm->ln1.push_back(p); p += d;
+        lm->wfc.push_back(p); p += 4 * d * d;
+        lm->wmlp.push_back(p); p += 4 * d * d;
+    }
+    lm->lnf = p;
+    FML_CUDA_TRY(cudaDeviceSynchronize());
+    *out = lm;
+    return FML_OK;
+}
+
+int fml_lm_destroy(fml_lm* lm)
+{
+    if (!lm) return FML_OK;
+    cudaSetDevice(lm->device);
+    cudaDeviceSynchronize();
+    free_all(lm);
+    delete lm;
+    return FML_OK;
+}
+
+int fml_lm_bind_weights(fml_lm* lm, const fml_lm_weights* w, fml_stream_t stream)
+{
+    FML_REQUIRE(lm && w && w->tok_emb && w->pos_emb && w->lnf && w->ln0 && w->wqkv && w->wproj && w->ln1 && w->wfc &&
+                    w->wmlp,
+                "fml_lm_bind_weights: null pointer");
+    cudaStream_t st = as_stream(stream);
+    const fml_lm_config& c = lm->cfg;
+    const uint64_t d = c.d_model, f = sizeof(float);
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->tok, w->tok_emb, (uint64_t)c.vocab * d * f, cudaMemcpyDeviceToDevice, st));
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->pos_emb, w->pos_emb, (uint64_t)c.context * d * f, cudaMemcpyDeviceToDevice, st));
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->lnf, w->lnf, d * f, cudaMemcpyDeviceToDevice, st));
+    const dim3 tb(32, 8);
+    auto tr = [&](float* dst, const float* src, uint32_t rows, uint32_t cols) -> int {
+        FML_REQUIRE(src, "fml_lm_bind_weights: null layer weight");
+        transpose_kernel<<<dim3((cols + 31) / 32, (rows + 31) / 32), tb, 0, st>>>(dst, src, rows, cols);
+        FML_LAUNCH_CHECK();
+        return FML_OK;
+    };
+    for (uint32_t l = 0; l < c.n_layer; ++l)
+    {
+        FML_REQUIRE(w->ln0[l] && w->ln1[l] && w->wproj[l], "fml_lm_bind_weights: null layer weight");
+        FML_CUDA_TRY(cudaMemcpyAsync(lm->ln0[l], w->ln0[l], d * f, cudaMemcpyDeviceToDevice, st));
+        FML_CUDA_TRY(cudaMemcpyAsync(lm->ln1[l], w->ln1[l], d * f, cudaMemcpyDeviceToDevice, st));
+        FML_CUDA_TRY(cudaMemcpyAsync(lm->wproj[l], w->wproj[l], d * d * f, cudaMemcpyDeviceToDevice, st));
+        FML_RC(tr(lm->wqkv[l], w->wqkv[l], (uint32_t)d, (uint32_t)(3 * d)));
+        FML_RC(tr(lm->wfc[l], w->wfc[l], (uint32_t)d, (uint32_t)(4 * d)));
+        FML_RC(tr(lm->wmlp[l], w->wmlp[l], (uint32_t)(4 * d), (uint32_t)d));
+    }
+    FML_CUDA_TRY(cudaStreamSynchronize(st));
+    lm->bound = true;
+    return FML_OK;
+}
+
+int fml_lm_bind_packed(fml_lm* lm, const float* params, int params_on_host, fml_stream_t stream)
+{
+    FML_REQUIRE(lm && params, "fml_lm_bind_packed: null argument");
+    const fml_lm_config& c = lm->cfg;
+    const uint64_t n = param_count(c), d = c.d_model;
+    const float* src = params;
+    float* staging = nullptr;
+    if (params_on_host)
+    {
+        FML_CUDA_TRY(cudaMalloc(&staging, n * sizeof(float)));
+        cudaError_t e = cudaMemcpy(staging, params, n * sizeof(float), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess)
+        {
+            cudaFree(staging);
+            return set_error(FML_ERR_CUDA, "cudaMemcpy params: %s", cudaGetErrorString(e));
+        }
+        src = staging;
+    }
+    std::vector<const float*> ln0, wqkv, wproj, ln1, wfc, wmlp;
+    const float* p = src + (uint64_t)c.vocab * d + (uint64_t)c.context * d;
+    for (uint32_t l = 0; l < c.n_layer; ++l)
+    {
+        ln0.push_back(p); p += d;
+        wqkv.push_back(p); p += 3 * d * d;
+        wproj.push_back(p); p += d * d;
+        ln1.push_back(p); p += d;
+        wfc.push_back(p); p += 4 * d * d;
+        wmlp.push_back(p); p += 4 * d * d;
+    }
+    fml_lm_weights w{};
+    w.tok_emb = src;
+    w.pos_emb = src + (uint64_t)c.vocab * d;
+    w.ln0 = ln0.data(); w.wqkv = wqkv.data(); w.wproj = wproj.data();
+    w.ln1 = ln1.data(); w.wfc = wfc.data(); w.wmlp = wmlp.data();
+    w.lnf = p;
+    int rc = fml_lm_bind_weights(lm, &w, stream);
+    if (staging) cudaFree(staging);
+    return rc;
+}
+
+int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t P, fml_stream_t stream)
+{
+    FML_REQUIRE(lm && prompts, "fml_lm_prefill: null argument");
+    if (!lm->bound) return set_error(FML_ERR_STATE, "fml_lm_prefill: weights not bound");
+    const fml_lm_config& c = lm->cfg;
+    FML_REQUIRE(batch >= 1 && batch <= c.max_batch, "fml_lm_prefill: batch %u outside [1, %u]", batch, c.max_batch);
+    FML_REQUIRE(P >= 1 && P < c.context, "fml_lm_prefill: prompt length %u outside [1, %u)", P, c.context);
+    cudaStream_t st = as_stream(stream);
+    const uint32_t d = c.d_model, R = batch * P;
+    lm->batch = batch;
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->prompt_dev, prompts, (uint64_t)R * 4, cudaMemcpyDeviceToDevice, st));
+    FML_CUDA_TRY(cudaMemsetAsync(lm->keys, 0, (uint64_t)c.max_batch * 8, st));
+    embed_kernel<<<R < 65535u ? R : 65535u, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->prompt_dev, nullptr, R, P, d,
+                                                          c.vocab, c.context);
+    FML_LAUNCH_CHECK();
+    const uint64_t n = (uint64_t)R * d;
+    for (uint32_t l = 0; l < c.n_layer; ++l)
+    {
+        float* kc = lm->kc + (uint64_t)l * lm->layer_stride;
+        float* vc = lm->vc + (uint64_t)l * lm->layer_stride;
+        FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
+        FML_RC(gemm_f32(lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * d), (int)d, (int)d, (int)d, (int)(3 * d), true,
+                        1, 0, 0, 0, st));
+        qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * d, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, d, lm->hd,
+                                                                              c.context, lm->seq_stride);
+        FML_LAUNCH_CHECK();
+        // prefill attention: one query row per (b, t), the whole causal key
+        // range in one CTA, launched in slabs of at most 65535 rows
+        for (uint32_t r0 = 0; r0 < R; r0 += 65535u)
+            FML_RC(launch_attention(lm, l, r0, R - r0 < 65535u ? R - r0 : 65535u, nullptr, P, 1, c.context, st));
+        FML_RC(gemm_f32(lm->tmp, lm->att, lm->wproj[l], (int)R, (int)d, (int)d, (int)d, (int)d, (int)d, true, 1, 0, 0,
+                        0, st));
+        add_kernel<<<grid_for(n, 256), 256, 0, st>>>(lm->buf, lm->x, lm->tmp, n);
+        FML_LAUNCH_CHECK();
+        FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
+        FML_RC(gemm_f32(lm->hid, lm->ln, lm->wfc[l], (int)R, (int)(4 * d), (int)d, (int)d, (int)d, (int)(4 * d), true, 1,
+                        0, 0, 0, st));
+        gelu_inplace_kernel<<<grid_for(n * 4, 256), 256, 0, st>>>(lm->hid, n * 4);
+        FML_LAUNCH_CHECK();
+        FML_RC(gemm_f32(lm->tmp, lm->hid, lm->wmlp[l], (int)R, (int)d, (int)(4 * d), (int)(4 * d), (int)(4 * d), (int)d,
+                        true, 1, 0, 0, 0, st));
+        add_kernel<<<grid_for(n, 256), 256, 0, st>>>(lm->x, lm->buf, lm->tmp, n);
+        FML_LAUNCH_CHECK();
+    }
+    // last prompt row of each sequence -> ln_f -> lm_head argmax
+    FML_RC(launch_layernorm(lm->ln, lm->x + (uint64_t)(P - 1) * d, lm->lnf, nullptr, nullptr, batch, d,
+                            (uint64_t)P * d, d, 1e-5f, st));
+    GemvArgs a{};
+    a.x = lm->ln; a.ldx = d; a.w = lm->tok; a.M = batch; a.N = c.vocab; a.K = d; a.y = nullptr; a.ldy = c.vocab;
+    a.keys = lm->keys;
+    FML_RC(launch_gemv<EPI_ARGMAX>(a, st));
+    finalize_kernel<<<(batch + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, nullptr, batch, P);
+    FML_LAUNCH_CHECK();
+    for (uint32_t b = 0; b < batch; ++b) lm->hpos[b] = P;
+    return FML_OK;
+}
+
+int fml_lm_set_graph(fml_lm* lm, int use_graph)
+{
+    FML_REQUIRE(lm, "fml_lm_set_graph: null engine");
+    lm->use_graph = use_graph != 0;
+    return FML_OK;
+}
+
+int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t stream)
+{
+    FML_REQUIRE(lm, "fml_lm_step: null engine");
+    if (!lm->bound || lm->batch == 0) return set_error(FML_ERR_STATE, "fml_lm_step: call fml_lm_prefill first");
+    for (uint32_t b = 0; b < lm->batch; ++b)
+        if (lm->hpos[b] >= lm->cfg.context)
+            return set_error(FML_ERR_STATE, "fml_lm_step: sequence %u is at the context limit (%u)", b,
+                             lm->cfg.context);
+    cudaStream_t st = as_stream(stream);
+    if (lm->use_graph && !lm->profiling)
+    {
+        if (!lm->graph_exec || lm->graph_next != next_tokens || lm->graph_logits != logits ||
+            lm->graph_batch != lm->batch)
+        {
+            if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
+            lm->graph_exec = nullptr;
+            cudaStream_t cap;
+            FML_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+            FML_CUDA_TRY(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
+            int rc = enqueue_step(lm, next_tokens, logits, cap);
+            cudaGraph_t g = nullptr;
+            cudaError_t e = cudaStreamEndCapture(cap, &g);
+            cudaStreamDestroy(cap);
+            if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+            if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+            e = cudaGraphInstantiate(&lm->graph_exec, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+            lm->graph_next = next_tokens;
+            lm->graph_logits = logits;
+            lm->graph_batch = lm->batch;
+            // capture counted the launches once; replays are counted below
+            launch_counter().fetch_sub(graph_nodes_per_step(lm->cfg), std::memory_order_relaxed);
+        }
+        FML_CUDA_TRY(cudaGraphLaunch(lm->graph_exec, st));
+        launch_counter().fetch_add(graph_nodes_per_step(lm->cfg), std::memory_order_relaxed);
+    }
+    else
+    {
+        FML_RC(enqueue_step(lm, next_tokens, logits, st));
+        if (lm->profiling) FML_RC(collect_profile(lm));
+    }
+    for (uint32_t b = 0; b < lm->batch; ++b) lm->hpos[b] += 1;
+    return FML_OK;
+}
+
+int fml_lm_step_host(fml_lm* lm, const uint32_t* tokens_in, uint32_t* tokens_out, fml_stream_t stream)
+{
+    FML_REQUIRE(lm && tokens_in && tokens_out, "fml_lm_step_host: null argument");
+    if (lm->batch == 0) return set_error(FML_ERR_STATE, "fml_lm_step_host: call fml_lm_prefill first");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t B = lm->batch;
+    std::memcpy(lm->host_io, tokens_in, B * 4);
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->pending, lm->host_io, B * 4, cudaMemcpyHostToDevice, st));
+    uint32_t* dev_next = lm->prompt_dev;  // scratch slot for the step's output tokens
+    FML_RC(fml_lm_step(lm, dev_next, nullptr, stream));
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->host_io + lm->cfg.max_batch, dev_next, B * 4, cudaMemcpyDeviceToHost, st));
+    FML_CUDA_TRY(cudaStreamSynchronize(st));
+    std::memcpy(tokens_out, lm->host_io + lm->cfg.max_batch, B * 4);
+    return FML_OK;
+}
+
+int fml_lm_pending(fml_lm* lm, uint32_t* out, fml_stream_t stream)
+{
+    FML_REQUIRE(lm && out, "fml_lm_pending: null argument");
+    if (lm->batch == 0) return set_error(FML_ERR_STATE, "fml_lm_pending: no active sequences");
+    FML_CUDA_TRY(cudaMemcpyAsync(out, lm->pending, lm->batch * 4, cudaMemcpyDeviceToDevice, as_stream(stream)));
+    return FML_OK;
+}
+
+int fml_lm_get_position(fml_lm* lm, uint32_t b, uint32_t* pos)
+{
+    FML_REQUIRE(lm && pos && b < lm->cfg.max_batch, "fml_lm_get_position: bad argument");
+    *pos = lm->hpos[b];
+    return FML_OK;
+}
+
+int fml_lm_rewind(fml_lm* lm, uint32_t pos, const uint32_t* pending, int pending_on_host, fml_stream_t stream)
+{
+    FML_REQUIRE(lm && pending, "fml_lm_rewind: null argument");
+    FML_REQUIRE(lm->batch > 0 && pos >= 1 && pos < lm->cfg.context, "fml_lm_rewind: bad position %u", pos);
+    cudaStream_t st = as_stream(stream);
+    const uint32_t B = lm->batch;
+    if (pending_on_host)
+    {
+        FML_CUDA_TRY(cudaStreamSynchronize(st));  // host_io may still feed an earlier copy
+        std::memcpy(lm->host_io, pending, B * 4);
+        FML_CUDA_TRY(cudaMemcpyAsync(lm->pending, lm->host_io, B * 4, cudaMemcpyHostToDevice, st));
+        rewind_kernel<<<(B + 127) / 128, 128, 0, st>>>(lm->pos, lm->pending, nullptr, B, pos);
+        FML_LAUNCH_CHECK();
+        FML_CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    else
+    {
+        rewind_kernel<<<(B + 127) / 128, 128, 0, st>>>(lm->pos, lm->pending, pending, B, pos);
+        FML_LAUNCH_CHECK();
+    }
+    for (uint32_t b = 0; b < B; ++b) lm->hpos[b] = pos;
+    return FML_OK;
+}
+
+uint64_t fml_lm_step_bytes(fml_lm* lm)
+{
+    if (!lm) return 0;
+    const fml_lm_config& c = lm->cfg;
+    const uint64_t d = c.d_model, L = c.n_layer, f = 4;
+    uint64_t bytes = f * (12 * d * d * L + (uint64_t)c.vocab * d + (2 * L + 1) * d);  // weights once
+    for (uint32_t b = 0; b < lm->batch; ++b)
+    {
+        const uint64_t len = lm->hpos[b] + 1;  // keys/values read this step, including the new row
+        bytes += f * 2 * d * L * len;          // K and V rows read
+        bytes += f * 2 * d * L;                // the new K and V rows written
+        bytes += f * 2 * d;                    // token + position rows
+    }
+    return bytes;
+}
+
+uint64_t fml_lm_attention_bytes(fml_lm* lm)
+{
+    if (!lm) return 0;
+    const fml_lm_config& c = lm->cfg;
+    const uint64_t d = c.d_model, L = c.n_layer, f = 4;
+    uint64_t bytes = 0;
+    for (uint32_t b = 0; b < lm->batch; ++b)
+        bytes += f * L * (2 * d * (uint64_t)(lm->hpos[b] + 1) + 2 * d);  // K,V rows + q in + out
+    return bytes;
+}
+
+int fml_lm_set_profiling(fml_lm* lm, int on)
+{
+    FML_REQUIRE(lm, "fml_lm_set_profiling: null engine");
+    lm->profiling = on != 0;
+    for (int i = 0; i < FML_LM_NCLASS; ++i) { lm->prof_ms[i] = 0; lm->prof_n[i] = 0; }
+    return FML_OK;
+}
+
+int fml_lm_get_profile(fml_lm* lm, double* ms, uint64_t* n, int ncls)
+{
+    FML_REQUIRE(lm && ms && n, "fml_lm_get_profile: null argument");
+    for (int i = 0; i < ncls && i < FML_LM_NCLASS; ++i) { ms[i] = lm->prof_ms[i]; n[i] = lm->prof_n[i]; }
+    return FML_OK;
+}
+
+}  // extern "C"

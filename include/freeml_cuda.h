@@ -1,0 +1,250 @@
+/*
+ * freeml_cuda.h -- C ABI of the B200 (sm_100a) backend for FreeML's
+ * language-model token loop.
+ *
+ * Two groups of entry points:
+ *
+ *  1. Operator entry points.  One per generic operator that the NanoLLM
+ *     forward reaches (MatrixLibrary/MatrixBase_Functions.h,
+ *     MatrixLibrary/MatrixBase_Mul.h).  The MatrixCUDA<float> overloads in
+ *     include/freeml_b200/MatrixCUDA_Functions.h call these, the same way the
+ *     DirectX11 backend's overloads (MatrixLibrary/GPU/DirectX11/
+ *     MatrixDX11_Functions.h) dispatch shaders.  Each comment names the
+ *     reference function it replaces.
+ *
+ *  2. The decode engine (fml_lm_*): a KV-cached, batched greedy token loop for
+ *     the NanoLLM graph (Examples/NanoLLM/NanoLLM.cpp:268-358) -- prefill, then
+ *     one fused step per generated token for B independent sequences.  The
+ *     reference has no decode loop; the engine produces the logits that
+ *     Model::Run (ModelLibrary/Model.h:764-788) would give for the same
+ *     window, row by row, and the argmax of NanoLLM.cpp:189-204.
+ *
+ * Conventions (the reference has none -- it asserts or returns silently):
+ *  - every function returns an int status, FML_OK (0) on success;
+ *    fml_last_error() gives a message for the calling thread;
+ *  - pointers are device pointers unless the name says host;
+ *  - matrices are row-major fp32, FreeML's Dims3D{x = cols, y = rows};
+ *  - `stream` is a cudaStream_t (NULL = the legacy default stream);
+ *  - operator entry points never allocate; the engine allocates only in
+ *    fml_lm_create / fml_lm_bind_weights;
+ *  - callers are single-threaded per device, like MatrixManager
+ *    (MatrixLibrary/MatrixManager.h:131-135).
+ */
+#ifndef FREEML_CUDA_H
+#define FREEML_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FML_API __attribute__((visibility("default")))
+#else
+#define FML_API
+#endif
+
+typedef void* fml_stream_t; /* cudaStream_t */
+
+enum fml_status
+{
+    FML_OK = 0,
+    FML_ERR_INVALID = 1,     /* bad shape, null pointer, unsupported argument */
+    FML_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+    FML_ERR_NOMEM = 3,       /* device allocation failed */
+    FML_ERR_UNSUPPORTED = 4, /* shape outside what the kernels handle */
+    FML_ERR_STATE = 5        /* engine used out of order */
+};
+
+/* Library / device information. */
+FML_API const char* fml_last_error(void);
+FML_API const char* fml_version(void);
+FML_API int fml_device_check(int* sm_count, int* cc_major, int* cc_minor);
+/* Number of kernels this library has launched in this process (all entry
+ * points, graph replays counted per kernel node). */
+FML_API uint64_t fml_kernel_launch_count(void);
+
+/* ---------------------------------------------------------------------
+ * 1. Operator entry points
+ * ------------------------------------------------------------------- */
+
+/* GatherRows(out, src, idx)  MatrixBase_Functions.h:203-242
+ * out[r, :] = src[(uint32)idx[r], :]; idx holds float token ids (one per row).
+ * The reference asserts ids < src_rows; here a row whose id is out of range
+ * is written as zeros (the kernel never reads outside src). */
+FML_API int fml_gather_rows(float* out, const float* src, const float* idx, uint32_t rows, uint32_t width,
+                    uint32_t src_rows, fml_stream_t stream);
+
+/* Add(out, L, R)  MatrixBase_Functions.h:471-479 (out may alias L or R). */
+FML_API int fml_add(float* out, const float* a, const float* b, uint64_t n, fml_stream_t stream);
+
+/* BroadcastAdd(out, L, R)  MatrixBase_Functions.h:717-731: out[i] = L[i] + R[i % cols]. */
+FML_API int fml_broadcast_add(float* out, const float* a, const float* row, uint64_t n, uint32_t cols,
+                      fml_stream_t stream);
+
+/* PerElementMul(out, L, R)  MatrixBase_Functions.h:848-855. */
+FML_API int fml_mul_elementwise(float* out, const float* a, const float* b, uint64_t n, fml_stream_t stream);
+
+/* Scale(out, in, float)  MatrixBase_Functions.h:1032-1039 and
+ * Scale(out, in, Mat*)  :1021-1030 (scale_dev != NULL: scale read on device). */
+FML_API int fml_scale(float* out, const float* in, float scale, const float* scale_dev, uint64_t n,
+              fml_stream_t stream);
+
+/* ScaleAdd(out, in, Mat* scale, add)  MatrixBase_Functions.h:1056-1070:
+ * out = in * scale[0] + add (fused multiply-add, as the reference build). */
+FML_API int fml_scale_add(float* out, const float* in, const float* scale_dev, const float* add, uint64_t n,
+                  fml_stream_t stream);
+
+/* Fill(out, float) :1079-1086, Fill(out, Mat*) :1088-1096 (value_dev != NULL),
+ * Clear(out) :1073-1077 (value 0). */
+FML_API int fml_fill(float* out, float value, const float* value_dev, uint64_t n, fml_stream_t stream);
+
+/* Copy(out, in) :157-162 and CopyRange(out, in, outOff, inOff, n) :164-181. */
+FML_API int fml_copy(float* out, const float* in, uint64_t n, fml_stream_t stream);
+
+/* LayerNormOp(out, in, gamma, beta, xHat, eps)  MatrixBase_Functions.h:482-549.
+ * beta and xhat may be NULL. */
+FML_API int fml_layernorm(float* out, const float* in, const float* gamma, const float* beta, float* xhat,
+                  uint32_t rows, uint32_t cols, float eps, fml_stream_t stream);
+
+/* GeluMat(out, in)  MatrixBase_Functions.h:989-1000 (exact erf). */
+FML_API int fml_gelu(float* out, const float* in, uint64_t n, fml_stream_t stream);
+
+/* Softmax(out, in)  MatrixBase_Functions.h:50-80 (row-wise). */
+FML_API int fml_softmax(float* out, const float* in, uint32_t rows, uint32_t cols, fml_stream_t stream);
+
+/* SplitQKV(q, k, v, packed)  MatrixBase_Functions.h:330-367. */
+FML_API int fml_split_qkv(float* q, float* k, float* v, const float* packed, uint32_t rows, uint32_t d,
+                  fml_stream_t stream);
+
+/* Mul<Mode>(out, L, R)  MatrixBase_Mul.h:591-615 for Mode in {None, Right}:
+ *   trans_b == 0: out[M x N] = L[M x K] . R[K x N]
+ *   trans_b == 1: out[M x N] = L[M x K] . R[N x K]^T
+ * Precision follows fml_set_math_mode(). */
+FML_API int fml_matmul(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K,
+               int trans_b, fml_stream_t stream);
+
+/* MatMul_Strided<Mode>(out, L, R, Lrs, 1, Rrs, 1, Ors, 1)  MatrixBase_Mul.h:617-722
+ * (column strides of 1, the form CausalSelfAttentionLayer.h:445-497 uses),
+ * for `batch` planes spaced by the plane strides (elements). */
+FML_API int fml_matmul_strided(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K,
+                       uint32_t lda, uint32_t ldb, uint32_t ldc, int trans_b, uint32_t batch,
+                       uint64_t plane_a, uint64_t plane_b, uint64_t plane_c, fml_stream_t stream);
+
+/* Precision of fml_matmul / the engine's prefill contractions:
+ *   FML_MATH_FP32  -- fp32 FFMA on the CUDA cores (default; the logits bound
+ *                     of 1e-3 abs/rel against the reference holds);
+ *   FML_MATH_TF32X3 -- tcgen05 tensor cores, each fp32 operand split into a
+ *                     TF32 pair and three products accumulated in fp32;
+ *   FML_MATH_TF32  -- tcgen05 tensor cores, one TF32 product (looser bound). */
+enum fml_math_mode { FML_MATH_FP32 = 0, FML_MATH_TF32X3 = 1, FML_MATH_TF32 = 2 };
+FML_API int fml_set_math_mode(int mode);
+FML_API int fml_get_math_mode(void);
+
+/* ---------------------------------------------------------------------
+ * 2. Decode engine
+ * ------------------------------------------------------------------- */
+
+typedef struct fml_lm fml_lm;
+
+typedef struct
+{
+    uint32_t vocab;      /* V: token table rows, lm_head columns */
+    uint32_t context;    /* C: block_size, position table rows, max window */
+    uint32_t d_model;    /* d */
+    uint32_t n_head;     /* H (d % H == 0, head dim 32/64/128) */
+    uint32_t n_layer;    /* L */
+    uint32_t max_batch;  /* sequences held by this engine (KV-cache slots) */
+} fml_lm_config;
+
+/* Parameters in FreeML's storage layouts (device pointers, fp32):
+ *   tok_emb   [V x d]   Embedding_Weights of embedding_token (also lm_head, tied)
+ *   pos_emb   [C x d]   Embedding_Weights of embedding_pos
+ *   per layer l (arrays of n_layer pointers):
+ *     ln0[l]  [d]       GammaScale of LayerNorm0Data
+ *     wqkv[l] [d x 3d]  Dense_Weights of CSA_AttentionLayer (y = x W)
+ *     wproj[l][d x d]   Dense_Weights of CSA_ProjLayer (transposed: y = x W^T)
+ *     ln1[l]  [d]       GammaScale of LayerNorm1Data
+ *     wfc[l]  [d x 4d]  Dense_Weights of DenseFCData
+ *     wmlp[l] [4d x d]  Dense_Weights of DenseProjData
+ *   lnf       [d]       GammaScale of ln_f
+ * The engine copies them into its own K-contiguous layout at bind time, so
+ * the caller's buffers may be freed or changed afterwards. */
+typedef struct
+{
+    const float* tok_emb;
+    const float* pos_emb;
+    const float* const* ln0;
+    const float* const* wqkv;
+    const float* const* wproj;
+    const float* const* ln1;
+    const float* const* wfc;
+    const float* const* wmlp;
+    const float* lnf;
+} fml_lm_weights;
+
+FML_API int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out);
+FML_API int fml_lm_destroy(fml_lm* lm);
+FML_API int fml_lm_bind_weights(fml_lm* lm, const fml_lm_weights* w, fml_stream_t stream);
+/* Convenience: all parameters in one host or device buffer, in the canonical
+ * order tok_emb, pos_emb, per layer {ln0, wqkv, wproj, ln1, wfc, wmlp}, lnf. */
+FML_API int fml_lm_bind_packed(fml_lm* lm, const float* params, int params_on_host, fml_stream_t stream);
+FML_API uint64_t fml_lm_param_count(const fml_lm_config* cfg);
+
+/* Start `batch` sequences (batch <= max_batch) from prompts of `prompt_len`
+ * tokens each (device, sequence-major [batch x prompt_len]).  Runs the
+ * prompt through batched contractions, fills the KV cache, and leaves the
+ * argmax of each sequence's last prompt row as its next token. */
+FML_API int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t prompt_len,
+                   fml_stream_t stream);
+
+/* One decode step for every active sequence: consume each sequence's pending
+ * token, append its K/V, and produce the next token (greedy).  Optional
+ * outputs (device): next tokens [batch] and logits [batch x V] of the row
+ * just computed.  All work is enqueued on `stream`; nothing synchronises. */
+FML_API int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t stream);
+
+/* The same step through host memory, the way a host caller drives the loop:
+ * copies `tokens_in` (host, [batch]) into the pending tokens, runs the step,
+ * copies the next tokens into `tokens_out` (host) and waits for them. */
+FML_API int fml_lm_step_host(fml_lm* lm, const uint32_t* tokens_in, uint32_t* tokens_out, fml_stream_t stream);
+
+/* Replay the step as one CUDA graph (captured on first use; the step reads
+ * positions and tokens from device memory, so one graph serves every step).
+ * use_graph = 0 launches the kernels one by one. */
+FML_API int fml_lm_set_graph(fml_lm* lm, int use_graph);
+
+/* Copy the pending token of each active sequence (the greedy token it will
+ * consume next; after prefill, the argmax of its last prompt row) into
+ * `out` (device, [batch]). */
+FML_API int fml_lm_pending(fml_lm* lm, uint32_t* out, fml_stream_t stream);
+
+/* Position (tokens held in the cache) of sequence b, and rewinding every
+ * active sequence to `pos` (cache rows [0, pos) are kept) with the given
+ * pending tokens ([batch], host or device memory).  The device form is
+ * stream-ordered and does not synchronise. */
+FML_API int fml_lm_get_position(fml_lm* lm, uint32_t b, uint32_t* pos);
+FML_API int fml_lm_rewind(fml_lm* lm, uint32_t pos, const uint32_t* pending, int pending_on_host,
+                          fml_stream_t stream);
+
+/* Per-step algorithmic HBM bytes (weights once + K/V read + K/V written) for
+ * the current positions, the quantity the bench divides by step time. */
+FML_API uint64_t fml_lm_step_bytes(fml_lm* lm);
+
+/* Kernel timing: with profiling on (and graphs off), every step records CUDA
+ * events around each kernel class and accumulates milliseconds and launch
+ * counts per class: 0 embed, 1 layernorm, 2 qkv, 3 attention, 4 proj,
+ * 5 fc, 6 mlp, 7 lm_head, 8 argmax/finalize.  Reset when turned on. */
+enum { FML_LM_NCLASS = 9 };
+FML_API int fml_lm_set_profiling(fml_lm* lm, int on);
+FML_API int fml_lm_get_profile(fml_lm* lm, double* ms_by_class, uint64_t* launches_by_class, int n_classes);
+/* Algorithmic bytes of the attention kernels of one step (K/V rows read,
+ * queries read, outputs written), for the attention roofline. */
+FML_API uint64_t fml_lm_attention_bytes(fml_lm* lm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FREEML_CUDA_H */

@@ -1,0 +1,159 @@
+"""Parity of the KV-cached decode engine (fml_lm_*) with FreeML's reference
+token loop.
+
+Bound (fp32 mode): every logit within
+|gpu - ref| <= 1e-3 + 1e-3 |ref|; greedy tokens identical wherever the
+reference's top-2 logit gap exceeds 2e-3 (where it does not, the first
+divergence step is reported and the check stops there, as both tokens are
+acceptable argmaxes within tolerance).
+
+Small shapes are compared with the committed golden vectors (the reference's
+own greedy loop); BASELINE config 3 (32 sequences) is checked teacher-forced:
+one oracle forward over each GPU token stream gives the reference logits of
+every generated row (row t depends on tokens <= t only)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ATOL = RTOL = 1e-3
+GAP = 2e-3
+
+
+def _lm(shape, batch):
+    from freeml_b200.lm import NanoLLMShape, NanoLM
+    s = NanoLLMShape(shape.V, shape.C, shape.d, shape.H, shape.L)
+    return NanoLM(s, batch)
+
+
+def first_divergence(ref_logits, gpu_tokens_next):
+    """Index of the first row whose reference argmax (with a clear top-2 gap)
+    differs from the GPU's token, or -1."""
+    for t in range(ref_logits.shape[0]):
+        row = ref_logits[t]
+        top2 = np.sort(row)[-2:]
+        if O.argmax_first(row) != gpu_tokens_next[t]:
+            if top2[1] - top2[0] > GAP:
+                return t
+            return -2 - t  # a near-tie: acceptable, stop comparing here
+    return -1
+
+
+@pytest.mark.parametrize("name", ["cfg1", "odd"])
+def test_greedy_matches_reference_loop(golden, name):
+    meta, g, _ = golden
+    m = meta["greedy"][name]
+    s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
+    w = O.init_weights(s, m["wseed"])
+    lm = _lm(s, 1)
+    lm.bind(w)
+    prompt = g[f"{name}_prompt"].reshape(1, -1)
+    toks, logits = lm.generate(prompt, m["new"], want_logits=True)
+    ref_toks, ref_logits = g[f"{name}_tokens"], g[f"{name}_logits"]
+    # logits[k] is generated row plen + k (the rows after the prefill's)
+    np.testing.assert_allclose(logits[:, 0, :], ref_logits[1:], rtol=RTOL, atol=ATOL)
+    div = first_divergence(ref_logits, toks[0, m["plen"]:])
+    assert div == -1, f"first divergence at step {div}"
+    np.testing.assert_array_equal(toks[0], ref_toks)
+    lm.close()
+
+
+def test_graph_and_eager_steps_are_identical(golden):
+    meta, g, _ = golden
+    m = meta["greedy"]["cfg1"]
+    s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
+    w = O.init_weights(s, m["wseed"])
+    outs = []
+    for graph in (True, False):
+        lm = _lm(s, 1)
+        lm.bind(w)
+        lm.set_graph(graph)
+        toks, logits = lm.generate(g["cfg1_prompt"].reshape(1, -1), 40, want_logits=True)
+        outs.append((toks, logits))
+        lm.close()
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+
+
+def test_host_step_matches_device_step(golden):
+    meta, g, _ = golden
+    m = meta["greedy"]["cfg1"]
+    s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
+    w = O.init_weights(s, m["wseed"])
+    lm = _lm(s, 1)
+    lm.bind(w)
+    prompt = g["cfg1_prompt"].reshape(1, -1)
+    lm.prefill(prompt)
+    tok = lm.pending_tokens().cpu().numpy().view(np.uint32).copy()
+    seq = [int(tok[0])]
+    out = np.zeros(1, np.uint32)
+    for _ in range(30):
+        lm.step_host(tok, out)
+        seq.append(int(out[0]))
+        tok = out.copy()
+    np.testing.assert_array_equal(np.array(seq, np.uint32), g["cfg1_tokens"][16:47])
+    lm.close()
+
+
+def test_rewind_replays_the_same_stream(golden):
+    meta, g, _ = golden
+    m = meta["greedy"]["cfg1"]
+    s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
+    w = O.init_weights(s, m["wseed"])
+    lm = _lm(s, 1)
+    lm.bind(w)
+    toks, _ = lm.generate(g["cfg1_prompt"].reshape(1, -1), 20)
+    assert lm.position(0) == 16 + 19
+    lm.rewind(16 + 5, toks[:, 16 + 5])
+    again = [lm.step()[0].cpu().numpy().view(np.uint32)[0] for _ in range(10)]
+    np.testing.assert_array_equal(np.array(again, np.uint32), toks[0, 16 + 6:16 + 16])
+    lm.close()
+
+
+def test_batched_sequences_are_independent(golden):
+    """Four copies of different prompts in one batch give the same streams as
+    one-at-a-time runs (no cross-talk between KV-cache slots)."""
+    meta, g, _ = golden
+    m = meta["greedy"]["cfg1"]
+    s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
+    w = O.init_weights(s, m["wseed"])
+    prompts = np.random.RandomState(9).randint(0, s.V, size=(4, 16)).astype(np.uint32)
+    lm = _lm(s, 4)
+    lm.bind(w)
+    batched, _ = lm.generate(prompts, 24)
+    lm.close()
+    for b in range(4):
+        lm1 = _lm(s, 1)
+        lm1.bind(w)
+        single, _ = lm1.generate(prompts[b:b + 1], 24)
+        lm1.close()
+        np.testing.assert_array_equal(batched[b], single[0])
+
+
+@pytest.mark.parametrize("nseq_checked", [4])
+def test_config3_teacher_forced(nseq_checked):
+    """V4096 C512 d512 H8 L8, 32 sequences, 128-token
+    prompts (seed 4), 384 greedy tokens.  The engine decodes all 32; the
+    oracle checks `nseq_checked` of them (every generated row) teacher-forced."""
+    from freeml_b200.lm import CONFIGS, prompt_tokens
+    c = CONFIGS[3]
+    sh = c["shape"]
+    s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
+    w = O.init_weights(s, c["wseed"])
+    prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])
+    lm = _lm(s, c["batch"])
+    lm.bind(w)
+    toks, logits = lm.generate(prompts, c["new"], want_logits=True)
+    lm.close()
+    P, N = c["prompt"], c["new"]
+    assert toks.shape == (c["batch"], P + N)
+    for b in np.linspace(0, c["batch"] - 1, nseq_checked).astype(int):
+        ref = O.forward(s, w, toks[b, : P + N - 1], row0=P - 1, nrows=N)  # rows P-1 .. P+N-2
+        div = first_divergence(ref, toks[b, P:])
+        assert div == -1 or div < -1, f"sequence {b}: first divergence at step {div}"
+        upto = N if div == -1 else (-2 - div)
+        got = logits[: upto - 1, b, :]
+        np.testing.assert_allclose(got, ref[1:upto], rtol=RTOL, atol=ATOL)
