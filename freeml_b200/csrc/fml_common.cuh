@@ -42,6 +42,12 @@ std::atomic<uint64_t>& launch_counter();
         if (!(cond)) return ::fml::set_error(FML_ERR_INVALID, __VA_ARGS__);                    \
     } while (0)
 
+#define FML_RC(expr)                   \
+    do {                               \
+        int _rc = (expr);              \
+        if (_rc != FML_OK) return _rc; \
+    } while (0)
+
 inline cudaStream_t as_stream(fml_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline unsigned grid_for(uint64_t n, unsigned block, unsigned cap = 148u * 32u)

@@ -32,6 +32,7 @@
 #include <cstring>
 #include <vector>
 
+#include "attention.cuh"
 #include "fml_common.cuh"
 
 namespace fml {
@@ -218,183 +219,6 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
         float* cache = c3 < 2 * d ? kc : vc;
         cache[(uint64_t)b * seq_stride + ((uint64_t)h * C + t) * hd + e] = v;
     }
-}
-
-struct AttnArgs
-{
-    const float* q;  // row r, head h at q + r*ldq + h*HD
-    uint32_t ldq;
-    uint32_t row0;   // first row of this launch (rows row0 + blockIdx.y)
-    const float* kc;
-    const float* vc;
-    uint64_t seq_stride;  // H*C*HD
-    uint32_t H, C;
-    float* out;      // row r, head h at out + r*ldo + h*HD
-    uint32_t ldo;
-    const uint32_t* pos;  // decode: b = r, t = pos[r]; prefill (null): b = r / P, t = r % P
-    uint32_t P;
-    uint32_t S, chunk;    // splits over the key range, positions per split
-    float scale;          // 1/sqrt(hd), CausalSelfAttentionLayer.h:73-77
-    float* part;          // [B][H][S][HD + 2] split partials
-    uint32_t* counters;   // [B][H]
-};
-
-// Causal attention for one query row over the cached keys 0..t
-// (CausalSelfAttentionLayer.h:424-499: Q_h K_h^T, * 1/sqrt(hd) + causal
-// mask, Softmax, P V_h), as one pass with an online softmax.
-// grid = (H, rows, S); 4 warps per CTA take 32-key tiles in turn.  Per tile a
-// lane holds HD/32 dims of q; the 32 partial dot products are summed by a
-// transpose-reduce, so lane j ends with key j's score; p_j is then
-// broadcast for the P.V update.  With S > 1 each CTA writes (m, l, acc) and
-// the last CTA of the (row, head) to finish merges the S partials.
-template <int HD>
-__global__ void __launch_bounds__(128) attention_kernel(AttnArgs a)
-{
-    constexpr int DPL = HD / 32;
-    __shared__ float sm_m[4], sm_l[4];
-    __shared__ float sm_acc[4][HD];
-    __shared__ int sm_last;
-
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t h = blockIdx.x, r = a.row0 + blockIdx.y, s = blockIdx.z;
-    uint32_t b, t;
-    if (a.pos) { b = r; t = a.pos[r]; }
-    else { b = r / a.P; t = r % a.P; }
-    const uint32_t len = t + 1;
-    const uint32_t begin = s * a.chunk;
-    const uint32_t end = min(len, begin + a.chunk);
-
-    const float* K = a.kc + (uint64_t)b * a.seq_stride + (uint64_t)h * a.C * HD;
-    const float* Vv = a.vc + (uint64_t)b * a.seq_stride + (uint64_t)h * a.C * HD;
-
-    float qv[DPL];
-    const float* qp = a.q + (uint64_t)r * a.ldq + h * HD + lane * DPL;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) qv[i] = qp[i];
-
-    float m_run = -INFINITY, l_run = 0.0f;
-    float acc[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = 0.0f;
-
-    for (uint32_t j0 = begin + warp * 32u; j0 < end; j0 += 128u)
-    {
-        float part[32];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj)
-        {
-            float sdot = 0.0f;
-            if (j0 + jj < end)
-            {
-                const float* kr = K + (uint64_t)(j0 + jj) * HD + lane * DPL;
-                if constexpr (DPL == 4)
-                {
-                    const float4 k4 = *reinterpret_cast<const float4*>(kr);
-                    sdot = qv[0] * k4.x + qv[1] * k4.y + qv[2] * k4.z + qv[3] * k4.w;
-                }
-                else if constexpr (DPL == 2)
-                {
-                    const float2 k2 = *reinterpret_cast<const float2*>(kr);
-                    sdot = qv[0] * k2.x + qv[1] * k2.y;
-                }
-                else
-                {
-                    sdot = qv[0] * kr[0];
-                }
-            }
-            part[jj] = sdot;
-        }
-        warp_transpose_reduce<32>(part, lane);
-        // lane now holds the full dot product of key j0 + lane
-        const bool valid = j0 + lane < end;
-        const float sc = valid ? part[0] * a.scale : -INFINITY;
-        const float tile_max = warp_max(sc);
-        const float m_new = fmaxf(m_run, tile_max);
-        const float p = valid ? expf(sc - m_new) : 0.0f;
-        const float corr = expf(m_run - m_new);
-        l_run = l_run * corr + warp_sum(p);
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] *= corr;
-        const uint32_t nvalid = min(32u, end - j0);
-        for (uint32_t jj = 0; jj < nvalid; ++jj)
-        {
-            const float pj = __shfl_sync(FULL_MASK, p, jj);
-            const float* vr = Vv + (uint64_t)(j0 + jj) * HD + lane * DPL;
-            if constexpr (DPL == 4)
-            {
-                const float4 v4 = *reinterpret_cast<const float4*>(vr);
-                acc[0] = fmaf(pj, v4.x, acc[0]);
-                acc[1] = fmaf(pj, v4.y, acc[1]);
-                acc[2] = fmaf(pj, v4.z, acc[2]);
-                acc[3] = fmaf(pj, v4.w, acc[3]);
-            }
-            else if constexpr (DPL == 2)
-            {
-                const float2 v2 = *reinterpret_cast<const float2*>(vr);
-                acc[0] = fmaf(pj, v2.x, acc[0]);
-                acc[1] = fmaf(pj, v2.y, acc[1]);
-            }
-            else
-            {
-                acc[0] = fmaf(pj, vr[0], acc[0]);
-            }
-        }
-        m_run = m_new;
-    }
-
-    if (lane == 0) { sm_m[warp] = m_run; sm_l[warp] = l_run; }
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) sm_acc[warp][lane * DPL + i] = acc[i];
-    __syncthreads();
-
-    // merge the 4 warps
-    const float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
-    float w4[4];
-    float L = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-    {
-        w4[i] = (M == -INFINITY) ? 0.0f : expf(sm_m[i] - M);
-        L += sm_l[i] * w4[i];
-    }
-    const int e = threadIdx.x;
-    if (a.S == 1)
-    {
-        if (e < HD)
-        {
-            const float A = sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3];
-            a.out[(uint64_t)r * a.ldo + h * HD + e] = A / L;
-        }
-        return;
-    }
-
-    float* mypart = a.part + (((uint64_t)b * a.H + h) * a.S + s) * (HD + 2);
-    if (e < HD)
-        mypart[e] = sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3];
-    if (e == 0) { mypart[HD] = M; mypart[HD + 1] = L; }
-    __threadfence();
-    __syncthreads();
-    if (e == 0)
-    {
-        const uint32_t prev = atomicAdd(a.counters + (uint64_t)b * a.H + h, 1u);
-        sm_last = (prev == a.S - 1) ? 1 : 0;
-    }
-    __syncthreads();
-    if (!sm_last) return;
-    __threadfence();
-    const float* parts = a.part + ((uint64_t)b * a.H + h) * a.S * (HD + 2);
-    float Mg = -INFINITY;
-    for (uint32_t i = 0; i < a.S; ++i) Mg = fmaxf(Mg, __ldcg(parts + i * (HD + 2) + HD));
-    float Lg = 0.0f, Ag = 0.0f;
-    for (uint32_t i = 0; i < a.S; ++i)
-    {
-        const float mi = __ldcg(parts + i * (HD + 2) + HD);
-        const float wi = (mi == -INFINITY) ? 0.0f : expf(mi - Mg);
-        Lg += __ldcg(parts + i * (HD + 2) + HD + 1) * wi;
-        if (e < HD) Ag += __ldcg(parts + i * (HD + 2) + e) * wi;
-    }
-    if (e < HD) a.out[(uint64_t)r * a.ldo + h * HD + e] = Ag / Lg;
-    if (e == 0) a.counters[(uint64_t)b * a.H + h] = 0u;
 }
 
 // After lm_head: pending token = argmax, advance the position, reset keys.
@@ -602,24 +426,10 @@ int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, c
     a.scale = 1.0f / sqrtf((float)lm->hd);
     a.part = lm->part;
     a.counters = lm->counters;
-    dim3 grid(lm->cfg.n_head, rows, S);
     FML_REQUIRE(rows <= 65535u, "attention: too many rows in one launch (%u)", rows);
-    switch (lm->hd)
-    {
-    case 32: attention_kernel<32><<<grid, 128, 0, st>>>(a); break;
-    case 64: attention_kernel<64><<<grid, 128, 0, st>>>(a); break;
-    case 128: attention_kernel<128><<<grid, 128, 0, st>>>(a); break;
-    default: return set_error(FML_ERR_UNSUPPORTED, "head dim %u not supported (32/64/128)", lm->hd);
-    }
-    FML_LAUNCH_CHECK();
+    FML_RC(launch_attention_kernel(a, lm->hd, dim3(lm->cfg.n_head, rows, S), st));
     return FML_OK;
 }
-
-#define FML_RC(expr)                   \
-    do {                               \
-        int _rc = (expr);              \
-        if (_rc != FML_OK) return _rc; \
-    } while (0)
 
 // Enqueue one decode step for the active batch.
 int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
@@ -725,20 +535,7 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     lm->layer_stride = B * lm->seq_stride;
     const uint64_t rows = B * Ctx;
 
-    // attention split: enough CTAs for ~2 waves of 148 SMs at full batch,
-    // each split a multiple of 32 keys
-    {
-        const uint64_t pairs = B * H;
-        uint64_t S = (2 * 148 + pairs - 1) / pairs;
-        const uint64_t max_s = (Ctx + 31) / 32;
-        if (S > max_s) S = max_s;
-        if (S < 1) S = 1;
-        uint64_t chunk = (Ctx + S - 1) / S;
-        chunk = (chunk + 31) / 32 * 32;
-        S = (Ctx + chunk - 1) / chunk;
-        lm->S = (uint32_t)S;
-        lm->chunk = (uint32_t)chunk;
-    }
+    attention_splits(B * H, Ctx, &lm->S, &lm->chunk);
 
     auto alloc = [&](void** p, uint64_t bytes) -> int {
         cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);

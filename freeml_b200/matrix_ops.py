@@ -115,3 +115,21 @@ def MatMul_Strided(out, L, R, M, N, K, lda, ldb, ldc, mode: int = NONE, batch=1,
     es = 4
     call("fml_matmul_strided", out.data_ptr() + off_c * es, L.data_ptr() + off_a * es, R.data_ptr() + off_b * es,
          M, N, K, lda, ldb, ldc, int(mode == RIGHT), batch, plane_a, plane_b, plane_c, _s())
+
+
+def attention_decode_workspace_bytes(batch: int, heads: int, head_dim: int, context: int) -> int:
+    from ._lib import load
+    return int(load().fml_attention_workspace_bytes(batch, heads, head_dim, context))
+
+
+def attention_decode(out, q, kcache, vcache, lens, scale, workspace=None):
+    """Causal attention of the newest row per sequence over a KV cache
+    (fml_attention_decode).  q/out: [B, H*hd]; kcache/vcache: [B, H, C, hd];
+    lens: int32 [B] (keys 0..lens[b]-1)."""
+    B, H, C, hd = kcache.shape
+    need = attention_decode_workspace_bytes(B, H, hd, C)
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    _check(lens.dtype == torch.int32 and lens.is_cuda, "lens must be a CUDA int32 tensor")
+    call("fml_attention_decode", _p(out), _p(q), _p(kcache), _p(vcache), lens.data_ptr(), B, H, hd, C, float(scale),
+         workspace.data_ptr(), workspace.numel(), _s())

@@ -133,6 +133,25 @@ FML_API int fml_matmul_strided(float* out, const float* a, const float* b, uint3
                        uint32_t lda, uint32_t ldb, uint32_t ldc, int trans_b, uint32_t batch,
                        uint64_t plane_a, uint64_t plane_b, uint64_t plane_c, fml_stream_t stream);
 
+/* Causal attention of one query row per sequence over a KV cache -- the
+ * attention core of CausalSelfAttentionLayer::Forward
+ * (LayerLibrary/CausalSelfAttentionLayer.h:424-499: MatMul_Strided<Right>
+ * scores, ScaleAdd with the causal mask, Softmax, MatMul_Strided<None>) for
+ * the newest row, where the mask leaves keys 0..len-1:
+ *   q      [batch x heads*head_dim]
+ *   kcache, vcache [batch][heads][context][head_dim]
+ *   lens   [batch] (device): keys 0 .. lens[b]-1 attend (0 gives zeros)
+ *   out    [batch x heads*head_dim]
+ *   scale  1/sqrt(head_dim) in the reference ("ScalarScale", :73-77)
+ * The key range is split across CTAs; `workspace` (device, at least
+ * fml_attention_workspace_bytes(batch, heads, head_dim, context) bytes) holds
+ * the per-split partial results. */
+FML_API size_t fml_attention_workspace_bytes(uint32_t batch, uint32_t heads, uint32_t head_dim, uint32_t context);
+FML_API int fml_attention_decode(float* out, const float* q, const float* kcache, const float* vcache,
+                                 const uint32_t* lens, uint32_t batch, uint32_t heads, uint32_t head_dim,
+                                 uint32_t context, float scale, void* workspace, size_t workspace_bytes,
+                                 fml_stream_t stream);
+
 /* Precision of fml_matmul / the engine's prefill contractions:
  *   FML_MATH_FP32  -- fp32 FFMA on the CUDA cores (default; the logits bound
  *                     of 1e-3 abs/rel against the reference holds);

@@ -157,3 +157,50 @@ def test_elementwise_and_fill():
     z = torch.empty(6, 5, device="cuda")
     F.BroadcastAdd(z, cu(m), cu(bias))
     np.testing.assert_array_equal(host(z), m + bias)
+
+
+def _attention_case(B, H, hd, C, lens, seed):
+    rs = np.random.RandomState(seed)
+    q = rs.randn(B, H * hd).astype(np.float32)
+    kc = rs.randn(B, H, C, hd).astype(np.float32)
+    vc = rs.randn(B, H, C, hd).astype(np.float32)
+    return q, kc, vc, np.asarray(lens, np.int32)
+
+
+def _attention_oracle(q, kc, vc, lens, scale):
+    B, H, C, hd = kc.shape
+    out = np.zeros((B, H * hd), np.float32)
+    for b in range(B):
+        n = int(lens[b])
+        if n == 0:
+            continue
+        out[b] = O.attention_decode_ref(q[b].reshape(H, hd), kc[b, :, :n], vc[b, :, :n], scale).ravel()
+    return out
+
+
+@pytest.mark.parametrize("B,H,hd,C,lens", [
+    (1, 8, 64, 128, [128]),    # config 2: 8 heads x hd 64, KV length 128
+    (1, 8, 64, 512, [512]),    # ... 512
+    (1, 8, 64, 2048, [2048]),  # ... 2048
+    (3, 4, 32, 100, [1, 37, 100]),
+    (2, 2, 128, 300, [300, 65]),
+    (4, 8, 64, 512, [0, 1, 511, 512]),
+])
+def test_attention_decode_vs_oracle(B, H, hd, C, lens):
+    from freeml_b200 import matrix_ops as F
+    q, kc, vc, ln = _attention_case(B, H, hd, C, lens, B * 100 + C)
+    scale = float(1.0 / np.sqrt(np.float32(hd)))
+    out = torch.empty(B, H * hd, device="cuda")
+    F.attention_decode(out, cu(q), cu(kc), cu(vc), torch.from_numpy(ln).cuda(), scale)
+    ref = _attention_oracle(q, kc, vc, ln, np.float32(scale))
+    close(host(out), ref, 2e-5, 2e-5)
+
+
+def test_attention_decode_rejects_small_workspace():
+    from freeml_b200 import FmlError
+    from freeml_b200 import matrix_ops as F
+    q, kc, vc, ln = _attention_case(1, 8, 64, 128, [128], 0)
+    out = torch.empty(1, 512, device="cuda")
+    with pytest.raises(FmlError):
+        F.attention_decode(out, cu(q), cu(kc), cu(vc), torch.from_numpy(ln).cuda(), 0.125,
+                           workspace=torch.empty(16, dtype=torch.uint8, device="cuda"))
