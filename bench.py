@@ -143,7 +143,8 @@ def hbm_peak():
 
 def ncu_traffic():
     """dram bytes (read + write) per attention launch from the committed ncu
-    summary, scaled to the bench's average key length."""
+    summary (profiles/attention_traffic.json), scaled to the bench's average
+    key length."""
     p = os.path.join(ROOT, "profiles", "attention_traffic.json")
     try:
         with open(p) as f:
