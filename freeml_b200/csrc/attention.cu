@@ -3,6 +3,7 @@
 // one query row at a time, used by the decode engine (decode and prefill
 // rows) and exposed as the fml_attention_decode operator.
 #include <cmath>
+#include <mutex>
 
 #include "attention.cuh"
 
@@ -245,6 +246,90 @@ int fml_attention_decode(float* out, const float* q, const float* kcache, const 
     a.pos = nullptr; a.lens = lens; a.P = 1;
     a.S = S; a.chunk = chunk; a.scale = scale;
     a.part = static_cast<float*>(workspace);
+    a.counters = counters;
+    return launch_attention_kernel(a, head_dim, dim3(heads, batch, S), st);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free attention (fml_attention_decode_noalloc).
+//
+// For callers that may not allocate device memory: a host runtime that hands
+// every byte of the GPU to its own pool and forbids libraries from calling
+// cudaMalloc, or code running inside such a pool's out-of-memory handling,
+// where a new allocation could recurse or fail.  The split partials and the
+// merge counters live in the fixed array below, part of this library's own
+// device image: every GPU that loads the library holds these
+// FML_NOALLOC_SCRATCH_BYTES until the process exits.
+//
+// Host code may not hand `g_attention_scratch` to a kernel: on the host that
+// name is only a stand-in, not a device address.  The device address is
+// fetched with cudaGetSymbolAddress once per device (with that device
+// current) and cached; the first call on a device does this set-up, so make
+// that first call outside any stream capture.
+// ---------------------------------------------------------------------------
+
+static __device__ __align__(256) unsigned char g_attention_scratch[FML_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_addr[kMaxDevices] = {};
+
+int noalloc_scratch(void** out)
+{
+    int dev = 0;
+    FML_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices)
+        return set_error(FML_ERR_UNSUPPORTED, "fml_attention_decode_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev])
+    {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(FML_ERR_CUDA, "fml_attention_decode_noalloc: cudaGetSymbolAddress failed: %s",
+                             cudaGetErrorString(e));
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return FML_OK;
+}
+}  // namespace
+
+int fml_attention_decode_noalloc(float* out, const float* q, const float* kcache, const float* vcache,
+                                 const uint32_t* lens, uint32_t batch, uint32_t heads, uint32_t head_dim,
+                                 uint32_t context, float scale, fml_stream_t stream)
+{
+    if (batch == 0) return FML_OK;
+    FML_REQUIRE(out && q && kcache && vcache && lens, "fml_attention_decode_noalloc: null pointer");
+    FML_REQUIRE(heads >= 1 && context >= 1, "fml_attention_decode_noalloc: zero heads or context");
+    FML_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128,
+                "fml_attention_decode_noalloc: head_dim %u (need 32, 64 or 128)", head_dim);
+    FML_REQUIRE(batch <= 65535u, "fml_attention_decode_noalloc: batch %u > 65535", batch);
+    uint32_t S, chunk;
+    attention_splits((uint64_t)batch * heads, context, &S, &chunk);
+    const uint64_t need = attention_workspace_bytes(batch, heads, head_dim, S);
+    if (need > FML_NOALLOC_SCRATCH_BYTES)
+        return set_error(FML_ERR_UNSUPPORTED,
+                         "fml_attention_decode_noalloc: batch %u x heads %u x head_dim %u needs %llu bytes of "
+                         "scratch, above the fixed %u-byte array; use fml_attention_decode with a workspace",
+                         batch, heads, head_dim, (unsigned long long)need, (unsigned)FML_NOALLOC_SCRATCH_BYTES);
+    void* scratch = nullptr;
+    FML_RC(noalloc_scratch(&scratch));
+    cudaStream_t st = as_stream(stream);
+    // The array keeps whatever the previous call left; the merge counters must
+    // start at zero, so clear them (a memset, not an allocation).
+    const uint64_t part_bytes = need - (uint64_t)batch * heads * sizeof(uint32_t);
+    uint32_t* counters = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + part_bytes);
+    FML_CUDA_TRY(cudaMemsetAsync(counters, 0, (size_t)batch * heads * sizeof(uint32_t), st));
+    AttnArgs a{};
+    a.q = q; a.ldq = heads * head_dim; a.row0 = 0;
+    a.kc = kcache; a.vc = vcache; a.seq_stride = (uint64_t)heads * context * head_dim;
+    a.H = heads; a.C = context;
+    a.out = out; a.ldo = heads * head_dim;
+    a.pos = nullptr; a.lens = lens; a.P = 1;
+    a.S = S; a.chunk = chunk; a.scale = scale;
+    a.part = static_cast<float*>(scratch);
     a.counters = counters;
     return launch_attention_kernel(a, head_dim, dim3(heads, batch, S), st);
 }

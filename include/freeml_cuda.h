@@ -152,6 +152,26 @@ FML_API int fml_attention_decode(float* out, const float* q, const float* kcache
                                  uint32_t context, float scale, void* workspace, size_t workspace_bytes,
                                  fml_stream_t stream);
 
+/* fml_attention_decode without a workspace argument: it allocates nothing.
+ * No counterpart in the reference (FreeML's CPU path never needs scratch
+ * device memory).  It is for callers that may not allocate device memory --
+ * a host runtime that owns the GPU's memory through its own pool and forbids
+ * libraries to call cudaMalloc, or code running inside that pool's
+ * out-of-memory handling.  The split partials live in a fixed
+ * FML_NOALLOC_SCRATCH_BYTES array inside this library's device image, held by
+ * every GPU that loads the library until the process exits.  Shapes whose
+ * scratch would exceed it are rejected with FML_ERR_UNSUPPORTED (use
+ * fml_attention_decode instead).  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * outside any stream capture.  Every call shares the one array: calls that
+ * overlap on the GPU (different streams, or different host threads on the same
+ * device) race and must be serialised by the caller.  Same arguments and
+ * results as fml_attention_decode otherwise. */
+#define FML_NOALLOC_SCRATCH_BYTES (4u << 20)
+FML_API int fml_attention_decode_noalloc(float* out, const float* q, const float* kcache, const float* vcache,
+                                         const uint32_t* lens, uint32_t batch, uint32_t heads, uint32_t head_dim,
+                                         uint32_t context, float scale, fml_stream_t stream);
+
 /* Precision of fml_matmul / the engine's prefill contractions:
  *   FML_MATH_FP32  -- fp32 FFMA on the CUDA cores (default; the logits bound
  *                     of 1e-3 abs/rel against the reference holds);
