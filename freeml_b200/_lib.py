@@ -44,6 +44,7 @@ SIGNATURES = {
     "fml_version": (ctypes.c_char_p, []),
     "fml_device_check": (_I, [_P, _P, _P]),
     "fml_kernel_launch_count": (_U64, []),
+    "fml_device_error_count": (_I, [_P]),
     "fml_gather_rows": (_I, [_P, _P, _P, _U32, _U32, _U32, _P]),
     "fml_add": (_I, [_P, _P, _P, _U64, _P]),
     "fml_broadcast_add": (_I, [_P, _P, _P, _U64, _U32, _P]),

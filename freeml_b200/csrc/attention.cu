@@ -3,6 +3,7 @@
 // one query row at a time, used by the decode engine (decode and prefill
 // rows) and exposed as the fml_attention_decode operator.
 #include <cmath>
+#include <cstdlib>
 #include <mutex>
 
 #include "attention.cuh"
@@ -17,191 +18,303 @@ namespace fml {
 // transpose-reduce, so lane j ends with key j's score; p_j is then
 // broadcast for the P.V update.  With S > 1 each CTA writes (m, l, acc) and
 // the last CTA of the (row, head) to finish merges the S partials.
-template <int HD>
-__global__ void __launch_bounds__(128) attention_kernel(AttnArgs a)
+// ---- TMA bulk-copy + mbarrier helpers (sm_90+ PTX) -------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
 {
-    constexpr int DPL = HD / 32;
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// One contiguous global -> shared copy by the TMA unit, completing on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Bounded wait for phase `parity` of `bar`: false if it did not complete
+// within the iteration limit (the caller reports a device error and stops).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
+{
+    const uint32_t addr = smem_u32(bar);
+    for (uint32_t it = 0; it < (1u << 24); ++it)
+    {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ int g_attention_timeouts;  // wait limits hit (read by fml_device_error_count)
+
+// Causal attention for one query row over the cached keys 0..len-1
+// (CausalSelfAttentionLayer.h:424-499: Q_h K_h^T, * 1/sqrt(hd) + causal
+// mask, Softmax, P V_h) as one pass with an online softmax.
+//
+// CTA = 4 warps on one (row, head, key split); grid = (heads, rows, splits).
+// Inside a warp, G = HD/4 lanes form a group that owns one key at a time,
+// each lane holding 4 dims (one float4 of the K row and of the V row), so a
+// score needs log2(G) shuffles and a warp covers 32/G keys per step.  Every
+// group keeps its own running max / sum / accumulator (no per-key
+// broadcast); U steps of K and V loads are issued before any is used, and a
+// thread stays under 64 registers so that 8 CTAs (32 warps) fit on an SM and
+// the loads of many warps overlap.  Groups, warps and then splits are merged
+// at the end; with S > 1 each CTA writes (m, l, acc) and the last CTA of the
+// (row, head) to finish merges the partials.
+struct AttnUnit
+{
+    uint32_t r, b, begin, end, nsplit;
+};
+
+__device__ __forceinline__ AttnUnit attention_unit(const AttnArgs& a, uint32_t r, uint32_t s)
+{
+    AttnUnit t;
+    t.r = r;
+    uint32_t len;
+    if (a.lens) { t.b = r; len = a.lens[r]; }
+    else if (a.pos) { t.b = r; len = a.pos[r] + 1; }
+    else { t.b = r / a.P; len = r % a.P + 1; }
+    // keys per split: fixed, or an even share of this row's keys
+    const uint32_t chunk = a.chunk ? a.chunk : max(32u, ((len + a.S - 1) / a.S + 31u) & ~31u);
+    t.begin = min(s * chunk, len);
+    t.end = min(len, t.begin + chunk);
+    t.nsplit = (len + chunk - 1) / chunk;  // non-empty splits of this row
+    return t;
+}
+
+__device__ __forceinline__ float dot4(const float4& a, const float4& b)
+{
+    return fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, a.w * b.w)));
+}
+
+// merge (m2, l2, acc2) into (m, l, acc)
+__device__ __forceinline__ void softmax_merge(float& m, float& l, float4& acc, float m2, float l2, const float4& acc2)
+{
+    const float mn = fmaxf(m, m2);
+    const float w1 = (m == -INFINITY) ? 0.0f : expf(m - mn);
+    const float w2 = (m2 == -INFINITY) ? 0.0f : expf(m2 - mn);
+    l = l * w1 + l2 * w2;
+    acc.x = acc.x * w1 + acc2.x * w2;
+    acc.y = acc.y * w1 + acc2.y * w2;
+    acc.z = acc.z * w1 + acc2.z * w2;
+    acc.w = acc.w * w1 + acc2.w * w2;
+    m = mn;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
+{
+    constexpr int G = HD / 4;       // lanes per key
+    constexpr int KPW = 32 / G;     // keys per warp step
+    constexpr int U = 4;            // steps whose loads are in flight together
     __shared__ float sm_m[4], sm_l[4];
-    __shared__ float sm_acc[4][HD];
+    __shared__ __align__(16) float sm_acc[4][HD];
     __shared__ int sm_last;
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int grp = lane / G, lig = lane % G;
     const uint32_t h = blockIdx.x, r = a.row0 + blockIdx.y, s = blockIdx.z;
-    uint32_t b, len;
-    if (a.lens) { b = r; len = a.lens[r]; }
-    else if (a.pos) { b = r; len = a.pos[r] + 1; }
-    else { b = r / a.P; len = r % a.P + 1; }
-    const uint32_t begin = s * a.chunk;
-    const uint32_t end = min(len, begin + a.chunk);
 
-    const float* K = a.kc + (uint64_t)b * a.seq_stride + (uint64_t)h * a.C * HD;
-    const float* Vv = a.vc + (uint64_t)b * a.seq_stride + (uint64_t)h * a.C * HD;
+    griddep_launch_dependents();
+    griddep_wait();  // q and the newest K/V rows come from the previous kernel
 
-    float qv[DPL];
-    const float* qp = a.q + (uint64_t)r * a.ldq + h * HD + lane * DPL;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) qv[i] = qp[i];
+    const AttnUnit cu = attention_unit(a, r, s);
+    const float* K = a.kc + (uint64_t)cu.b * a.seq_stride + (uint64_t)h * a.C * HD + lig * 4;
+    const float* V = a.vc + (uint64_t)cu.b * a.seq_stride + (uint64_t)h * a.C * HD + lig * 4;
+    float4 q = *reinterpret_cast<const float4*>(a.q + (uint64_t)r * a.ldq + h * HD + lig * 4);
+    q.x *= a.scale; q.y *= a.scale; q.z *= a.scale; q.w *= a.scale;
 
-    float m_run = -INFINITY, l_run = 0.0f;
-    float acc[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = 0.0f;
-
-    for (uint32_t j0 = begin + warp * 32u; j0 < end; j0 += 128u)
+    float m = -INFINITY, l = 0.0f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr uint32_t STEP = 4 * KPW;  // keys per CTA step (4 warps)
+    const uint32_t last = cu.end > 0 ? cu.end - 1 : 0;
+    // the trip count depends on the warp only (never on the lane group): the
+    // loop body has full-warp shuffles, so every lane must run every step
+    for (uint32_t kw = cu.begin + warp * KPW; kw < cu.end; kw += U * STEP)
     {
-        float part[32];
+        const uint32_t kb = kw + grp;  // this group's first key of the step
+        float4 kk[U], vv[U];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj)
+        for (int u = 0; u < U; ++u)
         {
-            float sdot = 0.0f;
-            if (j0 + jj < end)
-            {
-                const float* kr = K + (uint64_t)(j0 + jj) * HD + lane * DPL;
-                if constexpr (DPL == 4)
-                {
-                    const float4 k4 = *reinterpret_cast<const float4*>(kr);
-                    sdot = qv[0] * k4.x + qv[1] * k4.y + qv[2] * k4.z + qv[3] * k4.w;
-                }
-                else if constexpr (DPL == 2)
-                {
-                    const float2 k2 = *reinterpret_cast<const float2*>(kr);
-                    sdot = qv[0] * k2.x + qv[1] * k2.y;
-                }
-                else
-                {
-                    sdot = qv[0] * kr[0];
-                }
-            }
-            part[jj] = sdot;
+            const uint32_t j = min(kb + u * STEP, last);  // clamped in range, masked below
+            kk[u] = *reinterpret_cast<const float4*>(K + (uint64_t)j * HD);
+            vv[u] = *reinterpret_cast<const float4*>(V + (uint64_t)j * HD);
         }
-        warp_transpose_reduce<32>(part, lane);
-        // lane now holds the full dot product of key j0 + lane
-        const bool valid = j0 + lane < end;
-        const float sc = valid ? part[0] * a.scale : -INFINITY;
-        const float tile_max = warp_max(sc);
-        const float m_new = fmaxf(m_run, tile_max);
-        const float p = valid ? expf(sc - m_new) : 0.0f;
-        const float corr = expf(m_run - m_new);
-        l_run = l_run * corr + warp_sum(p);
+        float sc[U];
+        float smax = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[i] *= corr;
-        const uint32_t nvalid = min(32u, end - j0);
-        for (uint32_t jj = 0; jj < nvalid; ++jj)
+        for (int u = 0; u < U; ++u)
         {
-            const float pj = __shfl_sync(FULL_MASK, p, jj);
-            const float* vr = Vv + (uint64_t)(j0 + jj) * HD + lane * DPL;
-            if constexpr (DPL == 4)
-            {
-                const float4 v4 = *reinterpret_cast<const float4*>(vr);
-                acc[0] = fmaf(pj, v4.x, acc[0]);
-                acc[1] = fmaf(pj, v4.y, acc[1]);
-                acc[2] = fmaf(pj, v4.z, acc[2]);
-                acc[3] = fmaf(pj, v4.w, acc[3]);
-            }
-            else if constexpr (DPL == 2)
-            {
-                const float2 v2 = *reinterpret_cast<const float2*>(vr);
-                acc[0] = fmaf(pj, v2.x, acc[0]);
-                acc[1] = fmaf(pj, v2.y, acc[1]);
-            }
-            else
-            {
-                acc[0] = fmaf(pj, vr[0], acc[0]);
-            }
+            float d = dot4(q, kk[u]);
+#pragma unroll
+            for (int o = G / 2; o > 0; o >>= 1) d += __shfl_xor_sync(FULL_MASK, d, o);
+            sc[u] = (kb + u * STEP < cu.end) ? d : -INFINITY;
+            smax = fmaxf(smax, sc[u]);
         }
-        m_run = m_new;
+        if (smax > m)  // rescale only when the running max grows
+        {
+            const float corr = (m == -INFINITY) ? 0.0f : expf(m - smax);
+            l *= corr;
+            acc.x *= corr; acc.y *= corr; acc.z *= corr; acc.w *= corr;
+            m = smax;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const float p = (sc[u] == -INFINITY) ? 0.0f : expf(sc[u] - m);
+            l += p;
+            acc.x = fmaf(p, vv[u].x, acc.x);
+            acc.y = fmaf(p, vv[u].y, acc.y);
+            acc.z = fmaf(p, vv[u].z, acc.z);
+            acc.w = fmaf(p, vv[u].w, acc.w);
+        }
     }
 
-    if (lane == 0) { sm_m[warp] = m_run; sm_l[warp] = l_run; }
+    // merge the KPW groups of the warp (xor across groups)
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) sm_acc[warp][lane * DPL + i] = acc[i];
+    for (int o = G; o < 32; o <<= 1)
+    {
+        const float m2 = __shfl_xor_sync(FULL_MASK, m, o);
+        const float l2 = __shfl_xor_sync(FULL_MASK, l, o);
+        float4 a2;
+        a2.x = __shfl_xor_sync(FULL_MASK, acc.x, o);
+        a2.y = __shfl_xor_sync(FULL_MASK, acc.y, o);
+        a2.z = __shfl_xor_sync(FULL_MASK, acc.z, o);
+        a2.w = __shfl_xor_sync(FULL_MASK, acc.w, o);
+        softmax_merge(m, l, acc, m2, l2, a2);
+    }
+    if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
+    if (grp == 0) *reinterpret_cast<float4*>(&sm_acc[warp][lig * 4]) = acc;
     __syncthreads();
 
-    // merge the 4 warps
+    // merge the 4 warps: thread e < HD owns output dim e
+    const int e = tid;
     const float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
-    float w4[4];
-    float L = 0.0f;
+    float w4[4], L = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
     {
-        w4[i] = (M == -INFINITY) ? 0.0f : expf(sm_m[i] - M);
+        w4[i] = (sm_m[i] == -INFINITY) ? 0.0f : expf(sm_m[i] - M);
         L += sm_l[i] * w4[i];
     }
-    const int e = threadIdx.x;
-    if (a.S == 1)
+    const float A = e < HD ? sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3]
+                           : 0.0f;
+    if (cu.nsplit <= 1)
     {
-        if (e < HD)
-        {
-            const float A = sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3];
-            a.out[(uint64_t)r * a.ldo + h * HD + e] = L > 0.0f ? A / L : 0.0f;
-        }
+        if (e < HD && s == 0) a.out[(uint64_t)r * a.ldo + h * HD + e] = L > 0.0f ? A / L : 0.0f;
         return;
     }
-
-    float* mypart = a.part + (((uint64_t)b * a.H + h) * a.S + s) * (HD + 2);
-    if (e < HD)
-        mypart[e] = sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3];
+    if (cu.begin >= cu.end) return;  // an empty split beyond this row's keys
+    float* mypart = a.part + (((uint64_t)cu.b * a.H + h) * a.S + s) * (HD + 2);
+    if (e < HD) mypart[e] = A;
     if (e == 0) { mypart[HD] = M; mypart[HD + 1] = L; }
     __threadfence();
     __syncthreads();
     if (e == 0)
     {
-        const uint32_t prev = atomicAdd(a.counters + (uint64_t)b * a.H + h, 1u);
-        sm_last = (prev == a.S - 1) ? 1 : 0;
+        const uint32_t prev = atomicAdd(a.counters + (uint64_t)cu.b * a.H + h, 1u);
+        sm_last = (prev == cu.nsplit - 1) ? 1 : 0;
     }
     __syncthreads();
     if (!sm_last) return;
     __threadfence();
-    const float* parts = a.part + ((uint64_t)b * a.H + h) * a.S * (HD + 2);
+    const float* parts = a.part + ((uint64_t)cu.b * a.H + h) * a.S * (HD + 2);
     float Mg = -INFINITY;
-    for (uint32_t i = 0; i < a.S; ++i) Mg = fmaxf(Mg, __ldcg(parts + i * (HD + 2) + HD));
+    for (uint32_t i = 0; i < cu.nsplit; ++i) Mg = fmaxf(Mg, __ldcg(parts + i * (HD + 2) + HD));
     float Lg = 0.0f, Ag = 0.0f;
-    for (uint32_t i = 0; i < a.S; ++i)
+    for (uint32_t i = 0; i < cu.nsplit; ++i)
     {
-        const float mi = __ldcg(parts + i * (HD + 2) + HD);
-        const float wi = (mi == -INFINITY) ? 0.0f : expf(mi - Mg);
+        const float wi = expf(__ldcg(parts + i * (HD + 2) + HD) - Mg);
         Lg += __ldcg(parts + i * (HD + 2) + HD + 1) * wi;
         if (e < HD) Ag += __ldcg(parts + i * (HD + 2) + e) * wi;
     }
     if (e < HD) a.out[(uint64_t)r * a.ldo + h * HD + e] = Lg > 0.0f ? Ag / Lg : 0.0f;
-    if (e == 0) a.counters[(uint64_t)b * a.H + h] = 0u;
+    if (e == 0) a.counters[(uint64_t)cu.b * a.H + h] = 0u;
 }
 
-
-int launch_attention_kernel(const AttnArgs& a, uint32_t hd, dim3 grid, cudaStream_t st)
+template <int HD>
+static int launch_attention_hd(AttnArgs a, dim3 grid, cudaStream_t st, bool pdl)
 {
-    switch (hd)
-    {
-    case 32: attention_kernel<32><<<grid, 128, 0, st>>>(a); break;
-    case 64: attention_kernel<64><<<grid, 128, 0, st>>>(a); break;
-    case 128: attention_kernel<128><<<grid, 128, 0, st>>>(a); break;
-    default: return set_error(FML_ERR_UNSUPPORTED, "head dim %u not supported (32/64/128)", hd);
-    }
+    a.rows = grid.y;
+    if (grid.x == 0 || grid.y == 0 || grid.z == 0) return FML_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
     FML_LAUNCH_CHECK();
     return FML_OK;
 }
 
-// Split count for `pairs` (row, head) pairs over keys up to `ctx`: about two
-// waves of 148 SMs, each split a multiple of 32 keys.
+int launch_attention_kernel(const AttnArgs& a, uint32_t hd, dim3 grid, cudaStream_t st, bool pdl)
+{
+    switch (hd)
+    {
+    case 32: return launch_attention_hd<32>(a, grid, st, pdl);
+    case 64: return launch_attention_hd<64>(a, grid, st, pdl);
+    case 128: return launch_attention_hd<128>(a, grid, st, pdl);
+    default: return set_error(FML_ERR_UNSUPPORTED, "head dim %u not supported (32/64/128)", hd);
+    }
+}
+
+// Split count for `pairs` (row, head) pairs over keys up to `ctx`: about
+// one wave of 4-warp CTAs (8 per SM on 148 SMs).
 void attention_splits(uint64_t pairs, uint64_t ctx, uint32_t* S_out, uint32_t* chunk_out)
 {
-    uint64_t S = (2 * 148 + pairs - 1) / pairs;
+    uint64_t S = (8 * 148 + pairs - 1) / pairs;
+    if (const char* e = getenv("FML_ATTN_SPLITS"))  // tuning override
+    {
+        const long v = strtol(e, nullptr, 10);
+        if (v >= 1 && v <= 256) S = (uint64_t)v;
+    }
     const uint64_t max_s = (ctx + 31) / 32;
     if (S > max_s) S = max_s;
     if (S < 1) S = 1;
-    uint64_t chunk = (ctx + S - 1) / S;
-    chunk = (chunk + 31) / 32 * 32;
-    if (chunk < 32) chunk = 32;
-    S = (ctx + chunk - 1) / chunk;
     *S_out = (uint32_t)S;
-    *chunk_out = (uint32_t)chunk;
+    *chunk_out = 0;  // keys per split follow each row's length
 }
 
 uint64_t attention_workspace_bytes(uint32_t B, uint32_t H, uint32_t hd, uint32_t S)
 {
-    // split partials (floats), then the per-(row, head) counters, 256-aligned
+    // split partials (floats), then the per-(row, head) merge counters and
+    // the work-unit counter, 256-aligned
     const uint64_t part = (uint64_t)B * H * S * (hd + 2) * sizeof(float);
-    return ((part + 255) / 256) * 256 + (uint64_t)B * H * sizeof(uint32_t);
+    return ((part + 255) / 256) * 256 + ((uint64_t)B * H + 1) * sizeof(uint32_t);
 }
 
 }  // namespace fml
@@ -209,6 +322,15 @@ uint64_t attention_workspace_bytes(uint32_t B, uint32_t H, uint32_t hd, uint32_t
 using namespace fml;
 
 extern "C" {
+
+int fml_device_error_count(uint64_t* count)
+{
+    FML_REQUIRE(count, "fml_device_error_count: null argument");
+    int v = 0;
+    FML_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_attention_timeouts, sizeof(int)));
+    *count = (uint64_t)v;
+    return FML_OK;
+}
 
 size_t fml_attention_workspace_bytes(uint32_t batch, uint32_t heads, uint32_t head_dim, uint32_t context)
 {
@@ -228,6 +350,8 @@ int fml_attention_decode(float* out, const float* q, const float* kcache, const 
     FML_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128,
                 "fml_attention_decode: head_dim %u (need 32, 64 or 128)", head_dim);
     FML_REQUIRE(batch <= 65535u, "fml_attention_decode: batch %u > 65535", batch);
+    FML_REQUIRE(aligned16(q) && aligned16(kcache) && aligned16(vcache),
+                "fml_attention_decode: q and the K/V caches must be 16-byte aligned");
     uint32_t S, chunk;
     attention_splits((uint64_t)batch * heads, context, &S, &chunk);
     const uint64_t need = attention_workspace_bytes(batch, heads, head_dim, S);
@@ -235,9 +359,9 @@ int fml_attention_decode(float* out, const float* q, const float* kcache, const 
                 "fml_attention_decode: workspace of %llu bytes needed (fml_attention_workspace_bytes)",
                 (unsigned long long)need);
     cudaStream_t st = as_stream(stream);
-    const uint64_t part_bytes = need - (uint64_t)batch * heads * sizeof(uint32_t);
+    const uint64_t part_bytes = need - ((uint64_t)batch * heads + 1) * sizeof(uint32_t);
     uint32_t* counters = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + part_bytes);
-    FML_CUDA_TRY(cudaMemsetAsync(counters, 0, (size_t)batch * heads * sizeof(uint32_t), st));
+    FML_CUDA_TRY(cudaMemsetAsync(counters, 0, ((size_t)batch * heads + 1) * sizeof(uint32_t), st));
     AttnArgs a{};
     a.q = q; a.ldq = heads * head_dim; a.row0 = 0;
     a.kc = kcache; a.vc = vcache; a.seq_stride = (uint64_t)heads * context * head_dim;
@@ -247,6 +371,7 @@ int fml_attention_decode(float* out, const float* q, const float* kcache, const 
     a.S = S; a.chunk = chunk; a.scale = scale;
     a.part = static_cast<float*>(workspace);
     a.counters = counters;
+    a.grab = counters + (uint64_t)batch * heads;
     return launch_attention_kernel(a, head_dim, dim3(heads, batch, S), st);
 }
 
@@ -306,6 +431,8 @@ int fml_attention_decode_noalloc(float* out, const float* q, const float* kcache
     FML_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128,
                 "fml_attention_decode_noalloc: head_dim %u (need 32, 64 or 128)", head_dim);
     FML_REQUIRE(batch <= 65535u, "fml_attention_decode_noalloc: batch %u > 65535", batch);
+    FML_REQUIRE(aligned16(q) && aligned16(kcache) && aligned16(vcache),
+                "fml_attention_decode_noalloc: q and the K/V caches must be 16-byte aligned");
     uint32_t S, chunk;
     attention_splits((uint64_t)batch * heads, context, &S, &chunk);
     const uint64_t need = attention_workspace_bytes(batch, heads, head_dim, S);
@@ -319,9 +446,9 @@ int fml_attention_decode_noalloc(float* out, const float* q, const float* kcache
     cudaStream_t st = as_stream(stream);
     // The array keeps whatever the previous call left; the merge counters must
     // start at zero, so clear them (a memset, not an allocation).
-    const uint64_t part_bytes = need - (uint64_t)batch * heads * sizeof(uint32_t);
+    const uint64_t part_bytes = need - ((uint64_t)batch * heads + 1) * sizeof(uint32_t);
     uint32_t* counters = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + part_bytes);
-    FML_CUDA_TRY(cudaMemsetAsync(counters, 0, (size_t)batch * heads * sizeof(uint32_t), st));
+    FML_CUDA_TRY(cudaMemsetAsync(counters, 0, ((size_t)batch * heads + 1) * sizeof(uint32_t), st));
     AttnArgs a{};
     a.q = q; a.ldq = heads * head_dim; a.row0 = 0;
     a.kc = kcache; a.vc = vcache; a.seq_stride = (uint64_t)heads * context * head_dim;
@@ -331,6 +458,7 @@ int fml_attention_decode_noalloc(float* out, const float* q, const float* kcache
     a.S = S; a.chunk = chunk; a.scale = scale;
     a.part = static_cast<float*>(scratch);
     a.counters = counters;
+    a.grab = counters + (uint64_t)batch * heads;
     return launch_attention_kernel(a, head_dim, dim3(heads, batch, S), st);
 }
 

@@ -76,6 +76,16 @@ __device__ __forceinline__ float warp_max(float v)
     return v;
 }
 
+// Programmatic dependent launch (sm_90+): let the next kernel in the stream
+// start its prologue now / wait until the previous kernel's writes are
+// visible.  Both are no-ops when the launch did not opt in.
+__device__ __forceinline__ void griddep_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // GeluMat's formula (MatrixBase_Functions.h:989-1000): 0.5 x (1 + erf(x / sqrt 2)).
 __device__ __forceinline__ float gelu_exact(float x)
 {

@@ -29,7 +29,9 @@
 //   layernorm -> fc gemv (+gelu) -> mlp gemv (+residual) } -> layernorm ->
 //   lm_head gemv (+argmax keys) -> finalize
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 #include <vector>
 
 #include "attention.cuh"
@@ -49,8 +51,13 @@ int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int 
 // t = pos[b].  Prefill: r = b*P + t, id = prompt[r].
 __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ tok, const float* __restrict__ posemb,
                              const uint32_t* __restrict__ ids, const uint32_t* __restrict__ pos, uint32_t rows,
-                             uint32_t P, uint32_t d, uint32_t V, uint32_t C)
+                             uint32_t P, uint32_t d, uint32_t V, uint32_t C, uint32_t* zero, uint32_t nzero)
 {
+    griddep_launch_dependents();
+    griddep_wait();
+    // the step's first kernel clears the per-layer attention work counters
+    if (blockIdx.x == 0)
+        for (uint32_t i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0u;
     for (uint32_t r = blockIdx.x; r < rows; r += gridDim.x)
     {
         const uint32_t t = pos ? pos[r] : r % P;
@@ -88,57 +95,151 @@ struct GemvArgs
     uint64_t seq_stride;  // H*C*hd: one sequence's block inside a layer
     // EPI_ARGMAX
     unsigned long long* keys;
+    // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
+    const float* gamma;
 };
 
-// y[m, n] = sum_k x[m, k] W[n, k] for the small-M (decode) shapes.
-// CTA = 4 warps, 4 output columns n; the warps split K (each lane owns 4
-// consecutive k, a float4 of every W row and x row), so every W element is
-// read once per step.  Partial sums are combined by a warp transpose-reduce
-// (each lane ends up owning distinct outputs) and a 4-way shared-memory sum,
-// then the epilogue runs on one thread per output.
-template <int MT, int EPI>
+// y[m, n] = sum_k xn[m, k] W[n, k] for the small-M (decode) shapes, where
+// xn = x, or LayerNormOp(x) with gamma (LN = true: LayerNorm.h:148-165 fused
+// into the consumer -- every CTA recomputes the two-pass statistics of its
+// rows, so no separate LayerNorm launch and no cross-CTA reduction).
+//
+// CTA = 4 warps, 4 output columns n, MT rows m.  The 128 threads partition K
+// in float4 slices (thread t owns k = 4t + 512i), so each W element is read
+// once per step and every load of an iteration is issued before any use.
+// The CTA's first W slice is loaded before griddepcontrol.wait: with
+// programmatic dependent launch it streams in while the previous kernel
+// finishes.  Partial sums are combined by a warp transpose-reduce (each lane
+// ends up owning distinct outputs) and a 4-way shared-memory sum; the
+// epilogue runs on one thread per output.
+template <int MT, int EPI, bool LN>
 __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
 {
     constexpr int NW = 4;
     constexpr int CNT = MT * NW;
     constexpr int R = CNT >= 32 ? CNT / 32 : 1;
+    constexpr int RM = MT >= 32 ? MT / 32 : 1;
     __shared__ float red[4][CNT];
+    __shared__ float s_part[4][MT];
+    __shared__ float s_mean[MT], s_rstd[MT];
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // blockIdx.x walks the row chunks of one column group, so the CTAs that
-    // share a W slice run together and the slice comes from HBM once
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t n0 = blockIdx.y * NW;
     const uint32_t m0 = blockIdx.x * MT;
+    const uint32_t k_first = (uint32_t)tid * 4u;
+
+    const float* wrow[NW];
+#pragma unroll
+    for (int j = 0; j < NW; ++j) wrow[j] = a.w + (uint64_t)min(n0 + j, a.N - 1) * a.K;
+    // row pointers clamped into range: loads stay unconditional and in bounds
+    const float* xrow[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) xrow[m] = a.x + (uint64_t)min(m0 + m, a.M - 1) * a.ldx;
+
+    float4 wv[NW];
+    const bool have_first = k_first < a.K;
+#pragma unroll
+    for (int j = 0; j < NW; ++j)
+        wv[j] = have_first ? __ldg(reinterpret_cast<const float4*>(wrow[j] + k_first)) : make_float4(0, 0, 0, 0);
+
+    griddep_launch_dependents();
+    griddep_wait();
+
+    if constexpr (LN)
+    {
+        // two-pass mean / biased variance per row, like LayerNormOp
+        float ps[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) ps[m] = 0.0f;
+        for (uint32_t k = k_first; k < a.K; k += 512u)
+        {
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+            {
+                const float4 xv = *reinterpret_cast<const float4*>(xrow[m] + k);
+                ps[m] += (xv.x + xv.y) + (xv.z + xv.w);
+            }
+        }
+        warp_transpose_reduce<MT>(ps, lane);
+        if (reduce_owner<MT>(lane))
+        {
+            const int base = reduce_base<MT>(lane);
+#pragma unroll
+            for (int i = 0; i < RM; ++i) s_part[warp][base + i] = ps[i];
+        }
+        __syncthreads();
+        const float invK = 1.0f / (float)a.K;
+        if (tid < MT) s_mean[tid] = (s_part[0][tid] + s_part[1][tid] + s_part[2][tid] + s_part[3][tid]) * invK;
+        __syncthreads();
+        float mean[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) { mean[m] = s_mean[m]; ps[m] = 0.0f; }
+        for (uint32_t k = k_first; k < a.K; k += 512u)
+        {
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+            {
+                const float4 xv = *reinterpret_cast<const float4*>(xrow[m] + k);
+                const float d0 = xv.x - mean[m], d1 = xv.y - mean[m], d2 = xv.z - mean[m], d3 = xv.w - mean[m];
+                ps[m] = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, fmaf(d3, d3, ps[m]))));
+            }
+        }
+        warp_transpose_reduce<MT>(ps, lane);
+        __syncthreads();  // s_part reuse
+        if (reduce_owner<MT>(lane))
+        {
+            const int base = reduce_base<MT>(lane);
+#pragma unroll
+            for (int i = 0; i < RM; ++i) s_part[warp][base + i] = ps[i];
+        }
+        __syncthreads();
+        if (tid < MT)
+        {
+            const float var = s_part[0][tid] + s_part[1][tid] + s_part[2][tid] + s_part[3][tid];
+            s_rstd[tid] = 1.0f / sqrtf(fmaf(var, invK, 1e-5f));
+        }
+        __syncthreads();
+    }
 
     float acc[CNT];
 #pragma unroll
     for (int i = 0; i < CNT; ++i) acc[i] = 0.0f;
 
-    const float* wrow[NW];
-#pragma unroll
-    for (int j = 0; j < NW; ++j) wrow[j] = a.w + (uint64_t)min(n0 + j, a.N - 1) * a.K;
-
-    for (uint32_t k = (uint32_t)warp * 128u + (uint32_t)lane * 4u; k < a.K; k += 512u)
+    for (uint32_t k = k_first; k < a.K; k += 512u)
     {
-        float4 wv[NW];
+        if (k != k_first)
+        {
 #pragma unroll
-        for (int j = 0; j < NW; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(wrow[j] + k));
+            for (int j = 0; j < NW; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(wrow[j] + k));
+        }
+        float4 xv[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) xv[m] = *reinterpret_cast<const float4*>(xrow[m] + k);
+        if constexpr (LN)
+        {
+            const float4 g = *reinterpret_cast<const float4*>(a.gamma + k);
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+            {
+                const float mu = s_mean[m], rs = s_rstd[m];
+                xv[m].x = (xv[m].x - mu) * rs * g.x;
+                xv[m].y = (xv[m].y - mu) * rs * g.y;
+                xv[m].z = (xv[m].z - mu) * rs * g.z;
+                xv[m].w = (xv[m].w - mu) * rs * g.w;
+            }
+        }
 #pragma unroll
         for (int m = 0; m < MT; ++m)
         {
-            if (m0 + m < a.M)
-            {
-                const float4 xv = *reinterpret_cast<const float4*>(a.x + (uint64_t)(m0 + m) * a.ldx + k);
 #pragma unroll
-                for (int j = 0; j < NW; ++j)
-                {
-                    float s = acc[m * NW + j];
-                    s = fmaf(xv.x, wv[j].x, s);
-                    s = fmaf(xv.y, wv[j].y, s);
-                    s = fmaf(xv.z, wv[j].z, s);
-                    s = fmaf(xv.w, wv[j].w, s);
-                    acc[m * NW + j] = s;
-                }
+            for (int j = 0; j < NW; ++j)
+            {
+                float sacc = acc[m * NW + j];
+                sacc = fmaf(xv[m].x, wv[j].x, sacc);
+                sacc = fmaf(xv[m].y, wv[j].y, sacc);
+                sacc = fmaf(xv[m].z, wv[j].z, sacc);
+                sacc = fmaf(xv[m].w, wv[j].w, sacc);
+                acc[m * NW + j] = sacc;
             }
         }
     }
@@ -225,6 +326,7 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
 __global__ void finalize_kernel(unsigned long long* keys, uint32_t* pending, uint32_t* pos, uint32_t* next_out,
                                 uint32_t B, uint32_t set_pos)
 {
+    griddep_wait();
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const uint32_t tok = argmax_key_index(keys[b]);
@@ -305,14 +407,16 @@ struct fml_lm
     unsigned long long* keys = nullptr;
     float* part = nullptr;
     uint32_t* counters = nullptr;
+    uint32_t* grab = nullptr;  // [L] attention work-unit counters
     uint32_t* host_io = nullptr;  // pinned [2 * max_batch]
     uint32_t S = 1, chunk = 0;
 
     uint32_t batch = 0;                // active sequences
     std::vector<uint32_t> hpos;        // host mirror of positions
 
-    // graph
+    // graph / programmatic dependent launch
     bool use_graph = true;
+    bool pdl = true;
     cudaGraphExec_t graph_exec = nullptr;
     cudaStream_t graph_stream = nullptr;
     uint32_t* graph_next = nullptr;
@@ -342,7 +446,7 @@ void free_all(fml_lm* lm)
     for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
     void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
                     lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
-                    lm->counters, lm->prompt_dev};
+                    lm->counters, lm->prompt_dev, lm->grab};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (lm->host_io) cudaFreeHost(lm->host_io);
@@ -392,21 +496,42 @@ int collect_profile(fml_lm* lm)
     return FML_OK;
 }
 
-template <int EPI>
-int launch_gemv(const GemvArgs& a, cudaStream_t st)
+// Launch with programmatic dependent launch when `pdl` is set: the kernel may
+// start while the previous one in the stream finishes (it calls
+// griddepcontrol.wait before reading that kernel's output).
+template <typename... KArgs, typename... Args>
+int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args... args)
 {
-    FML_REQUIRE(a.K % 4 == 0 && a.ldx % 4 == 0, "gemv: K and ldx must be multiples of 4");
-    const unsigned gy = (a.N + 3) / 4;
-    FML_REQUIRE(gy <= 65535u, "gemv: N = %u too large", a.N);
-    if (a.M <= 4) gemv_kernel<4, EPI><<<dim3(1, gy), 128, 0, st>>>(a);
-    else if (a.M <= 8) gemv_kernel<8, EPI><<<dim3(1, gy), 128, 0, st>>>(a);
-    else gemv_kernel<16, EPI><<<dim3((a.M + 15) / 16, gy), 128, 0, st>>>(a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "cudaLaunchKernelEx: %s", cudaGetErrorString(e));
     FML_LAUNCH_CHECK();
     return FML_OK;
 }
 
+template <int EPI, bool LN>
+int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
+{
+    FML_REQUIRE(a.K % 4 == 0 && a.ldx % 4 == 0, "gemv: K and ldx must be multiples of 4");
+    FML_REQUIRE(!LN || a.gamma, "gemv: LayerNorm prologue without gamma");
+    const unsigned gy = (a.N + 3) / 4;
+    FML_REQUIRE(gy <= 65535u, "gemv: N = %u too large", a.N);
+    if (a.M <= 4) return launch_k(gemv_kernel<4, EPI, LN>, dim3(1, gy), dim3(128), st, pdl, a);
+    if (a.M <= 8) return launch_k(gemv_kernel<8, EPI, LN>, dim3(1, gy), dim3(128), st, pdl, a);
+    return launch_k(gemv_kernel<16, EPI, LN>, dim3((a.M + 15) / 16, gy), dim3(128), st, pdl, a);
+}
+
 int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, const uint32_t* pos, uint32_t P,
-                     uint32_t S, uint32_t chunk, cudaStream_t st)
+                     uint32_t S, uint32_t chunk, cudaStream_t st, bool pdl = false)
 {
     AttnArgs a{};
     a.row0 = row0;
@@ -426,85 +551,79 @@ int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, c
     a.scale = 1.0f / sqrtf((float)lm->hd);
     a.part = lm->part;
     a.counters = lm->counters;
+    a.grab = lm->grab + layer;
     FML_REQUIRE(rows <= 65535u, "attention: too many rows in one launch (%u)", rows);
-    FML_RC(launch_attention_kernel(a, lm->hd, dim3(lm->cfg.n_head, rows, S), st));
+    FML_RC(launch_attention_kernel(a, lm->hd, dim3(lm->cfg.n_head, rows, S), st, pdl));
     return FML_OK;
 }
 
-// Enqueue one decode step for the active batch.
+// Enqueue one decode step for the active batch: embed, per layer
+// {qkv (LayerNorm fused) -> attention -> proj + residual -> fc (LayerNorm
+// fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
+// finalize.  Every launch after the first uses programmatic dependent launch.
 int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
 {
     const fml_lm_config& c = lm->cfg;
     const uint32_t B = lm->batch, d = c.d_model;
+    const bool pdl = lm->pdl && !lm->profiling;
     {
         ProfScope ps(lm, 0, st);
-        embed_kernel<<<B, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->pending, lm->pos, B, 1, d, c.vocab, c.context);
-        FML_LAUNCH_CHECK();
+        FML_RC(launch_k(embed_kernel, dim3(B), dim3(128), st, false, lm->x, (const float*)lm->tok,
+                        (const float*)lm->pos_emb, (const uint32_t*)lm->pending, (const uint32_t*)lm->pos, B, 1u, d,
+                        c.vocab, c.context, lm->grab, c.n_layer));
     }
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         {
-            ProfScope ps(lm, 1, st);
-            FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
-        }
-        {
             ProfScope ps(lm, 2, st);
             GemvArgs a{};
-            a.x = lm->ln; a.ldx = d; a.w = lm->wqkv[l]; a.M = B; a.N = 3 * d; a.K = d;
+            a.x = lm->x; a.ldx = d; a.w = lm->wqkv[l]; a.M = B; a.N = 3 * d; a.K = d; a.gamma = lm->ln0[l];
             a.q = lm->q; a.kc = lm->kc + (uint64_t)l * lm->layer_stride; a.vc = lm->vc + (uint64_t)l * lm->layer_stride;
             a.pos = lm->pos; a.d = d; a.H = c.n_head; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
-            FML_RC(launch_gemv<EPI_QKV>(a, st));
+            FML_RC((launch_gemv<EPI_QKV, true>(a, st, pdl)));
         }
         {
             ProfScope ps(lm, 3, st);
-            FML_RC(launch_attention(lm, l, 0, B, lm->pos, 1, lm->S, lm->chunk, st));
+            FML_RC(launch_attention(lm, l, 0, B, lm->pos, 1, lm->S, 0, st, pdl));
         }
         {
             ProfScope ps(lm, 4, st);
             GemvArgs a{};
             a.x = lm->att; a.ldx = d; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = d;
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            FML_RC(launch_gemv<EPI_RESID>(a, st));
-        }
-        {
-            ProfScope ps(lm, 1, st);
-            FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
+            FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
         }
         {
             ProfScope ps(lm, 5, st);
             GemvArgs a{};
-            a.x = lm->ln; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = 4 * d; a.K = d;
+            a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = 4 * d; a.K = d; a.gamma = lm->ln1[l];
             a.y = lm->hid; a.ldy = 4 * d;
-            FML_RC(launch_gemv<EPI_GELU>(a, st));
+            FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl)));
         }
         {
             ProfScope ps(lm, 6, st);
             GemvArgs a{};
             a.x = lm->hid; a.ldx = 4 * d; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = 4 * d;
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            FML_RC(launch_gemv<EPI_RESID>(a, st));
+            FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
         }
-    }
-    {
-        ProfScope ps(lm, 1, st);
-        FML_RC(launch_layernorm(lm->ln, lm->x, lm->lnf, nullptr, nullptr, B, d, d, d, 1e-5f, st));
     }
     {
         ProfScope ps(lm, 7, st);
         GemvArgs a{};
-        a.x = lm->ln; a.ldx = d; a.w = lm->tok; a.M = B; a.N = c.vocab; a.K = d;
+        a.x = lm->x; a.ldx = d; a.w = lm->tok; a.M = B; a.N = c.vocab; a.K = d; a.gamma = lm->lnf;
         a.y = logits; a.ldy = c.vocab; a.keys = lm->keys;
-        FML_RC(launch_gemv<EPI_ARGMAX>(a, st));
+        FML_RC((launch_gemv<EPI_ARGMAX, true>(a, st, pdl)));
     }
     {
         ProfScope ps(lm, 8, st);
-        finalize_kernel<<<(B + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, next_out, B, 0);
-        FML_LAUNCH_CHECK();
+        FML_RC(launch_k(finalize_kernel, dim3((B + 127) / 128), dim3(128), st, pdl, lm->keys, lm->pending, lm->pos,
+                        next_out, B, 0u));
     }
     return FML_OK;
 }
 
-uint32_t graph_nodes_per_step(const fml_lm_config& c) { return 1 + c.n_layer * 7 + 3; }
+uint32_t graph_nodes_per_step(const fml_lm_config& c) { return 1 + c.n_layer * 5 + 2; }
 
 }  // namespace
 
@@ -536,6 +655,11 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     const uint64_t rows = B * Ctx;
 
     attention_splits(B * H, Ctx, &lm->S, &lm->chunk);
+    if (const char* e = getenv("FML_ATTN_SPLITS"))  // tuning override (keys split over S CTAs)
+    {
+        const long v = strtol(e, nullptr, 10);
+        if (v >= 1 && v <= 64) lm->S = (uint32_t)v;
+    }
 
     auto alloc = [&](void** p, uint64_t bytes) -> int {
         cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
@@ -565,6 +689,7 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     if (!rc) rc = alloc((void**)&lm->keys, B * 8);
     if (!rc) rc = alloc((void**)&lm->part, B * H * lm->S * (hd + 2) * f);
     if (!rc) rc = alloc((void**)&lm->counters, B * H * 4);
+    if (!rc) rc = alloc((void**)&lm->grab, L * 4);
     if (!rc && cudaMallocHost((void**)&lm->host_io, 2 * B * 4) != cudaSuccess)
         rc = set_error(FML_ERR_NOMEM, "cudaMallocHost failed");
     if (rc)
@@ -577,6 +702,7 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     cudaMemset(lm->pos, 0, B * 4);
     cudaMemset(lm->keys, 0, B * 8);
     cudaMemset(lm->counters, 0, B * H * 4);
+    cudaMemset(lm->grab, 0, L * 4);
 
     // carve the weight buffer
     float* p = lm->wbuf;
@@ -693,7 +819,7 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     FML_CUDA_TRY(cudaMemcpyAsync(lm->prompt_dev, prompts, (uint64_t)R * 4, cudaMemcpyDeviceToDevice, st));
     FML_CUDA_TRY(cudaMemsetAsync(lm->keys, 0, (uint64_t)c.max_batch * 8, st));
     embed_kernel<<<R < 65535u ? R : 65535u, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->prompt_dev, nullptr, R, P, d,
-                                                          c.vocab, c.context);
+                                                          c.vocab, c.context, nullptr, 0u);
     FML_LAUNCH_CHECK();
     const uint64_t n = (uint64_t)R * d;
     for (uint32_t l = 0; l < c.n_layer; ++l)
@@ -709,7 +835,10 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
         // prefill attention: one query row per (b, t), the whole causal key
         // range in one CTA, launched in slabs of at most 65535 rows
         for (uint32_t r0 = 0; r0 < R; r0 += 65535u)
+        {
+            FML_CUDA_TRY(cudaMemsetAsync(lm->grab + l, 0, sizeof(uint32_t), st));
             FML_RC(launch_attention(lm, l, r0, R - r0 < 65535u ? R - r0 : 65535u, nullptr, P, 1, c.context, st));
+        }
         FML_RC(gemm_f32(lm->tmp, lm->att, lm->wproj[l], (int)R, (int)d, (int)d, (int)d, (int)d, (int)d, true, 1, 0, 0,
                         0, st));
         add_kernel<<<grid_for(n, 256), 256, 0, st>>>(lm->buf, lm->x, lm->tmp, n);
@@ -730,7 +859,7 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     GemvArgs a{};
     a.x = lm->ln; a.ldx = d; a.w = lm->tok; a.M = batch; a.N = c.vocab; a.K = d; a.y = nullptr; a.ldy = c.vocab;
     a.keys = lm->keys;
-    FML_RC(launch_gemv<EPI_ARGMAX>(a, st));
+    FML_RC((launch_gemv<EPI_ARGMAX, false>(a, st, false)));
     finalize_kernel<<<(batch + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, nullptr, batch, P);
     FML_LAUNCH_CHECK();
     for (uint32_t b = 0; b < batch; ++b) lm->hpos[b] = P;

@@ -62,6 +62,10 @@ enum fml_status
 FML_API const char* fml_last_error(void);
 FML_API const char* fml_version(void);
 FML_API int fml_device_check(int* sm_count, int* cc_major, int* cc_minor);
+/* Device-side waits that hit their iteration limit since the library loaded
+ * (every wait in these kernels is bounded; a non-zero count means a kernel
+ * gave up and its output is invalid).  Synchronises the device. */
+FML_API int fml_device_error_count(uint64_t* count);
 /* Number of kernels this library has launched in this process (all entry
  * points, graph replays counted per kernel node). */
 FML_API uint64_t fml_kernel_launch_count(void);
