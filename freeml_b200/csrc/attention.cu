@@ -131,6 +131,7 @@ __device__ __forceinline__ void softmax_merge(float& m, float& l, float4& acc, f
 template <int HD>
 __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
 {
+    FML_TIMELINE_SCOPE(20);
     constexpr int G = HD / 4;       // lanes per key
     constexpr int KPW = 32 / G;     // keys per warp step
     constexpr int U = 4;            // steps whose loads are in flight together
@@ -292,11 +293,12 @@ int launch_attention_kernel(const AttnArgs& a, uint32_t hd, dim3 grid, cudaStrea
     }
 }
 
-// Split count for `pairs` (row, head) pairs over keys up to `ctx`: about
-// one wave of 4-warp CTAs (8 per SM on 148 SMs).
+// Split count for `pairs` (row, head) pairs over keys up to `ctx`: as many
+// splits as still fit one wave of 4-warp CTAs (8 per SM on 148 SMs) -- a
+// partial second wave would double the kernel's latency chain.
 void attention_splits(uint64_t pairs, uint64_t ctx, uint32_t* S_out, uint32_t* chunk_out)
 {
-    uint64_t S = (8 * 148 + pairs - 1) / pairs;
+    uint64_t S = (8 * 148) / pairs;
     if (const char* e = getenv("FML_ATTN_SPLITS"))  // tuning override
     {
         const long v = strtol(e, nullptr, 10);

@@ -86,6 +86,47 @@ __device__ __forceinline__ void griddep_launch_dependents()
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ---- optional per-CTA timeline (debug builds with -DFML_TIMELINE only) ----
+// Thread 0 of every CTA appends (kernel id, start, end) global-timer stamps
+// to a device ring that the host reads back; compiled out otherwise.
+#ifdef FML_TIMELINE
+struct TimelineRec
+{
+    unsigned long long start, end;
+    uint32_t kernel, cta;
+};
+extern __device__ TimelineRec* g_fml_timeline;
+extern __device__ uint32_t g_fml_timeline_cap;
+extern __device__ uint32_t g_fml_timeline_n;
+__device__ __forceinline__ unsigned long long fml_globaltimer()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+struct TimelineScope
+{
+    unsigned long long t0;
+    uint32_t id;
+    __device__ explicit TimelineScope(uint32_t k) : t0(fml_globaltimer()), id(k) {}
+    __device__ ~TimelineScope()
+    {
+        if (threadIdx.x == 0 && threadIdx.y == 0 && g_fml_timeline)
+        {
+            const uint32_t i = atomicAdd(&g_fml_timeline_n, 1u);
+            if (i < g_fml_timeline_cap)
+                g_fml_timeline[i] = {t0, fml_globaltimer(), id,
+                                     blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)};
+        }
+    }
+};
+#define FML_TIMELINE_SCOPE(k) ::fml::TimelineScope _fml_tl_scope(k)
+#else
+#define FML_TIMELINE_SCOPE(k) \
+    do {                      \
+    } while (0)
+#endif
+
 // GeluMat's formula (MatrixBase_Functions.h:989-1000): 0.5 x (1 + erf(x / sqrt 2)).
 __device__ __forceinline__ float gelu_exact(float x)
 {

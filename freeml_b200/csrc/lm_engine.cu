@@ -37,6 +37,23 @@
 #include "attention.cuh"
 #include "fml_common.cuh"
 
+#ifdef FML_TIMELINE
+namespace fml {
+__device__ TimelineRec* g_fml_timeline = nullptr;
+__device__ uint32_t g_fml_timeline_cap = 0;
+__device__ uint32_t g_fml_timeline_n = 0;
+}  // namespace fml
+extern "C" __attribute__((visibility("default"))) int fml_debug_timeline(void* buf, uint32_t cap)
+{
+    fml::TimelineRec* p = static_cast<fml::TimelineRec*>(buf);
+    const uint32_t zero = 0;
+    if (cudaMemcpyToSymbol(fml::g_fml_timeline, &p, sizeof(p)) != cudaSuccess) return 2;
+    if (cudaMemcpyToSymbol(fml::g_fml_timeline_cap, &cap, sizeof(cap)) != cudaSuccess) return 2;
+    if (cudaMemcpyToSymbol(fml::g_fml_timeline_n, &zero, sizeof(zero)) != cudaSuccess) return 2;
+    return 0;
+}
+#endif
+
 namespace fml {
 
 int launch_layernorm(float* out, const float* in, const float* gamma, const float* beta, float* xhat, uint32_t rows,
@@ -53,6 +70,7 @@ __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ to
                              const uint32_t* __restrict__ ids, const uint32_t* __restrict__ pos, uint32_t rows,
                              uint32_t P, uint32_t d, uint32_t V, uint32_t C, uint32_t* zero, uint32_t nzero)
 {
+    FML_TIMELINE_SCOPE(1);
     griddep_launch_dependents();
     griddep_wait();
     // the step's first kernel clears the per-layer attention work counters
@@ -115,6 +133,7 @@ struct GemvArgs
 template <int MT, int EPI, bool LN>
 __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
 {
+    FML_TIMELINE_SCOPE(10 + EPI);
     constexpr int NW = 4;
     constexpr int CNT = MT * NW;
     constexpr int R = CNT >= 32 ? CNT / 32 : 1;
@@ -130,7 +149,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
 
     const float* wrow[NW];
 #pragma unroll
-    for (int j = 0; j < NW; ++j) wrow[j] = a.w + (uint64_t)min(n0 + j, a.N - 1) * a.K;
+    for (int j = 0; j < NW; ++j) wrow[j] = a.w + (uint64_t)min(blockIdx.y * NW + j, a.N - 1) * a.K;
     // row pointers clamped into range: loads stay unconditional and in bounds
     const float* xrow[MT];
 #pragma unroll
@@ -201,103 +220,122 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
         __syncthreads();
     }
 
-    float acc[CNT];
-#pragma unroll
-    for (int i = 0; i < CNT; ++i) acc[i] = 0.0f;
-
-    for (uint32_t k = k_first; k < a.K; k += 512u)
+    // column groups of this CTA: n0 = 4 * (blockIdx.y + i * gridDim.y)
+    const uint32_t ngroups = (a.N + NW - 1) / NW;
+    for (uint32_t g = blockIdx.y; g < ngroups; g += gridDim.y)
     {
-        if (k != k_first)
-        {
+        const uint32_t n0 = g * NW;
+        const uint32_t gnext = g + gridDim.y;
+        float acc[CNT];
 #pragma unroll
-            for (int j = 0; j < NW; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(wrow[j] + k));
-        }
-        float4 xv[MT];
-#pragma unroll
-        for (int m = 0; m < MT; ++m) xv[m] = *reinterpret_cast<const float4*>(xrow[m] + k);
-        if constexpr (LN)
+        for (int i = 0; i < CNT; ++i) acc[i] = 0.0f;
+
+        for (uint32_t k = k_first; k < a.K; k += 512u)
         {
-            const float4 g = *reinterpret_cast<const float4*>(a.gamma + k);
+            if (k != k_first)
+            {
+#pragma unroll
+                for (int j = 0; j < NW; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(wrow[j] + k));
+            }
+            float4 xv[MT];
+#pragma unroll
+            for (int m = 0; m < MT; ++m) xv[m] = *reinterpret_cast<const float4*>(xrow[m] + k);
+            if constexpr (LN)
+            {
+                const float4 gm = *reinterpret_cast<const float4*>(a.gamma + k);
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                {
+                    const float mu = s_mean[m], rs = s_rstd[m];
+                    xv[m].x = (xv[m].x - mu) * rs * gm.x;
+                    xv[m].y = (xv[m].y - mu) * rs * gm.y;
+                    xv[m].z = (xv[m].z - mu) * rs * gm.z;
+                    xv[m].w = (xv[m].w - mu) * rs * gm.w;
+                }
+            }
 #pragma unroll
             for (int m = 0; m < MT; ++m)
             {
-                const float mu = s_mean[m], rs = s_rstd[m];
-                xv[m].x = (xv[m].x - mu) * rs * g.x;
-                xv[m].y = (xv[m].y - mu) * rs * g.y;
-                xv[m].z = (xv[m].z - mu) * rs * g.z;
-                xv[m].w = (xv[m].w - mu) * rs * g.w;
+#pragma unroll
+                for (int j = 0; j < NW; ++j)
+                {
+                    float sacc = acc[m * NW + j];
+                    sacc = fmaf(xv[m].x, wv[j].x, sacc);
+                    sacc = fmaf(xv[m].y, wv[j].y, sacc);
+                    sacc = fmaf(xv[m].z, wv[j].z, sacc);
+                    sacc = fmaf(xv[m].w, wv[j].w, sacc);
+                    acc[m * NW + j] = sacc;
+                }
             }
         }
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
+
+        // prefetch the next group's first W slice while this one is reduced
+        if (gnext < ngroups)
         {
 #pragma unroll
             for (int j = 0; j < NW; ++j)
             {
-                float sacc = acc[m * NW + j];
-                sacc = fmaf(xv[m].x, wv[j].x, sacc);
-                sacc = fmaf(xv[m].y, wv[j].y, sacc);
-                sacc = fmaf(xv[m].z, wv[j].z, sacc);
-                sacc = fmaf(xv[m].w, wv[j].w, sacc);
-                acc[m * NW + j] = sacc;
+                wrow[j] = a.w + (uint64_t)min(gnext * NW + j, a.N - 1) * a.K;
+                wv[j] = have_first ? __ldg(reinterpret_cast<const float4*>(wrow[j] + k_first)) : make_float4(0, 0, 0, 0);
             }
         }
-    }
 
-    warp_transpose_reduce<CNT>(acc, lane);
-    if (reduce_owner<CNT>(lane))
-    {
-        const int base = reduce_base<CNT>(lane);
+        warp_transpose_reduce<CNT>(acc, lane);
+        __syncthreads();  // red[] of the previous group has been consumed
+        if (reduce_owner<CNT>(lane))
+        {
+            const int base = reduce_base<CNT>(lane);
 #pragma unroll
-        for (int i = 0; i < R; ++i) red[warp][base + i] = acc[i];
-    }
-    __syncthreads();
+            for (int i = 0; i < R; ++i) red[warp][base + i] = acc[i];
+        }
+        __syncthreads();
 
-    const int t = threadIdx.x;
-    if (t < CNT || EPI == EPI_ARGMAX)
-    {
-        const int tt = t < CNT ? t : 0;
-        const float v = red[0][tt] + red[1][tt] + red[2][tt] + red[3][tt];
-        const uint32_t m = m0 + tt / NW, n = n0 + tt % NW;
-        const bool valid = t < CNT && m < a.M && n < a.N;
-        if constexpr (EPI == EPI_STORE)
+        const int t = threadIdx.x;
+        if (t < CNT || EPI == EPI_ARGMAX)
         {
-            if (valid) a.y[(uint64_t)m * a.ldy + n] = v;
-        }
-        else if constexpr (EPI == EPI_GELU)
-        {
-            if (valid) a.y[(uint64_t)m * a.ldy + n] = gelu_exact(v);
-        }
-        else if constexpr (EPI == EPI_RESID)
-        {
-            if (valid) a.y[(uint64_t)m * a.ldy + n] = a.r[(uint64_t)m * a.ldr + n] + v;
-        }
-        else if constexpr (EPI == EPI_QKV)
-        {
-            if (valid)
+            const int tt = t < CNT ? t : 0;
+            const float v = red[0][tt] + red[1][tt] + red[2][tt] + red[3][tt];
+            const uint32_t m = m0 + tt / NW, n = n0 + tt % NW;
+            const bool valid = t < CNT && m < a.M && n < a.N;
+            if constexpr (EPI == EPI_STORE)
             {
-                if (n < a.d) a.q[(uint64_t)m * a.d + n] = v;
-                else
+                if (valid) a.y[(uint64_t)m * a.ldy + n] = v;
+            }
+            else if constexpr (EPI == EPI_GELU)
+            {
+                if (valid) a.y[(uint64_t)m * a.ldy + n] = gelu_exact(v);
+            }
+            else if constexpr (EPI == EPI_RESID)
+            {
+                if (valid) a.y[(uint64_t)m * a.ldy + n] = a.r[(uint64_t)m * a.ldr + n] + v;
+            }
+            else if constexpr (EPI == EPI_QKV)
+            {
+                if (valid)
                 {
-                    const uint32_t c = n % a.d, h = c / a.hd, e = c % a.hd;
-                    float* cache = n < 2 * a.d ? a.kc : a.vc;
-                    cache[(uint64_t)m * a.seq_stride + ((uint64_t)h * a.C + a.pos[m]) * a.hd + e] = v;
+                    if (n < a.d) a.q[(uint64_t)m * a.d + n] = v;
+                    else
+                    {
+                        const uint32_t c = n % a.d, h = c / a.hd, e = c % a.hd;
+                        float* cache = n < 2 * a.d ? a.kc : a.vc;
+                        cache[(uint64_t)m * a.seq_stride + ((uint64_t)h * a.C + a.pos[m]) * a.hd + e] = v;
+                    }
                 }
             }
-        }
-        else if constexpr (EPI == EPI_ARGMAX)
-        {
-            // logits (optional) and the per-row argmax over this CTA's 4
-            // columns, folded into the row's global key with one atomicMax.
-            if (valid && a.y) a.y[(uint64_t)m * a.ldy + n] = v;
-            if (t < 32 * ((CNT + 31) / 32))
+            else if constexpr (EPI == EPI_ARGMAX)
             {
-                unsigned long long key = valid ? argmax_key(v, n) : 0ull;
-                unsigned long long o1 = __shfl_xor_sync(FULL_MASK, key, 1);
-                key = o1 > key ? o1 : key;
-                unsigned long long o2 = __shfl_xor_sync(FULL_MASK, key, 2);
-                key = o2 > key ? o2 : key;
-                if (valid && (t % NW) == 0) atomicMax(a.keys + m, key);
+                // logits (optional) and the per-row argmax over these 4
+                // columns, folded into the row's global key with one atomicMax
+                if (valid && a.y) a.y[(uint64_t)m * a.ldy + n] = v;
+                if (t < 32 * ((CNT + 31) / 32))
+                {
+                    unsigned long long key = valid ? argmax_key(v, n) : 0ull;
+                    unsigned long long o1 = __shfl_xor_sync(FULL_MASK, key, 1);
+                    key = o1 > key ? o1 : key;
+                    unsigned long long o2 = __shfl_xor_sync(FULL_MASK, key, 2);
+                    key = o2 > key ? o2 : key;
+                    if (valid && (t % NW) == 0) atomicMax(a.keys + m, key);
+                }
             }
         }
     }
@@ -326,6 +364,7 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
 __global__ void finalize_kernel(unsigned long long* keys, uint32_t* pending, uint32_t* pos, uint32_t* next_out,
                                 uint32_t B, uint32_t set_pos)
 {
+    FML_TIMELINE_SCOPE(30);
     griddep_wait();
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
@@ -518,16 +557,50 @@ int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, boo
     return FML_OK;
 }
 
+// Resident CTAs per SM of a gemv instantiation (cached per instantiation).
+template <int MT, int EPI, bool LN>
+int gemv_blocks_per_sm()
+{
+    static int n = 0;
+    if (!n)
+    {
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, gemv_kernel<MT, EPI, LN>, 128, 0) != cudaSuccess || b < 1)
+            b = 1;
+        n = b;
+    }
+    return n;
+}
+
+template <int MT, int EPI, bool LN>
+int launch_gemv_mt(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
+{
+    const unsigned gx = (a.M + MT - 1) / MT;
+    const unsigned ngroups = (a.N + 3) / 4;
+    // one wave: every CTA resident at once, each walking several column groups
+    const unsigned slots = (unsigned)(gemv_blocks_per_sm<MT, EPI, LN>() * sms);
+    unsigned gy = slots / gx;
+    if (gy < 1) gy = 1;
+    if (gy > ngroups) gy = ngroups;
+    if (gy > 65535u) gy = 65535u;
+    return launch_k(gemv_kernel<MT, EPI, LN>, dim3(gx, gy), dim3(128), st, pdl, a);
+}
+
 template <int EPI, bool LN>
 int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
 {
     FML_REQUIRE(a.K % 4 == 0 && a.ldx % 4 == 0, "gemv: K and ldx must be multiples of 4");
     FML_REQUIRE(!LN || a.gamma, "gemv: LayerNorm prologue without gamma");
-    const unsigned gy = (a.N + 3) / 4;
-    FML_REQUIRE(gy <= 65535u, "gemv: N = %u too large", a.N);
-    if (a.M <= 4) return launch_k(gemv_kernel<4, EPI, LN>, dim3(1, gy), dim3(128), st, pdl, a);
-    if (a.M <= 8) return launch_k(gemv_kernel<8, EPI, LN>, dim3(1, gy), dim3(128), st, pdl, a);
-    return launch_k(gemv_kernel<16, EPI, LN>, dim3((a.M + 15) / 16, gy), dim3(128), st, pdl, a);
+    static int sms = 0;
+    if (!sms)
+    {
+        int dev = 0;
+        FML_CUDA_TRY(cudaGetDevice(&dev));
+        FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    }
+    if (a.M <= 4) return launch_gemv_mt<4, EPI, LN>(a, st, pdl, sms);
+    if (a.M <= 8) return launch_gemv_mt<8, EPI, LN>(a, st, pdl, sms);
+    return launch_gemv_mt<16, EPI, LN>(a, st, pdl, sms);
 }
 
 int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, const uint32_t* pos, uint32_t P,
