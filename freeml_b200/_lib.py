@@ -45,6 +45,11 @@ SIGNATURES = {
     "fml_device_check": (_I, [_P, _P, _P]),
     "fml_kernel_launch_count": (_U64, []),
     "fml_device_error_count": (_I, [_P]),
+    "fml_device_alloc": (_I, [ctypes.POINTER(_P), ctypes.c_size_t]),
+    "fml_device_free": (_I, [_P]),
+    "fml_memcpy_to_device": (_I, [_P, _P, ctypes.c_size_t]),
+    "fml_memcpy_to_host": (_I, [_P, _P, ctypes.c_size_t]),
+    "fml_synchronize": (_I, []),
     "fml_gather_rows": (_I, [_P, _P, _P, _U32, _U32, _U32, _P]),
     "fml_add": (_I, [_P, _P, _P, _U64, _P]),
     "fml_broadcast_add": (_I, [_P, _P, _P, _U64, _U32, _P]),

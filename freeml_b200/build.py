@@ -67,6 +67,43 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     return LIB
 
 
+DROPIN_SRC = os.path.join(HERE, "dropin", "nanollm_dropin.cpp")
+DROPIN_BIN = os.path.join(BUILD, "nanollm_dropin")
+
+
+def freeml_root() -> str | None:
+    """The FreeML source tree the drop-in example compiles against."""
+    for cand in (os.environ.get("FREEML_ROOT"), "/root/reference"):
+        if cand and os.path.exists(os.path.join(cand, "ModelLibrary", "Model.h")):
+            return cand
+    return None
+
+
+def build_dropin(verbose: bool = False) -> str | None:
+    """Compile the Model<float, MatrixCUDA<float>> example (needs the FreeML
+    headers; skipped when the tree is absent, e.g. on a machine that only
+    runs the prebuilt binary)."""
+    root = freeml_root()
+    if root is None:
+        return None
+    inc = os.path.join(ROOT, "include")
+    deps = [DROPIN_SRC, LIB] + glob.glob(os.path.join(inc, "freeml_b200", "*.h")) + [os.path.join(inc, "freeml_cuda.h")]
+    if _needs(DROPIN_BIN, deps):
+        os.makedirs(BUILD, exist_ok=True)
+        # -O3 -march=x86-64-v3: the flags the reference CPU build uses.  FreeML
+        # draws its weights through libstdc++'s normal_distribution, which is
+        # instantiated in this translation unit, and FMA contraction there
+        # changes the last bit of the draws -- same flags, same weights.
+        cmd = [os.environ.get("CXX", "g++"), "-std=c++20", "-O3", "-march=x86-64-v3", "-w",
+               "-I" + os.path.join(inc, "freeml_b200", "gcc_compat"), "-I" + root, "-I" + inc,
+               "-o", DROPIN_BIN, DROPIN_SRC, "-L" + HERE, "-lfreeml_cuda", "-Wl,-rpath,$ORIGIN/.."]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+    return DROPIN_BIN
+
+
 if __name__ == "__main__":
     build(verbose="-v" in sys.argv, ptxas_info="--ptxas" in sys.argv)
     print(LIB)
+    print(build_dropin(verbose="-v" in sys.argv))

@@ -232,6 +232,46 @@ int fml_device_check(int* sm_count, int* cc_major, int* cc_minor)
     return FML_OK;
 }
 
+int fml_device_alloc(void** ptr, size_t bytes)
+{
+    FML_REQUIRE(ptr, "fml_device_alloc: null argument");
+    *ptr = nullptr;
+    const cudaError_t e = cudaMalloc(ptr, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+    {
+        cudaGetLastError();
+        return set_error(FML_ERR_NOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    return FML_OK;
+}
+
+int fml_device_free(void* ptr)
+{
+    if (ptr) FML_CUDA_TRY(cudaFree(ptr));
+    return FML_OK;
+}
+
+int fml_memcpy_to_device(void* dst, const void* src, size_t bytes)
+{
+    FML_REQUIRE(bytes == 0 || (dst && src), "fml_memcpy_to_device: null pointer");
+    if (bytes) FML_CUDA_TRY(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+    return FML_OK;
+}
+
+int fml_memcpy_to_host(void* dst, const void* src, size_t bytes)
+{
+    FML_REQUIRE(bytes == 0 || (dst && src), "fml_memcpy_to_host: null pointer");
+    FML_CUDA_TRY(cudaDeviceSynchronize());
+    if (bytes) FML_CUDA_TRY(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    return FML_OK;
+}
+
+int fml_synchronize(void)
+{
+    FML_CUDA_TRY(cudaDeviceSynchronize());
+    return FML_OK;
+}
+
 int fml_gather_rows(float* out, const float* src, const float* idx, uint32_t rows, uint32_t width, uint32_t src_rows,
                     fml_stream_t stream)
 {

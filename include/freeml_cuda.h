@@ -70,6 +70,15 @@ FML_API int fml_device_error_count(uint64_t* count);
  * points, graph replays counted per kernel node). */
 FML_API uint64_t fml_kernel_launch_count(void);
 
+/* Device memory for host bindings (the MatrixCUDA<float> storage of
+ * include/freeml_b200/MatrixCUDA.h): allocation, release, and synchronous
+ * copies (the copy to the host waits for all prior work on the device). */
+FML_API int fml_device_alloc(void** ptr, size_t bytes);
+FML_API int fml_device_free(void* ptr);
+FML_API int fml_memcpy_to_device(void* dst, const void* src, size_t bytes);
+FML_API int fml_memcpy_to_host(void* dst, const void* src, size_t bytes);
+FML_API int fml_synchronize(void);
+
 /* ---------------------------------------------------------------------
  * 1. Operator entry points
  * ------------------------------------------------------------------- */
