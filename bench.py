@@ -43,6 +43,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-only", action="store_true", help="a few passes for ncu (no JSON)")
+    ap.add_argument("--profile-phase", choices=["decode", "prefill"], default="decode",
+                    help="with --profile-only: 3 decode steps at mid-decode, or one prefill")
     return ap.parse_args()
 
 
@@ -265,6 +267,16 @@ def main():
     for _ in range(max(args.warmup, 0)):
         one_pass()
     torch.cuda.synchronize()
+
+    if args.profile_only and args.profile_phase == "prefill":
+        # for ncu (--profile-from-start off): one more prefill of the same
+        # prompts (tensor-core contractions, 4096 rows) between Start/Stop
+        torch.cuda.cudart().cudaProfilerStart()
+        lm.prefill(prompts)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        lm.close()
+        return 0
 
     if args.profile_only:
         # for ncu (--profile-from-start off): bring every sequence to the

@@ -78,6 +78,7 @@ SIGNATURES = {
     "fml_lm_step": (_I, [_P, _P, _P, _P]),
     "fml_lm_step_host": (_I, [_P, _P, _P, _P]),
     "fml_lm_set_graph": (_I, [_P, _I]),
+    "fml_lm_set_prefill_math": (_I, [_P, _I]),
     "fml_lm_pending": (_I, [_P, _P, _P]),
     "fml_lm_get_position": (_I, [_P, _U32, ctypes.POINTER(_U32)]),
     "fml_lm_rewind": (_I, [_P, _U32, _P, _I, _P]),

@@ -328,9 +328,10 @@ extern "C" {
 int fml_device_error_count(uint64_t* count)
 {
     FML_REQUIRE(count, "fml_device_error_count: null argument");
-    int v = 0;
+    int v = 0, g = 0;
     FML_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_attention_timeouts, sizeof(int)));
-    *count = (uint64_t)v;
+    FML_RC(gemm_tc_error_count(&g));
+    *count = (uint64_t)v + (uint64_t)g;
     return FML_OK;
 }
 

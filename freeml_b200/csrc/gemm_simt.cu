@@ -141,6 +141,24 @@ int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int 
 
 static int g_math_mode = FML_MATH_FP32;
 
+int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
+            int epi, const float* R, cudaStream_t st);
+
+int math_mode() { return g_math_mode; }
+
+// Contraction with C = A . B^T: tensor cores (tcgen05) in the TF32 modes when
+// the operands meet TMA's alignment rules, else the fp32 CUDA-core kernel.
+int gemm_nt(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, int epi,
+            const float* R, cudaStream_t st)
+{
+    const bool tc_ok = g_math_mode != FML_MATH_FP32 && K > 0 && aligned16(A) && aligned16(B) && lda % 4 == 0 &&
+                       ldb % 4 == 0;
+    if (tc_ok) return gemm_tc(C, A, B, M, N, K, lda, ldb, ldc, g_math_mode == FML_MATH_TF32X3, epi, R, st);
+    FML_RC(gemm_f32(C, A, B, M, N, K, lda, ldb, ldc, true, 1, 0, 0, 0, st));
+    if (epi == 0 || M <= 0 || N <= 0) return FML_OK;
+    return set_error(FML_ERR_UNSUPPORTED, "gemm_nt: epilogue %d needs the tensor-core path", epi);
+}
+
 }  // namespace fml
 
 using namespace fml;
@@ -149,7 +167,8 @@ extern "C" {
 
 int fml_set_math_mode(int mode)
 {
-    FML_REQUIRE(mode == FML_MATH_FP32, "math mode %d is not available in this build", mode);
+    FML_REQUIRE(mode == FML_MATH_FP32 || mode == FML_MATH_TF32X3 || mode == FML_MATH_TF32, "unknown math mode %d",
+                mode);
     g_math_mode = mode;
     return FML_OK;
 }
@@ -161,8 +180,8 @@ int fml_matmul(float* out, const float* a, const float* b, uint32_t M, uint32_t 
 {
     FML_REQUIRE(M == 0 || N == 0 || (out && a && b), "fml_matmul: null pointer");
     FML_REQUIRE(M < (1u << 31) && N < (1u << 31) && K < (1u << 31), "fml_matmul: dimension too large");
-    return gemm_f32(out, a, b, (int)M, (int)N, (int)K, (int)K, trans_b ? (int)K : (int)N, (int)N, trans_b != 0, 1, 0,
-                    0, 0, as_stream(stream));
+    if (trans_b) return gemm_nt(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)K, (int)N, 0, nullptr, as_stream(stream));
+    return gemm_f32(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, false, 1, 0, 0, 0, as_stream(stream));
 }
 
 int fml_matmul_strided(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,

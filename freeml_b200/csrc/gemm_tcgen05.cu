@@ -1,0 +1,399 @@
+// Tensor-core contractions on sm_100a (tcgen05 + TMEM + TMA): the batched /
+// prefill Dense products Mul<None|Right> (MatrixBase_Mul.h:591-615) for the
+// large-M shapes.
+//
+//   C[M x N] (+ epilogue) = A[M x K] . B[N x K]^T        (both K-contiguous)
+//
+// One CTA per 128 x 128 output tile, K staged 32 fp32 (one 128-byte row) at a
+// time through a 3-stage ring of TMA tensor loads (128-byte swizzle, no
+// multicast).  The accumulator lives in TMEM (128 lanes x 128 fp32 columns).
+// Warp roles (6 warps):
+//   warp 0      TMEM allocation; one thread issues the TMA loads
+//   warp 1      one thread issues tcgen05.mma and tcgen05.commit
+//   warps 2..5  TF32x3 split of each staged tile, then the epilogue
+//               (tcgen05.ld of the accumulator rows, store to global)
+//
+// Precision: kind::tf32 reads only the top 19 bits of each fp32 operand.
+// TF32x3 (default) splits x = hi + lo with hi = x with the low 13 bits
+// cleared (written back in place) and lo = x - hi (exact in fp32), then sums
+// hi*hi + hi*lo + lo*hi in the fp32 accumulator -- fp32-level results at
+// three MMAs per k-step.  TF32 (one MMA, hardware truncation) is the fast,
+// looser mode.
+//
+// Every mbarrier wait is bounded; a wait that runs out sets the device error
+// count (fml_device_error_count), waits (bounded) for the MMAs in flight and
+// still frees the CTA's TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "fml_common.cuh"
+
+namespace fml {
+
+__device__ int g_gemm_timeouts;
+
+namespace tc {
+
+constexpr int BM = 128, BN = 128, BK = 32;  // BK fp32 = 128 bytes per row
+constexpr int STAGES = 3;
+constexpr uint32_t TILE_BYTES = BM * BK * 4;  // 16 KB (A or B tile)
+constexpr uint32_t TMEM_COLS = 128;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
+{
+    const uint32_t addr = smem_u32(bar);
+    for (uint32_t it = 0; it < (1u << 24); ++it)
+    {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// 2-D TMA tile load (x = k, y = row) completing on `bar`; x * 4 bytes is a
+// multiple of 128 (k0 is a multiple of BK).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// K-major, 128-byte-swizzled shared-memory operand descriptor: rows of 128
+// bytes, 8-row (1024-byte) swizzle atoms stacked with a 1024-byte stride.
+__device__ __forceinline__ uint64_t smem_desc(const void* tile, uint32_t byte_offset)
+{
+    const uint64_t start = (uint64_t)((smem_u32(tile) + byte_offset) >> 4) & 0x3FFFull;
+    const uint64_t lbo = 1ull;                 // unused by swizzled K-major layouts
+    const uint64_t sbo = 1024ull >> 4;         // next 8-row group
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) /* version 1 */ | (2ull << 61) /* SWIZZLE_128B */;
+}
+
+// kind::tf32 instruction descriptor: F32 accumulator, TF32 A and B, both
+// K-major, M = 128, N = 128.
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, bool accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(IDESC), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace tc
+
+enum TcEpi { TC_STORE = 0, TC_GELU = 1, TC_RESID = 2 };
+
+struct TcArgs
+{
+    int M, N, K;
+    float* C;         // [M x N], row stride ldc
+    int ldc;
+    const float* R;   // TC_RESID: C = R + A.B^T (row stride ldc)
+};
+
+// Shared memory: STAGES x {A, B, A_lo, B_lo} tiles (1024-byte aligned), then
+// barriers and the TMEM base address.
+template <bool SPLIT3, int EPI>
+__global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                              const __grid_constant__ CUtensorMap map_b, TcArgs args)
+{
+    using namespace tc;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // align the carve-out to 1024 bytes (the swizzle atom)
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int NT = SPLIT3 ? 4 : 2;  // tiles per stage
+    unsigned char* tiles = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(tiles + STAGES * NT * TILE_BYTES);
+    uint64_t* conv = full + STAGES;
+    uint64_t* empty = conv + STAGES;
+    uint64_t* done = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int kblocks = (args.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < STAGES; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&conv[s], 4);  // one arrival per converter warp
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem_base = *tmem_slot;
+    bool ok = true;
+
+    auto tile_ptr = [&](int stage, int which) { return tiles + (stage * NT + which) * TILE_BYTES; };
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            for (int kb = 0; kb < kblocks && ok; ++kb)
+            {
+                const int s = kb % STAGES;
+                if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { ok = false; break; }
+                mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+                tma_load_2d(tile_ptr(s, 0), &map_a, kb * BK, m0, &full[s]);
+                tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
+            }
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            for (int kb = 0; kb < kblocks && ok; ++kb)
+            {
+                const int s = kb % STAGES;
+                if (!mbar_wait(&conv[s], (kb / STAGES) & 1)) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k)  // K = 8 tf32 (32 bytes) per MMA
+                {
+                    const uint32_t off = k * 32;
+                    const uint64_t da = smem_desc(tile_ptr(s, 0), off);
+                    const uint64_t db = smem_desc(tile_ptr(s, 1), off);
+                    const bool acc = kb > 0 || k > 0;
+                    mma_tf32(tmem_base, da, db, acc);
+                    if constexpr (SPLIT3)
+                    {
+                        mma_tf32(tmem_base, da, smem_desc(tile_ptr(s, 3), off), true);   // hi * lo
+                        mma_tf32(tmem_base, smem_desc(tile_ptr(s, 2), off), db, true);   // lo * hi
+                    }
+                }
+                mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+            }
+            mma_commit(done);
+        }
+    }
+    else
+    {
+        // warps 2..5: split each staged tile, then the epilogue
+        const int ct = threadIdx.x - 64;  // 0..127
+        for (int kb = 0; kb < kblocks; ++kb)
+        {
+            const int s = kb % STAGES;
+            if (!__all_sync(FULL_MASK, mbar_wait(&full[s], (kb / STAGES) & 1))) { ok = false; break; }
+            if constexpr (SPLIT3)
+            {
+                for (int which = 0; which < 2; ++which)
+                {
+                    float4* hi = reinterpret_cast<float4*>(tile_ptr(s, which));
+                    float4* lo = reinterpret_cast<float4*>(tile_ptr(s, which + 2));
+                    for (int i = ct; i < (int)(TILE_BYTES / 16); i += 128)
+                    {
+                        const float4 x = hi[i];
+                        float4 h, l;
+                        h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u); l.x = x.x - h.x;
+                        h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u); l.y = x.y - h.y;
+                        h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u); l.z = x.z - h.z;
+                        h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u); l.w = x.w - h.w;
+                        hi[i] = h;
+                        lo[i] = l;
+                    }
+                }
+                // make these generic-proxy writes visible to the tensor core
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv[s]);
+        }
+        if (ok && !__all_sync(FULL_MASK, mbar_wait(done, 0))) ok = false;
+        if (ok)
+        {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int lg = warp & 3;  // this warp's TMEM lane quarter
+            const int row = m0 + lg * 32 + lane;
+            for (int c0 = 0; c0 < BN; c0 += 32)
+            {
+                float v[32];
+                tc::tmem_ld32(tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)c0, v);
+                if (row < args.M)
+                {
+                    float* crow = args.C + (uint64_t)row * args.ldc + n0 + c0;
+                    const float* rrow = EPI == TC_RESID ? args.R + (uint64_t)row * args.ldc + n0 + c0 : nullptr;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                    {
+                        if (n0 + c0 + j < args.N)
+                        {
+                            float x = v[j];
+                            if constexpr (EPI == TC_GELU) x = gelu_exact(x);
+                            if constexpr (EPI == TC_RESID) x += rrow[j];
+                            crow[j] = x;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    if (!ok && lane == 0) atomicAdd(&g_gemm_timeouts, 1);
+    // the MMAs must have finished with TMEM before it is freed: on an early
+    // exit give them a last bounded wait
+    if (!ok && warp == 1 && lane == 0) tc::mbar_wait(done, 0);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+    {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---- host side ---------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Row-major [rows x K] fp32 matrix as 32 x 128 boxes with 128-byte swizzle.
+static int make_map(CUtensorMap* map, const float* base, int rows, int K, int ld)
+{
+    auto enc = get_encode();
+    if (!enc) return set_error(FML_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
+    const cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)tc::BM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(FML_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return FML_OK;
+}
+
+template <bool SPLIT3, int EPI>
+static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& args, cudaStream_t st)
+{
+    constexpr int NT = SPLIT3 ? 4 : 2;
+    const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 16 * 8;
+    static bool attr = false;
+    if (!attr)
+    {
+        FML_CUDA_TRY(cudaFuncSetAttribute(gemm_tcgen05_kernel<SPLIT3, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+        attr = true;
+    }
+    dim3 grid((args.N + tc::BN - 1) / tc::BN, (args.M + tc::BM - 1) / tc::BM);
+    gemm_tcgen05_kernel<SPLIT3, EPI><<<grid, 192, smem, st>>>(ma, mb, args);
+    FML_LAUNCH_CHECK();
+    return FML_OK;
+}
+
+// C = A . B^T (+ epilogue) on the tensor cores.  A [M x K] (row stride lda),
+// B [N x K] (row stride ldb), both 16-byte aligned with lda, ldb multiples of
+// 4 (TMA's rules); split3 selects TF32x3.
+int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
+            int epi, const float* R, cudaStream_t st)
+{
+    if (M <= 0 || N <= 0) return FML_OK;
+    FML_REQUIRE(K > 0, "gemm_tc: K must be positive");
+    FML_REQUIRE(aligned16(A) && aligned16(B) && lda % 4 == 0 && ldb % 4 == 0,
+                "gemm_tc: operands must be 16-byte aligned with row strides that are multiples of 4");
+    CUtensorMap ma, mb;
+    FML_RC(make_map(&ma, A, M, K, lda));
+    FML_RC(make_map(&mb, B, N, K, ldb));
+    TcArgs args{M, N, K, C, ldc, R};
+    if (split3)
+    {
+        if (epi == TC_GELU) return launch_tc<true, TC_GELU>(ma, mb, args, st);
+        if (epi == TC_RESID) return launch_tc<true, TC_RESID>(ma, mb, args, st);
+        return launch_tc<true, TC_STORE>(ma, mb, args, st);
+    }
+    if (epi == TC_GELU) return launch_tc<false, TC_GELU>(ma, mb, args, st);
+    if (epi == TC_RESID) return launch_tc<false, TC_RESID>(ma, mb, args, st);
+    return launch_tc<false, TC_STORE>(ma, mb, args, st);
+}
+
+int gemm_tc_error_count(int* out)
+{
+    FML_CUDA_TRY(cudaMemcpyFromSymbol(out, g_gemm_timeouts, sizeof(int)));
+    return FML_OK;
+}
+
+}  // namespace fml

@@ -60,6 +60,8 @@ int launch_layernorm(float* out, const float* in, const float* gamma, const floa
                      uint32_t cols, uint64_t in_stride, uint64_t out_stride, float eps, cudaStream_t st);
 int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool trans_b,
              int batch, uint64_t pa, uint64_t pb, uint64_t pc, cudaStream_t st);
+int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
+            int epi, const float* R, cudaStream_t st);
 
 // ---------------------------------------------------------------- kernels --
 
@@ -456,6 +458,7 @@ struct fml_lm
     // graph / programmatic dependent launch
     bool use_graph = true;
     bool pdl = true;
+    int prefill_math = FML_MATH_TF32X3;  // prefill contractions on the tensor cores
     cudaGraphExec_t graph_exec = nullptr;
     cudaStream_t graph_stream = nullptr;
     uint32_t* graph_next = nullptr;
@@ -696,6 +699,23 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
     return FML_OK;
 }
 
+// Prefill contraction C = A . W^T (W [N x K] K-contiguous) with an epilogue:
+// 0 store, 1 GELU, 2 C = R + A . W^T.  Tensor cores (tcgen05, TF32x3 or
+// TF32) unless the engine is set to fp32 CUDA-core math or the rows are not
+// 16-byte multiples (a TMA row stride must be).
+int prefill_gemm(fml_lm* lm, float* C, const float* A, const float* W, int M, int N, int K, int epi, const float* R,
+                 cudaStream_t st)
+{
+    if (lm->prefill_math != FML_MATH_FP32 && K % 4 == 0)
+        return gemm_tc(C, A, W, M, N, K, K, K, N, lm->prefill_math == FML_MATH_TF32X3, epi, R, st);
+    FML_RC(gemm_f32(C, A, W, M, N, K, K, K, N, true, 1, 0, 0, 0, st));
+    const uint64_t n = (uint64_t)M * N;
+    if (epi == 1) gelu_inplace_kernel<<<grid_for(n, 256), 256, 0, st>>>(C, n);
+    else if (epi == 2) add_kernel<<<grid_for(n, 256), 256, 0, st>>>(C, R, C, n);
+    if (epi) FML_LAUNCH_CHECK();
+    return FML_OK;
+}
+
 uint32_t graph_nodes_per_step(const fml_lm_config& c) { return 1 + c.n_layer * 5 + 2; }
 
 }  // namespace
@@ -894,14 +914,12 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     embed_kernel<<<R < 65535u ? R : 65535u, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->prompt_dev, nullptr, R, P, d,
                                                           c.vocab, c.context, nullptr, 0u);
     FML_LAUNCH_CHECK();
-    const uint64_t n = (uint64_t)R * d;
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         float* kc = lm->kc + (uint64_t)l * lm->layer_stride;
         float* vc = lm->vc + (uint64_t)l * lm->layer_stride;
         FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
-        FML_RC(gemm_f32(lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * d), (int)d, (int)d, (int)d, (int)(3 * d), true,
-                        1, 0, 0, 0, st));
+        FML_RC(prefill_gemm(lm, lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * d), (int)d, 0, nullptr, st));
         qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * d, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, d, lm->hd,
                                                                               c.context, lm->seq_stride);
         FML_LAUNCH_CHECK();
@@ -912,19 +930,11 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
             FML_CUDA_TRY(cudaMemsetAsync(lm->grab + l, 0, sizeof(uint32_t), st));
             FML_RC(launch_attention(lm, l, r0, R - r0 < 65535u ? R - r0 : 65535u, nullptr, P, 1, c.context, st));
         }
-        FML_RC(gemm_f32(lm->tmp, lm->att, lm->wproj[l], (int)R, (int)d, (int)d, (int)d, (int)d, (int)d, true, 1, 0, 0,
-                        0, st));
-        add_kernel<<<grid_for(n, 256), 256, 0, st>>>(lm->buf, lm->x, lm->tmp, n);
-        FML_LAUNCH_CHECK();
+        // buf = x + att . Wproj^T ; hid = gelu(LN1(buf) . Wfc^T) ; x = buf + hid . Wmlp^T
+        FML_RC(prefill_gemm(lm, lm->buf, lm->att, lm->wproj[l], (int)R, (int)d, (int)d, 2, lm->x, st));
         FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
-        FML_RC(gemm_f32(lm->hid, lm->ln, lm->wfc[l], (int)R, (int)(4 * d), (int)d, (int)d, (int)d, (int)(4 * d), true, 1,
-                        0, 0, 0, st));
-        gelu_inplace_kernel<<<grid_for(n * 4, 256), 256, 0, st>>>(lm->hid, n * 4);
-        FML_LAUNCH_CHECK();
-        FML_RC(gemm_f32(lm->tmp, lm->hid, lm->wmlp[l], (int)R, (int)d, (int)(4 * d), (int)(4 * d), (int)(4 * d), (int)d,
-                        true, 1, 0, 0, 0, st));
-        add_kernel<<<grid_for(n, 256), 256, 0, st>>>(lm->x, lm->buf, lm->tmp, n);
-        FML_LAUNCH_CHECK();
+        FML_RC(prefill_gemm(lm, lm->hid, lm->ln, lm->wfc[l], (int)R, (int)(4 * d), (int)d, 1, nullptr, st));
+        FML_RC(prefill_gemm(lm, lm->x, lm->hid, lm->wmlp[l], (int)R, (int)d, (int)(4 * d), 2, lm->buf, st));
     }
     // last prompt row of each sequence -> ln_f -> lm_head argmax
     FML_RC(launch_layernorm(lm->ln, lm->x + (uint64_t)(P - 1) * d, lm->lnf, nullptr, nullptr, batch, d,
@@ -936,6 +946,15 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     finalize_kernel<<<(batch + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, nullptr, batch, P);
     FML_LAUNCH_CHECK();
     for (uint32_t b = 0; b < batch; ++b) lm->hpos[b] = P;
+    return FML_OK;
+}
+
+int fml_lm_set_prefill_math(fml_lm* lm, int mode)
+{
+    FML_REQUIRE(lm, "fml_lm_set_prefill_math: null engine");
+    FML_REQUIRE(mode == FML_MATH_FP32 || mode == FML_MATH_TF32X3 || mode == FML_MATH_TF32, "unknown math mode %d",
+                mode);
+    lm->prefill_math = mode;
     return FML_OK;
 }
 

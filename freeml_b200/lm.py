@@ -138,6 +138,10 @@ class NanoLM:
         call("fml_lm_pending", self._h, buf.data_ptr(), self._stream())
         return buf
 
+    def set_prefill_math(self, mode: int) -> None:
+        """FML_MATH_TF32X3 (default, tensor cores), FML_MATH_TF32 or FML_MATH_FP32."""
+        call("fml_lm_set_prefill_math", self._h, int(mode))
+
     def set_graph(self, on: bool) -> None:
         call("fml_lm_set_graph", self._h, int(on))
 

@@ -252,6 +252,10 @@ FML_API uint64_t fml_lm_param_count(const fml_lm_config* cfg);
 FML_API int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t prompt_len,
                    fml_stream_t stream);
 
+/* Precision of the prefill contractions (FML_MATH_*; default
+ * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy). */
+FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
+
 /* One decode step for every active sequence: consume each sequence's pending
  * token, append its K/V, and produce the next token (greedy).  Optional
  * outputs (device): next tokens [batch] and logits [batch x V] of the row

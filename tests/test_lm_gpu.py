@@ -157,3 +157,35 @@ def test_config3_teacher_forced(nseq_checked):
         upto = N if div == -1 else (-2 - div)
         got = logits[: upto - 1, b, :]
         np.testing.assert_allclose(got, ref[1:upto], rtol=RTOL, atol=ATOL)
+
+
+# TF32 (one pass, 10-bit mantissa operands) prefill: a looser stated bound.
+# The prompt rows' K/V and the first token come from the prefill, so its
+# rounding reaches every later logit through attention.
+ATOL_TF32 = RTOL_TF32 = 1e-2
+
+
+@pytest.mark.parametrize("mode", ["fp32", "tf32x3", "tf32"])
+def test_prefill_math_modes(golden, mode):
+    """Prefill contractions on CUDA cores (fp32), on tcgen05 at fp32-level
+    accuracy (TF32x3, the default) and on tcgen05 TF32: each against the
+    reference's greedy loop."""
+    from freeml_b200 import _lib
+    meta, g, _ = golden
+    m = meta["greedy"]["cfg1"]
+    s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
+    w = O.init_weights(s, m["wseed"])
+    lm = _lm(s, 1)
+    lm.bind(w)
+    lm.set_prefill_math({"fp32": _lib.FML_MATH_FP32, "tf32x3": _lib.FML_MATH_TF32X3,
+                         "tf32": _lib.FML_MATH_TF32}[mode])
+    toks, logits = lm.generate(g["cfg1_prompt"].reshape(1, -1), m["new"], want_logits=True)
+    lm.close()
+    ref_toks, ref_logits = g["cfg1_tokens"], g["cfg1_logits"]
+    tol = ATOL_TF32 if mode == "tf32" else ATOL
+    div = first_divergence(ref_logits, toks[0, m["plen"]:])
+    assert div == -1 or (mode == "tf32" and div < -1), f"first divergence at step {div}"
+    upto = m["new"] if div == -1 else (-2 - div)
+    np.testing.assert_allclose(logits[: upto - 1, 0, :], ref_logits[1:upto], rtol=tol, atol=tol)
+    if div == -1:
+        np.testing.assert_array_equal(toks[0], ref_toks)

@@ -4,6 +4,8 @@ the C oracle on seeded random shapes.
 
 fp32 bound: |gpu - ref| <= 1e-5 + 1e-5 |ref| for the elementwise/row ops
 (only reduction order differs), 1e-4 relative-to-scale for contractions."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -204,3 +206,52 @@ def test_attention_decode_rejects_small_workspace():
     with pytest.raises(FmlError):
         F.attention_decode(out, cu(q), cu(kc), cu(vc), torch.from_numpy(ln).cuda(), 0.125,
                            workspace=torch.empty(16, dtype=torch.uint8, device="cuda"))
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (130, 96, 260), (512, 1536, 512), (4096, 512, 2048), (7, 300, 64)])
+def test_matmul_tensor_core_tf32x3_vs_oracle(M, N, K):
+    """Mul<Right> on tcgen05 (TF32x3): fp32-level accuracy."""
+    from freeml_b200 import _lib
+    from freeml_b200 import matrix_ops as F
+    rs = np.random.RandomState(M + N + K)
+    A = rs.randn(M, K).astype(np.float32)
+    B = (0.02 * rs.randn(N, K)).astype(np.float32)
+    out = torch.empty(M, N, device="cuda")
+    _lib.call("fml_set_math_mode", _lib.FML_MATH_TF32X3)
+    try:
+        F.Mul(out, cu(A), cu(B), F.RIGHT)
+        got = host(out)
+    finally:
+        _lib.call("fml_set_math_mode", _lib.FML_MATH_FP32)
+    ref = O.op_mul(A, B, 1)
+    gemm_close(got, ref, A, B.T)
+    n = ctypes_u64()
+    _lib.call("fml_device_error_count", ctypes.byref(n))
+    assert n.value == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (130, 96, 260)])
+def test_matmul_tensor_core_tf32_vs_oracle(M, N, K):
+    """Mul<Right> on tcgen05, one TF32 product: within TF32 rounding
+    (2^-10 relative per product, bounded by 2e-3 of sum |a||b|)."""
+    from freeml_b200 import _lib
+    from freeml_b200 import matrix_ops as F
+    rs = np.random.RandomState(M * N + K)
+    A = rs.randn(M, K).astype(np.float32)
+    B = (0.02 * rs.randn(N, K)).astype(np.float32)
+    out = torch.empty(M, N, device="cuda")
+    _lib.call("fml_set_math_mode", _lib.FML_MATH_TF32)
+    try:
+        F.Mul(out, cu(A), cu(B), F.RIGHT)
+        got = host(out)
+    finally:
+        _lib.call("fml_set_math_mode", _lib.FML_MATH_FP32)
+    ref = O.op_mul(A, B, 1)
+    scale = np.abs(A).astype(np.float64) @ np.abs(B.T).astype(np.float64)
+    assert np.all(np.abs(got - ref) <= 2e-3 * scale + 1e-6)
+    assert np.abs(got - ref).max() > 0  # it really is the reduced-precision path
+
+
+def ctypes_u64():
+    import ctypes
+    return ctypes.c_uint64()
