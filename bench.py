@@ -143,11 +143,11 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic():
-    """dram bytes (read + write) per attention launch from the committed ncu
-    summary (profiles/attention_traffic.json), scaled to the bench's average
-    key length."""
-    p = os.path.join(ROOT, "profiles", "attention_traffic.json")
+def ncu_traffic(name):
+    """dram bytes (read + write) per launch of the dominant kernel, from the
+    committed ncu summary (profiles/<name>_traffic.json) taken at the bench's
+    average key length."""
+    p = os.path.join(ROOT, "profiles", f"{name}_traffic.json")
     try:
         with open(p) as f:
             return json.load(f)
@@ -348,16 +348,25 @@ def main():
     prof = lm.profile()
     lm.set_profiling(False)
     lm.set_graph(True)
-    att_ms, att_n = prof["attention"]
     d, L = s.d_model, s.n_layer
-    att_bytes = sum(4 * L * B * (2 * d * (p + 1) + 2 * d) for p in range(P, P + steps_per_pass))
     peak, peak_kind = hbm_peak()
-    achieved = att_bytes / (att_ms / 1e3) / 1e9 if att_ms > 0 else None
     step_bytes = sum(4 * (12 * d * d * L + s.vocab * d + (2 * L + 1) * d) + B * 4 * (2 * d * L * (p + 1) + 2 * d * L + 2 * d)
                      for p in range(P, P + steps_per_pass))
     pass_ms = ms_max / args.steps
-    traffic = ncu_traffic()
     total_prof_ms = sum(v[0] for v in prof.values())
+    fused = lm.fused_step_active()
+    if fused:
+        # the fused step is the only kernel: its algorithmic bytes are the step's
+        k_ms, k_n = prof["step"]
+        k_bytes = step_bytes
+        k_name = "decode_step_kernel (fused decode step: all layers, attention, lm_head, argmax)"
+        traffic = ncu_traffic("decode_step")
+    else:
+        k_ms, k_n = prof["attention"]
+        k_bytes = sum(4 * L * B * (2 * d * (p + 1) + 2 * d) for p in range(P, P + steps_per_pass))
+        k_name = "attention_kernel (split-KV decode attention)"
+        traffic = ncu_traffic("attention")
+    achieved = k_bytes / (k_ms / 1e3) / 1e9 if k_ms > 0 else None
 
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": pass_ms, "higher_is_better": True, "scaling": "strong",
@@ -366,13 +375,13 @@ def main():
             "config": workload_config(ws, B),
             "gpu_launches": int(launches),
             "clocks": clocks,
-            "roofline": {"bound": "hbm", "kernel": "attention_kernel (split-KV decode attention)",
+            "roofline": {"bound": "hbm", "kernel": k_name,
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
                          "traffic": (traffic or {}).get("bytes_per_launch_at_bench_avg"),
-                         "algorithmic_bytes_per_launch": att_bytes / max(att_n, 1),
-                         "avg_launch_us": att_ms / max(att_n, 1) * 1e3,
-                         "share_of_step_time": att_ms / total_prof_ms if total_prof_ms else None},
+                         "algorithmic_bytes_per_launch": k_bytes / max(k_n, 1),
+                         "avg_launch_us": k_ms / max(k_n, 1) * 1e3,
+                         "share_of_step_time": k_ms / total_prof_ms if total_prof_ms else None},
             "step_roofline": {"algorithmic_bytes_per_pass": step_bytes,
                               "achieved_GBps": step_bytes / (pass_ms / 1e3) / 1e9,
                               "frac": step_bytes / (pass_ms / 1e3) / 1e9 / peak},

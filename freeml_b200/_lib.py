@@ -17,8 +17,8 @@ STATUS_NAMES = {1: "FML_ERR_INVALID", 2: "FML_ERR_CUDA", 3: "FML_ERR_NOMEM", 4: 
                 5: "FML_ERR_STATE"}
 
 FML_MATH_FP32, FML_MATH_TF32X3, FML_MATH_TF32 = 0, 1, 2
-FML_LM_NCLASS = 9
-PROFILE_CLASSES = ["embed", "layernorm", "qkv", "attention", "proj", "fc", "mlp", "lm_head", "finalize"]
+FML_LM_NCLASS = 10
+PROFILE_CLASSES = ["embed", "layernorm", "qkv", "attention", "proj", "fc", "mlp", "lm_head", "finalize", "step"]
 
 
 class FmlError(RuntimeError):
@@ -79,6 +79,8 @@ SIGNATURES = {
     "fml_lm_step_host": (_I, [_P, _P, _P, _P]),
     "fml_lm_set_graph": (_I, [_P, _I]),
     "fml_lm_set_prefill_math": (_I, [_P, _I]),
+    "fml_lm_set_fused_step": (_I, [_P, _I]),
+    "fml_lm_get_fused_step": (_I, [_P, _P]),
     "fml_lm_pending": (_I, [_P, _P, _P]),
     "fml_lm_get_position": (_I, [_P, _U32, ctypes.POINTER(_U32)]),
     "fml_lm_rewind": (_I, [_P, _U32, _P, _I, _P]),

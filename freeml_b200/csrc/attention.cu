@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "decode_step.cuh"
 
 namespace fml {
 
@@ -328,10 +329,11 @@ extern "C" {
 int fml_device_error_count(uint64_t* count)
 {
     FML_REQUIRE(count, "fml_device_error_count: null argument");
-    int v = 0, g = 0;
+    int v = 0, g = 0, f = 0;
     FML_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_attention_timeouts, sizeof(int)));
     FML_RC(gemm_tc_error_count(&g));
-    *count = (uint64_t)v + (uint64_t)g;
+    FML_RC(decode_step_error_count(&f));
+    *count = (uint64_t)v + (uint64_t)g + (uint64_t)f;
     return FML_OK;
 }
 

@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "decode_step.cuh"
 #include "fml_common.cuh"
 
 #ifdef FML_TIMELINE
@@ -459,6 +460,16 @@ struct fml_lm
     bool use_graph = true;
     bool pdl = true;
     int prefill_math = FML_MATH_TF32X3;  // prefill contractions on the tensor cores
+
+    // fused decode step (one persistent kernel per step), opt-in: on config 3
+    // it measures slower than the per-operation kernels (437 vs 337 us/step)
+    bool fused = false;
+    bool step_ok = false;
+    uint32_t step_batch = 0;  // batch the plan was made for (0: none)
+    StepArgs sa{};
+    int step_grid = 0;
+    size_t step_smem = 0;
+    uint32_t* step_sync = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
     cudaStream_t graph_stream = nullptr;
     uint32_t* graph_next = nullptr;
@@ -488,7 +499,7 @@ void free_all(fml_lm* lm)
     for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
     void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
                     lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
-                    lm->counters, lm->prompt_dev, lm->grab};
+                    lm->counters, lm->prompt_dev, lm->grab, lm->step_sync};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (lm->host_io) cudaFreeHost(lm->host_io);
@@ -633,6 +644,40 @@ int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, c
     return FML_OK;
 }
 
+// Plan the fused step for the active batch (once per batch size).
+bool fused_step_ready(fml_lm* lm)
+{
+    if (!lm->fused) return false;
+    if (lm->step_batch == lm->batch) return lm->step_ok;
+    const fml_lm_config& c = lm->cfg;
+    StepArgs& a = lm->sa;
+    a = StepArgs{};
+    a.wbuf = lm->wbuf;
+    a.kc = lm->kc;
+    a.vc = lm->vc;
+    a.layer_stride = lm->layer_stride;
+    a.seq_stride = lm->seq_stride;
+    a.x = lm->x;
+    a.buf = lm->buf;
+    a.q = lm->q;
+    a.att = lm->att;
+    a.hid = lm->hid;
+    a.pending = lm->pending;
+    a.pos = lm->pos;
+    a.keys = lm->keys;
+    a.sync = lm->step_sync;
+    a.B = lm->batch;
+    a.V = c.vocab;
+    a.C = c.context;
+    a.d = c.d_model;
+    a.H = c.n_head;
+    a.hd = lm->hd;
+    a.L = c.n_layer;
+    lm->step_ok = decode_step_plan(a, lm->device, &lm->step_grid, &lm->step_smem) == FML_OK;
+    lm->step_batch = lm->batch;
+    return lm->step_ok;
+}
+
 // Enqueue one decode step for the active batch: embed, per layer
 // {qkv (LayerNorm fused) -> attention -> proj + residual -> fc (LayerNorm
 // fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
@@ -642,6 +687,14 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
     const fml_lm_config& c = lm->cfg;
     const uint32_t B = lm->batch, d = c.d_model;
     const bool pdl = lm->pdl && !lm->profiling;
+    if (fused_step_ready(lm))
+    {
+        ProfScope ps(lm, 9, st);
+        StepArgs a = lm->sa;
+        a.next_out = next_out;
+        a.logits = logits;
+        return launch_decode_step(a, lm->step_grid, lm->step_smem, st);
+    }
     {
         ProfScope ps(lm, 0, st);
         FML_RC(launch_k(embed_kernel, dim3(B), dim3(128), st, false, lm->x, (const float*)lm->tok,
@@ -716,7 +769,10 @@ int prefill_gemm(fml_lm* lm, float* C, const float* A, const float* W, int M, in
     return FML_OK;
 }
 
-uint32_t graph_nodes_per_step(const fml_lm_config& c) { return 1 + c.n_layer * 5 + 2; }
+uint32_t graph_nodes_per_step(fml_lm* lm)
+{
+    return fused_step_ready(lm) ? 1u : 1u + lm->cfg.n_layer * 5u + 2u;
+}
 
 }  // namespace
 
@@ -783,6 +839,7 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     if (!rc) rc = alloc((void**)&lm->part, B * H * lm->S * (hd + 2) * f);
     if (!rc) rc = alloc((void**)&lm->counters, B * H * 4);
     if (!rc) rc = alloc((void**)&lm->grab, L * 4);
+    if (!rc) rc = alloc((void**)&lm->step_sync, (uint64_t)decode_step_sync_words((uint32_t)L, 2u) * 4);
     if (!rc && cudaMallocHost((void**)&lm->host_io, 2 * B * 4) != cudaSuccess)
         rc = set_error(FML_ERR_NOMEM, "cudaMallocHost failed");
     if (rc)
@@ -796,6 +853,7 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     cudaMemset(lm->keys, 0, B * 8);
     cudaMemset(lm->counters, 0, B * H * 4);
     cudaMemset(lm->grab, 0, L * 4);
+    cudaMemset(lm->step_sync, 0, (uint64_t)decode_step_sync_words((uint32_t)L, 2u) * 4);
 
     // carve the weight buffer
     float* p = lm->wbuf;
@@ -911,6 +969,7 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     lm->batch = batch;
     FML_CUDA_TRY(cudaMemcpyAsync(lm->prompt_dev, prompts, (uint64_t)R * 4, cudaMemcpyDeviceToDevice, st));
     FML_CUDA_TRY(cudaMemsetAsync(lm->keys, 0, (uint64_t)c.max_batch * 8, st));
+    FML_CUDA_TRY(cudaMemsetAsync(lm->step_sync, 0, (uint64_t)decode_step_sync_words(c.n_layer, 2u) * 4, st));
     embed_kernel<<<R < 65535u ? R : 65535u, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->prompt_dev, nullptr, R, P, d,
                                                           c.vocab, c.context, nullptr, 0u);
     FML_LAUNCH_CHECK();
@@ -958,6 +1017,23 @@ int fml_lm_set_prefill_math(fml_lm* lm, int mode)
     return FML_OK;
 }
 
+int fml_lm_set_fused_step(fml_lm* lm, int on)
+{
+    FML_REQUIRE(lm, "fml_lm_set_fused_step: null engine");
+    lm->fused = on != 0;
+    lm->step_batch = 0;
+    if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
+    lm->graph_exec = nullptr;
+    return FML_OK;
+}
+
+int fml_lm_get_fused_step(fml_lm* lm, int* active)
+{
+    FML_REQUIRE(lm && active, "fml_lm_get_fused_step: null argument");
+    *active = lm->batch > 0 && fused_step_ready(lm) ? 1 : 0;
+    return FML_OK;
+}
+
 int fml_lm_set_graph(fml_lm* lm, int use_graph)
 {
     FML_REQUIRE(lm, "fml_lm_set_graph: null engine");
@@ -997,10 +1073,10 @@ int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t s
             lm->graph_logits = logits;
             lm->graph_batch = lm->batch;
             // capture counted the launches once; replays are counted below
-            launch_counter().fetch_sub(graph_nodes_per_step(lm->cfg), std::memory_order_relaxed);
+            launch_counter().fetch_sub(graph_nodes_per_step(lm), std::memory_order_relaxed);
         }
         FML_CUDA_TRY(cudaGraphLaunch(lm->graph_exec, st));
-        launch_counter().fetch_add(graph_nodes_per_step(lm->cfg), std::memory_order_relaxed);
+        launch_counter().fetch_add(graph_nodes_per_step(lm), std::memory_order_relaxed);
     }
     else
     {

@@ -138,6 +138,15 @@ class NanoLM:
         call("fml_lm_pending", self._h, buf.data_ptr(), self._stream())
         return buf
 
+    def set_fused_step(self, on: bool) -> None:
+        """Fused decode step (one persistent kernel per step) on or off."""
+        call("fml_lm_set_fused_step", self._h, int(bool(on)))
+
+    def fused_step_active(self) -> bool:
+        v = ctypes.c_int(0)
+        call("fml_lm_get_fused_step", self._h, ctypes.byref(v))
+        return bool(v.value)
+
     def set_prefill_math(self, mode: int) -> None:
         """FML_MATH_TF32X3 (default, tensor cores), FML_MATH_TF32 or FML_MATH_FP32."""
         call("fml_lm_set_prefill_math", self._h, int(mode))

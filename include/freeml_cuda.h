@@ -256,6 +256,14 @@ FML_API int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, 
  * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy). */
 FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
 
+/* Fused decode step (default off): one persistent kernel per step when the
+ * shape fits (batch <= 32, d_model a multiple of 32, head dim 32/64/128,
+ * 4*d_model <= 8192); otherwise, or when off, the per-operation kernels run.
+ * fml_lm_get_fused_step reports whether the fused kernel serves the
+ * current batch. */
+FML_API int fml_lm_set_fused_step(fml_lm* lm, int on);
+FML_API int fml_lm_get_fused_step(fml_lm* lm, int* active);
+
 /* One decode step for every active sequence: consume each sequence's pending
  * token, append its K/V, and produce the next token (greedy).  Optional
  * outputs (device): next tokens [batch] and logits [batch x V] of the row
@@ -292,8 +300,9 @@ FML_API uint64_t fml_lm_step_bytes(fml_lm* lm);
 /* Kernel timing: with profiling on (and graphs off), every step records CUDA
  * events around each kernel class and accumulates milliseconds and launch
  * counts per class: 0 embed, 1 layernorm, 2 qkv, 3 attention, 4 proj,
- * 5 fc, 6 mlp, 7 lm_head, 8 argmax/finalize.  Reset when turned on. */
-enum { FML_LM_NCLASS = 9 };
+ * 5 fc, 6 mlp, 7 lm_head, 8 argmax/finalize, 9 the fused step kernel (the
+ * only class a fused step records).  Reset when turned on. */
+enum { FML_LM_NCLASS = 10 };
 FML_API int fml_lm_set_profiling(fml_lm* lm, int on);
 FML_API int fml_lm_get_profile(fml_lm* lm, double* ms_by_class, uint64_t* launches_by_class, int n_classes);
 /* Algorithmic bytes of the attention kernels of one step (K/V rows read,

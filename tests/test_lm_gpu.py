@@ -23,10 +23,12 @@ ATOL = RTOL = 1e-3
 GAP = 2e-3
 
 
-def _lm(shape, batch):
+def _lm(shape, batch, fused=False):
     from freeml_b200.lm import NanoLLMShape, NanoLM
     s = NanoLLMShape(shape.V, shape.C, shape.d, shape.H, shape.L)
-    return NanoLM(s, batch)
+    lm = NanoLM(s, batch)
+    lm.set_fused_step(fused)
+    return lm
 
 
 def first_divergence(ref_logits, gpu_tokens_next):
@@ -42,16 +44,20 @@ def first_divergence(ref_logits, gpu_tokens_next):
     return -1
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused_step", "per_op"])
 @pytest.mark.parametrize("name", ["cfg1", "odd"])
-def test_greedy_matches_reference_loop(golden, name):
+def test_greedy_matches_reference_loop(golden, name, fused):
+    """Fused step kernel and per-operation kernels, each against the
+    reference's greedy loop."""
     meta, g, _ = golden
     m = meta["greedy"][name]
     s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
     w = O.init_weights(s, m["wseed"])
-    lm = _lm(s, 1)
+    lm = _lm(s, 1, fused)
     lm.bind(w)
     prompt = g[f"{name}_prompt"].reshape(1, -1)
     toks, logits = lm.generate(prompt, m["new"], want_logits=True)
+    assert lm.fused_step_active() == fused
     ref_toks, ref_logits = g[f"{name}_tokens"], g[f"{name}_logits"]
     # logits[k] is generated row plen + k (the rows after the prefill's)
     np.testing.assert_allclose(logits[:, 0, :], ref_logits[1:], rtol=RTOL, atol=ATOL)
@@ -125,6 +131,12 @@ def test_batched_sequences_are_independent(golden):
     lm.bind(w)
     batched, _ = lm.generate(prompts, 24)
     lm.close()
+    fused = _lm(s, 4, fused=True)
+    fused.bind(w)
+    fused_toks, _ = fused.generate(prompts, 24)
+    assert fused.fused_step_active()
+    fused.close()
+    np.testing.assert_array_equal(batched, fused_toks)
     for b in range(4):
         lm1 = _lm(s, 1)
         lm1.bind(w)
@@ -133,8 +145,8 @@ def test_batched_sequences_are_independent(golden):
         np.testing.assert_array_equal(batched[b], single[0])
 
 
-@pytest.mark.parametrize("nseq_checked", [4])
-def test_config3_teacher_forced(nseq_checked):
+@pytest.mark.parametrize("fused,nseq_checked", [(False, 4), (True, 2)], ids=["per_op", "fused_step"])
+def test_config3_teacher_forced(fused, nseq_checked):
     """V4096 C512 d512 H8 L8, 32 sequences, 128-token
     prompts (seed 4), 384 greedy tokens.  The engine decodes all 32; the
     oracle checks `nseq_checked` of them (every generated row) teacher-forced."""
@@ -144,9 +156,10 @@ def test_config3_teacher_forced(nseq_checked):
     s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
     w = O.init_weights(s, c["wseed"])
     prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])
-    lm = _lm(s, c["batch"])
+    lm = _lm(s, c["batch"], fused)
     lm.bind(w)
     toks, logits = lm.generate(prompts, c["new"], want_logits=True)
+    assert lm.fused_step_active() == fused
     lm.close()
     P, N = c["prompt"], c["new"]
     assert toks.shape == (c["batch"], P + N)
