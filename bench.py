@@ -236,18 +236,20 @@ def main():
 
     from freeml_b200 import _lib
     from freeml_b200.lm import CONFIGS, NanoLM, prompt_tokens, random_params
+    from freeml_b200.shard import max_over_ranks, shard_bounds
 
     torch.cuda.set_device(local)
     c = CONFIGS[CONFIG]
     s = c["shape"]
     B_total, P, NEW = c["batch"], c["prompt"], c["new"]
     if B_total % ws:
-        raise SystemExit(f"{B_total} sequences do not shard over {ws} GPUs")
-    B = B_total // ws
+        raise SystemExit(f"{B_total} sequences do not shard evenly over {ws} GPUs")
+    b_lo, b_hi = shard_bounds(B_total, ws, rank)
+    B = b_hi - b_lo
     steps_per_pass = NEW - 1
 
     params = random_params(s, c["wseed"], local)
-    prompts = prompt_tokens(c["pseed"], s.vocab, B_total, P)[rank * B:(rank + 1) * B]
+    prompts = prompt_tokens(c["pseed"], s.vocab, B_total, P)[b_lo:b_hi]
     lm = NanoLM(s, B, device=local)
     lm.bind(params)
     del params
@@ -311,11 +313,7 @@ def main():
     barrier()
     clocks = sampler.stop()
     launches = _lib.launch_count() - launches0
-    ms = ev0.elapsed_time(ev1)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if pg is not None:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), pg, "cuda")
     tokens = ws * B * steps_per_pass * args.steps
     value = tokens / (ms_max / 1e3)
 
@@ -334,11 +332,8 @@ def main():
             lm.step_host(tok_in, tok_out)
             tok_in, tok_out = tok_out, tok_in
     torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if pg is not None:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    e2e_value = ws * B * steps_per_pass * e2e_passes / float(t.item())
+    e2e_s = max_over_ranks(time.perf_counter() - t0, pg, "cuda")
+    e2e_value = ws * B * steps_per_pass * e2e_passes / e2e_s
 
     # ---- roofline of the dominant kernel (attention), from a profiled pass ----
     lm.set_graph(False)
@@ -372,7 +367,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": pass_ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded N(0,0.02) weights of the config-3 architecture, seeded uniform prompts",
-            "config": workload_config(ws, B),
+            "config": dict(workload_config(ws, B),
+                           engine="fused step kernel" if fused else "per-operation kernels (CUDA graph, PDL)"),
             "gpu_launches": int(launches),
             "clocks": clocks,
             "roofline": {"bound": "hbm", "kernel": k_name,

@@ -165,7 +165,7 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
-// Global -> shared bulk copy (no multicast), completing on `bar`.
+// Global -> shared bulk copy into this CTA only, completing on `bar`.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

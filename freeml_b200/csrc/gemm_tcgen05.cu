@@ -5,8 +5,8 @@
 //   C[M x N] (+ epilogue) = A[M x K] . B[N x K]^T        (both K-contiguous)
 //
 // One CTA per 128 x 128 output tile, K staged 32 fp32 (one 128-byte row) at a
-// time through a 3-stage ring of TMA tensor loads (128-byte swizzle, no
-// multicast).  The accumulator lives in TMEM (128 lanes x 128 fp32 columns).
+// time through a 3-stage ring of TMA tensor loads (128-byte swizzle, each
+// load into this CTA only).  The accumulator lives in TMEM (128 lanes x 128 fp32 columns).
 // Warp roles (6 warps):
 //   warp 0      TMEM allocation; one thread issues the TMA loads
 //   warp 1      one thread issues tcgen05.mma and tcgen05.commit
