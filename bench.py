@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[3, 4, 5], default=3,
+                    help="BASELINE config (3 is the headline metric's; 4 and 5 add a timed prefill)")
     ap.add_argument("--profile-only", action="store_true", help="a few passes for ncu (no JSON)")
     ap.add_argument("--profile-phase", choices=["decode", "prefill"], default="decode",
                     help="with --profile-only: 3 decode steps at mid-decode, or one prefill")
@@ -59,11 +61,12 @@ def workload_config(n_gpus, b_local):
     from freeml_b200.lm import CONFIGS
     c = CONFIGS[CONFIG]
     s = c["shape"]
-    return {"workload": "BASELINE config 3: NanoLLM V4096 C512 d512 H8 L8, 32 sequences, prompt 128, greedy decode 384",
+    return {"workload": f"BASELINE config {CONFIG}: NanoLLM V{s.vocab} C{s.context} d{s.d_model} H{s.n_head} "
+                        f"L{s.n_layer}, {c['batch']} sequences, prompt {c['prompt']}, greedy decode {c['new']}",
             "vocab": s.vocab, "context": s.context, "d_model": s.d_model, "n_head": s.n_head, "n_layer": s.n_layer,
             "sequences": c["batch"], "sequences_per_gpu": b_local, "prompt": c["prompt"], "decode_tokens": c["new"],
-            "step": "one greedy decode pass (383 engine steps) of every sequence",
-            "l2": "per engine step the working set (weights 109 MB + K/V rows ~330 MB) exceeds the 126 MB L2",
+            "step": f"one greedy decode pass ({c['new'] - 1} engine steps) of every sequence",
+            "l2": "per engine step the working set (all weights + the K/V rows read) exceeds the 126 MB L2",
             "parallelism": f"dp{n_gpus} (sequence sharding, no collective)"}
 
 
@@ -143,6 +146,15 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def ncu_traffic(name):
     """dram bytes (read + write) per launch of the dominant kernel, from the
     committed ncu summary (profiles/<name>_traffic.json) taken at the bench's
@@ -212,7 +224,9 @@ def run_reference(args, ws, rank):
 # ------------------------------------------------------------------ ours --
 
 def main():
+    global CONFIG
     args = parse()
+    CONFIG = args.config
     ws, rank, local = dist_env()
     pg = None
     if ws > 1:
@@ -269,6 +283,17 @@ def main():
     for _ in range(max(args.warmup, 0)):
         one_pass()
     torch.cuda.synchronize()
+
+    # ---- one timed prefill of this rank's prompts (tensor-core contractions);
+    # it leaves the same KV rows and first tokens behind ----
+    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pe0.record()
+    lm.prefill(prompts)
+    pe1.record()
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(pe0.elapsed_time(pe1), pg, "cuda")
+    dm, Lm = s.d_model, s.n_layer
+    prefill_flop = ws * (Lm * (24 * B * P * dm * dm + 2 * B * P * P * dm) + 2 * B * s.vocab * dm)
 
     if args.profile_only and args.profile_phase == "prefill":
         # for ncu (--profile-from-start off): one more prefill of the same
@@ -355,18 +380,18 @@ def main():
         k_ms, k_n = prof["step"]
         k_bytes = step_bytes
         k_name = "decode_step_kernel (fused decode step: all layers, attention, lm_head, argmax)"
-        traffic = ncu_traffic("decode_step")
+        traffic = ncu_traffic("decode_step") if CONFIG == 3 else None
     else:
         k_ms, k_n = prof["attention"]
         k_bytes = sum(4 * L * B * (2 * d * (p + 1) + 2 * d) for p in range(P, P + steps_per_pass))
         k_name = "attention_kernel (split-KV decode attention)"
-        traffic = ncu_traffic("attention")
+        traffic = ncu_traffic("attention") if CONFIG == 3 else None
     achieved = k_bytes / (k_ms / 1e3) / 1e9 if k_ms > 0 else None
 
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": pass_ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic: seeded N(0,0.02) weights of the config-3 architecture, seeded uniform prompts",
+            "data": f"synthetic: seeded N(0,0.02) weights of the config-{CONFIG} architecture, seeded uniform prompts",
             "config": dict(workload_config(ws, B),
                            engine="fused step kernel" if fused else "per-operation kernels (CUDA graph, PDL)"),
             "gpu_launches": int(launches),
@@ -382,11 +407,17 @@ def main():
                               "achieved_GBps": step_bytes / (pass_ms / 1e3) / 1e9,
                               "frac": step_bytes / (pass_ms / 1e3) / 1e9 / peak},
             "kernel_ms_per_pass": {k: v[0] for k, v in prof.items()},
+            "prefill": {"ms": prefill_ms, "tokens_per_s": ws * B * P / (prefill_ms / 1e3),
+                        "algorithmic_tflop": prefill_flop / 1e12,
+                        "tflops": prefill_flop / (prefill_ms / 1e3) / 1e12,
+                        "math": "TF32x3 on tcgen05 (three kind::tf32 MMAs per product, fp32 accumulate in TMEM)",
+                        "frac_of_tf32x3_peak": prefill_flop / (prefill_ms / 1e3) / 1e12 / (tensor_peak() / 2 / 3),
+                        "peak_note": "tf32 dense = half the measured bf16 peak, / 3 for the three-pass split"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * B * ws * steps_per_pass,
                     "d2h_bytes_per_step": 4 * B * ws * steps_per_pass,
                     "path": "fml_lm_step_host (host token buffers, H2D + D2H + sync every engine step)"}}
 
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and CONFIG == 3:
         try:
             r = cpu_reference_time(2, 1)
             line["cpu_baseline"] = {"value": 1.0 / r["seconds_per_forward"], "unit": UNIT, "cores": r["threads"],

@@ -113,20 +113,22 @@ class NanoLM:
         assert tokens_in.dtype == np.uint32 and tokens_out.dtype == np.uint32
         call("fml_lm_step_host", self._h, tokens_in.ctypes.data, tokens_out.ctypes.data, self._stream())
 
-    def generate(self, prompts: np.ndarray, n_new: int, want_logits: bool = False):
+    def generate(self, prompts: np.ndarray, n_new: int, want_logits: bool = False, logit_rows=None):
         """Greedy decode: returns tokens [B, P + n_new] (uint32) and, if asked,
-        the logits of every generated position [n_new, B, V] (the prefill's
-        last-row logits are not returned; step k's logits are row P + k)."""
+        the logits of every generated position [n_new - 1, B, V] (the prefill's
+        last-row logits are not returned; step k's logits are row P + k).
+        `logit_rows` keeps only those sequences' logits ([n_new - 1, len, V])."""
         B, P = prompts.shape
         self.prefill(prompts)
         toks = [torch.from_numpy(np.ascontiguousarray(prompts, np.uint32).view(np.int32)).cuda(self.device)]
         pending = self.pending_tokens()
         outs, logits = [pending.clone().view(B, 1)], []
+        sel = None if logit_rows is None else torch.as_tensor(list(logit_rows), device=pending.device)
         for k in range(n_new - 1):
             nxt, lg = self.step(want_logits)
             outs.append(nxt.clone().view(B, 1))
             if want_logits:
-                logits.append(lg.clone())
+                logits.append(lg.clone() if sel is None else lg.index_select(0, sel))
         torch.cuda.synchronize()
         seq = torch.cat(toks + outs, dim=1).cpu().numpy().view(np.uint32)
         return seq, (torch.stack(logits).cpu().numpy() if want_logits else None)

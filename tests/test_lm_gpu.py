@@ -145,25 +145,27 @@ def test_batched_sequences_are_independent(golden):
         np.testing.assert_array_equal(batched[b], single[0])
 
 
-@pytest.mark.parametrize("fused,nseq_checked", [(False, 4), (True, 2)], ids=["per_op", "fused_step"])
-def test_config3_teacher_forced(fused, nseq_checked):
+@pytest.mark.parametrize("fused,nseq_checked,batch", [(False, 4, 32), (True, 2, 32), (False, 2, 8)],
+                         ids=["per_op", "fused_step", "per_op_8seq"])
+def test_config3_teacher_forced(fused, nseq_checked, batch):
     """V4096 C512 d512 H8 L8, 32 sequences, 128-token
-    prompts (seed 4), 384 greedy tokens.  The engine decodes all 32; the
-    oracle checks `nseq_checked` of them (every generated row) teacher-forced."""
+    prompts (seed 4), 384 greedy tokens.  The engine decodes all 32 (or the
+    first 8: the 8-row GEMV variants, as on each of 4 GPUs); the oracle checks
+    `nseq_checked` of them (every generated row) teacher-forced."""
     from freeml_b200.lm import CONFIGS, prompt_tokens
     c = CONFIGS[3]
     sh = c["shape"]
     s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
     w = O.init_weights(s, c["wseed"])
-    prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])
-    lm = _lm(s, c["batch"], fused)
+    prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])[:batch]
+    lm = _lm(s, batch, fused)
     lm.bind(w)
     toks, logits = lm.generate(prompts, c["new"], want_logits=True)
     assert lm.fused_step_active() == fused
     lm.close()
     P, N = c["prompt"], c["new"]
-    assert toks.shape == (c["batch"], P + N)
-    for b in np.linspace(0, c["batch"] - 1, nseq_checked).astype(int):
+    assert toks.shape == (batch, P + N)
+    for b in np.linspace(0, batch - 1, nseq_checked).astype(int):
         ref = O.forward(s, w, toks[b, : P + N - 1], row0=P - 1, nrows=N)  # rows P-1 .. P+N-2
         div = first_divergence(ref, toks[b, P:])
         assert div == -1 or div < -1, f"sequence {b}: first divergence at step {div}"
@@ -202,3 +204,30 @@ def test_prefill_math_modes(golden, mode):
     np.testing.assert_allclose(logits[: upto - 1, 0, :], ref_logits[1:upto], rtol=tol, atol=tol)
     if div == -1:
         np.testing.assert_array_equal(toks[0], ref_toks)
+
+
+def test_config4_prefill_heavy_teacher_forced():
+    """V32000 C2048 d1024 H16 L12, 64 sequences of 1536
+    prompt tokens (seed 6) prefilled on the tensor cores (TF32x3), then 64
+    greedy tokens.  Two sequences (first and last) are checked teacher-forced
+    against the oracle's forward over their GPU token streams."""
+    from freeml_b200.lm import CONFIGS, prompt_tokens
+    c = CONFIGS[4]
+    sh = c["shape"]
+    s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
+    w = O.init_weights(s, c["wseed"])
+    prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])
+    checked = [0, c["batch"] - 1]
+    lm = _lm(s, c["batch"])
+    lm.bind(w)
+    toks, logits = lm.generate(prompts, c["new"], want_logits=True, logit_rows=checked)
+    lm.close()
+    P, N = c["prompt"], c["new"]
+    assert toks.shape == (c["batch"], P + N)
+    np.testing.assert_array_equal(toks[:, :P], prompts)
+    for k, b in enumerate(checked):
+        ref = O.forward(s, w, toks[b, : P + N - 1], row0=P - 1, nrows=N)
+        div = first_divergence(ref, toks[b, P:])
+        assert div == -1 or div < -1, f"sequence {b}: first divergence at step {div}"
+        upto = N if div == -1 else (-2 - div)
+        np.testing.assert_allclose(logits[: upto - 1, k, :], ref[1:upto], rtol=RTOL, atol=ATOL)
