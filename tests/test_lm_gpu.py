@@ -231,3 +231,39 @@ def test_config4_prefill_heavy_teacher_forced():
         assert div == -1 or div < -1, f"sequence {b}: first divergence at step {div}"
         upto = N if div == -1 else (-2 - div)
         np.testing.assert_allclose(logits[: upto - 1, k, :], ref[1:upto], rtol=RTOL, atol=ATOL)
+
+
+def test_config5_teacher_forced_vs_torch_fp32():
+    """BASELINE config 5 on one GPU: V32000 C4096 d4096 H32 L32 (6.6e9 fp32
+    parameters, seeded N(0, 0.02) on the device), 8 sequences of 1024 prompt
+    tokens (seed 8), 8 greedy tokens.  The C oracle cannot run this size, so
+    two sequences are checked teacher-forced against the PyTorch fp32
+    restatement (pinned to the reference's golden logits on CPU), with TF32
+    off in the check."""
+    import torch
+
+    from freeml_b200.lm import CONFIGS, NanoLM, prompt_tokens, random_params
+    from tests import torch_ref
+    c = CONFIGS[5]
+    sh = c["shape"]
+    params = random_params(sh, c["wseed"], 0)
+    P, N, B = c["prompt"], 8, c["batch"]
+    prompts = prompt_tokens(c["pseed"], sh.vocab, B, P)
+    checked = [0, B - 1]
+    lm = NanoLM(sh, B)
+    lm.bind(params)
+    toks, logits = lm.generate(prompts, N, want_logits=True, logit_rows=checked)
+    lm.close()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for k, b in enumerate(checked):
+            with torch.no_grad():
+                ref = torch_ref.forward(params, sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer,
+                                        toks[b, : P + N - 1].astype(np.int64), P - 1, N).cpu().numpy()
+            div = first_divergence(ref, toks[b, P:])
+            assert div == -1 or div < -1, f"sequence {b}: first divergence at step {div}"
+            upto = N if div == -1 else (-2 - div)
+            np.testing.assert_allclose(logits[: upto - 1, k, :], ref[1:upto], rtol=RTOL, atol=ATOL)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
