@@ -42,8 +42,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[3, 4, 5], default=3,
-                    help="BASELINE config (3 is the headline metric's; 4 and 5 add a timed prefill)")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=3,
+                    help="BASELINE config (3 is the headline metric's; 4 and 5 add a timed prefill; 2 is the "
+                         "per-operator microbench through the C ABI)")
     ap.add_argument("--profile-only", action="store_true", help="a few passes for ncu (no JSON)")
     ap.add_argument("--profile-phase", choices=["decode", "prefill"], default="decode",
                     help="with --profile-only: 3 decode steps at mid-decode, or one prefill")
@@ -221,6 +222,93 @@ def run_reference(args, ws, rank):
     return 0
 
 
+# ------------------------------------------------------------ config 2 --
+
+def run_microbench(args, rank):
+    """single operators through the C ABI (the calls the
+    MatrixCUDA drop-in makes), seed 2, inputs N(0,1), weights N(0,0.02).
+    Each call is timed alone with CUDA events, L2 flushed (a 256 MB write)
+    before every timed call; median of the timed calls."""
+    import torch
+
+    from freeml_b200 import _lib
+    from freeml_b200 import matrix_ops as ops
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    dev = torch.device("cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+    peak, peak_kind = hbm_peak()
+    reps = max(args.steps, 5)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    def randn(*shape, std=1.0):
+        return torch.randn(*shape, generator=g, device=dev) * std
+
+    rows = []
+    launches0 = _lib.launch_count()
+    for (fin, fout) in [(512, 512), (1024, 4096), (4096, 1024), (4096, 4096)]:
+        for batch in (1, 8, 64):
+            x, w = randn(batch, fin), randn(fin, fout, std=0.02)
+            y = torch.empty(batch, fout, device=dev)
+            ms = timed(lambda: ops.Mul(y, x, w))
+            nbytes = 4 * (fin * fout + batch * (fin + fout))
+            rows.append({"op": "Dense y = x.W (Mul<None>)", "in": fin, "out": fout, "batch": batch, "us": ms * 1e3,
+                         "bytes": nbytes, "GBps": nbytes / ms / 1e6, "frac_hbm": nbytes / ms / 1e6 / peak,
+                         "gflops": 2 * batch * fin * fout / ms / 1e6})
+    for width in (512, 4096):
+        nrows = 4096
+        x, gm = randn(nrows, width), torch.ones(width, device=dev)
+        y = torch.empty_like(x)
+        ms = timed(lambda: ops.LayerNormOp(y, x, gm))
+        nbytes = 8 * nrows * width
+        rows.append({"op": "LayerNormOp", "rows": nrows, "width": width, "us": ms * 1e3, "bytes": nbytes,
+                     "GBps": nbytes / ms / 1e6, "frac_hbm": nbytes / ms / 1e6 / peak})
+    x = randn(1 << 20)
+    y = torch.empty_like(x)
+    ms = timed(lambda: ops.GeluMat(y, x))
+    rows.append({"op": "GeluMat", "elements": 1 << 20, "us": ms * 1e3, "bytes": 8 << 20,
+                 "GBps": (8 << 20) / ms / 1e6, "frac_hbm": (8 << 20) / ms / 1e6 / peak})
+    H, hd = 8, 64
+    for kv in (128, 512, 2048):
+        q = randn(1, H * hd)
+        kc, vc = randn(1, H, kv, hd), randn(1, H, kv, hd)
+        lens = torch.full((1,), kv, dtype=torch.int32, device=dev)
+        out = torch.empty(1, H * hd, device=dev)
+        ws_bytes = ops.attention_decode_workspace_bytes(1, H, hd, kv)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+        ms = timed(lambda: ops.attention_decode(out, q, kc, vc, lens, 1.0 / hd ** 0.5, ws))
+        nbytes = 4 * (2 * kv * H * hd + 2 * H * hd)
+        rows.append({"op": "attention decode step (1 query, causal, split-KV)", "heads": H, "head_dim": hd,
+                     "kv_len": kv, "us": ms * 1e3, "bytes": nbytes, "GBps": nbytes / ms / 1e6,
+                     "frac_hbm": nbytes / ms / 1e6 / peak})
+    launches = _lib.launch_count() - launches0
+    line = {"metric": "per-operator time and HBM fraction (BASELINE config 2)", "value": None, "unit": "us",
+            "n_gpus": 1, "steps": reps, "warmup": max(args.warmup, 3), "ms_per_step": None,
+            "higher_is_better": False, "scaling": "replicas only", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: seed 2, inputs N(0,1), weights N(0,0.02)",
+            "config": {"workload": "BASELINE config 2 per-op microbench", "l2": "flushed before every timed call",
+                       "ln_rows": 4096},
+            "gpu_launches": int(launches), "peak_hbm_gbs": peak, "peak_source": peak_kind, "ops": rows}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------ ours --
 
 def main():
@@ -241,6 +329,11 @@ def main():
         pg = dist
     if args.impl == "reference":
         rc = run_reference(args, ws, rank)
+        if pg is not None:
+            pg.destroy_process_group()
+        return rc
+    if CONFIG == 2:
+        rc = run_microbench(args, rank)
         if pg is not None:
             pg.destroy_process_group()
         return rc
