@@ -143,6 +143,10 @@ static int g_math_mode = FML_MATH_FP32;
 
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
             int epi, const float* R, cudaStream_t st);
+int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
+bool skinny_nn_ok(const float* C, const float* A, const float* B, int M, int N, int K, int ldb, int ldc);
+int skinny_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc,
+              cudaStream_t st);
 
 int math_mode() { return g_math_mode; }
 
@@ -180,8 +184,17 @@ int fml_matmul(float* out, const float* a, const float* b, uint32_t M, uint32_t 
 {
     FML_REQUIRE(M == 0 || N == 0 || (out && a && b), "fml_matmul: null pointer");
     FML_REQUIRE(M < (1u << 31) && N < (1u << 31) && K < (1u << 31), "fml_matmul: dimension too large");
-    if (trans_b) return gemm_nt(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)K, (int)N, 0, nullptr, as_stream(stream));
-    return gemm_f32(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, false, 1, 0, 0, 0, as_stream(stream));
+    cudaStream_t st = as_stream(stream);
+    // at most 64 rows: the memory-bound kernels (exact fp32 in every math mode)
+    if (trans_b)
+    {
+        if (M >= 1 && M <= 64 && K > 0 && K % 4 == 0 && aligned16(a) && aligned16(b))
+            return gemv_nt(out, a, b, M, N, K, st);
+        return gemm_nt(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)K, (int)N, 0, nullptr, st);
+    }
+    if (skinny_nn_ok(out, a, b, (int)M, (int)N, (int)K, (int)N, (int)N))
+        return skinny_nn(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, st);
+    return gemm_f32(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, false, 1, 0, 0, 0, st);
 }
 
 int fml_matmul_strided(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,

@@ -63,6 +63,7 @@ int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int 
              int batch, uint64_t pa, uint64_t pb, uint64_t pc, cudaStream_t st);
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
             int epi, const float* R, cudaStream_t st);
+int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 
 // ---------------------------------------------------------------- kernels --
 
@@ -782,6 +783,26 @@ int prefill_gemm(fml_lm* lm, float* C, const float* A, const float* W, int M, in
     if (epi) FML_LAUNCH_CHECK();
     return FML_OK;
 }
+
+}  // namespace
+
+// y[M x N] = x[M x K] . w[N x K]^T for M <= 64 rows (fml_matmul's small-batch
+// Mul<Right>): the decode GEMV without epilogue or programmatic launch.
+int fml::gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st)
+{
+    GemvArgs a{};
+    a.x = x;
+    a.ldx = K;
+    a.w = w;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.y = y;
+    a.ldy = N;
+    return launch_gemv<EPI_STORE, false>(a, st, false);
+}
+
+namespace {
 
 uint32_t graph_nodes_per_step(fml_lm* lm)
 {

@@ -94,9 +94,12 @@ def test_golden_strided_attention_pieces(golden):
     gemm_close(got[:, h * hd:(h + 1) * hd], ref[:, h * hd:(h + 1) * hd], P, K[:, h * hd:(h + 1) * hd])
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 5, 7), (128, 512, 128), (130, 96, 260), (512, 1536, 512)])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 5, 7), (128, 512, 128), (130, 96, 260), (512, 1536, 512),
+                                   (1, 512, 512), (8, 1024, 4096), (64, 4096, 1024), (33, 12, 2048), (5, 260, 100)])
 @pytest.mark.parametrize("mode", [0, 1])
 def test_matmul_vs_oracle(M, N, K, mode):
+    """Tiled GEMM, and at <= 64 rows the small-batch kernels (split-K for
+    Mul<None>, the decode GEMV for Mul<Right>), against the oracle."""
     from freeml_b200 import matrix_ops as F
     rs = np.random.RandomState(M * 7 + N * 3 + K + mode)
     A = rs.randn(M, K).astype(np.float32)
