@@ -42,6 +42,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="with N > 1 GPUs: tensor parallelism over all ranks (each runs every sequence) "
+                         "instead of sequence sharding (BASELINE config 5's scheme)")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=3,
                     help="BASELINE config (3 is the headline metric's; 4 and 5 add a timed prefill; 2 is the "
                          "per-operator microbench through the C ABI)")
@@ -58,7 +61,7 @@ def dist_env():
     return ws, rank, local
 
 
-def workload_config(n_gpus, b_local):
+def workload_config(n_gpus, b_local, tp=False):
     from freeml_b200.lm import CONFIGS
     c = CONFIGS[CONFIG]
     s = c["shape"]
@@ -68,7 +71,8 @@ def workload_config(n_gpus, b_local):
             "sequences": c["batch"], "sequences_per_gpu": b_local, "prompt": c["prompt"], "decode_tokens": c["new"],
             "step": f"one greedy decode pass ({c['new'] - 1} engine steps) of every sequence",
             "l2": "per engine step the working set (all weights + the K/V rows read) exceeds the 126 MB L2",
-            "parallelism": f"dp{n_gpus} (sequence sharding, no collective)"}
+            "parallelism": (f"tp{n_gpus} (heads / fc columns / vocabulary split, NCCL all-reduce after each "
+                            f"row-parallel projection)") if tp else f"dp{n_gpus} (sequence sharding, no collective)"}
 
 
 # ---------------------------------------------------------------- clocks --
@@ -351,13 +355,22 @@ def main():
     B_total, P, NEW = c["batch"], c["prompt"], c["new"]
     if B_total % ws:
         raise SystemExit(f"{B_total} sequences do not shard evenly over {ws} GPUs")
-    b_lo, b_hi = shard_bounds(B_total, ws, rank)
+    tp = args.tp and ws > 1
+    b_lo, b_hi = (0, B_total) if tp else shard_bounds(B_total, ws, rank)
     B = b_hi - b_lo
+    dp = 1 if tp else ws  # ranks whose tokens add up
     steps_per_pass = NEW - 1
 
     params = random_params(s, c["wseed"], local)
     prompts = prompt_tokens(c["pseed"], s.vocab, B_total, P)[b_lo:b_hi]
     lm = NanoLM(s, B, device=local)
+    if tp:
+        from freeml_b200.lm import nccl_unique_id
+        nid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            nid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+        pg.broadcast(nid, src=0)
+        lm.set_tensor_parallel(rank, ws, bytes(nid.cpu().numpy().tobytes()))
     lm.bind(params)
     del params
     lm.prefill(prompts)
@@ -386,7 +399,7 @@ def main():
     torch.cuda.synchronize()
     prefill_ms = max_over_ranks(pe0.elapsed_time(pe1), pg, "cuda")
     dm, Lm = s.d_model, s.n_layer
-    prefill_flop = ws * (Lm * (24 * B * P * dm * dm + 2 * B * P * P * dm) + 2 * B * s.vocab * dm)
+    prefill_flop = dp * (Lm * (24 * B * P * dm * dm + 2 * B * P * P * dm) + 2 * B * s.vocab * dm)
 
     if args.profile_only and args.profile_phase == "prefill":
         # for ncu (--profile-from-start off): one more prefill of the same
@@ -432,7 +445,7 @@ def main():
     clocks = sampler.stop()
     launches = _lib.launch_count() - launches0
     ms_max = max_over_ranks(ev0.elapsed_time(ev1), pg, "cuda")
-    tokens = ws * B * steps_per_pass * args.steps
+    tokens = dp * B * steps_per_pass * args.steps
     value = tokens / (ms_max / 1e3)
 
     # ---- e2e: the same passes through the host-buffer step (H2D + D2H) ----
@@ -451,7 +464,7 @@ def main():
             tok_in, tok_out = tok_out, tok_in
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0, pg, "cuda")
-    e2e_value = ws * B * steps_per_pass * e2e_passes / e2e_s
+    e2e_value = dp * B * steps_per_pass * e2e_passes / e2e_s
 
     # ---- roofline of the dominant kernel (attention), from a profiled pass ----
     lm.set_graph(False)
@@ -463,7 +476,10 @@ def main():
     lm.set_graph(True)
     d, L = s.d_model, s.n_layer
     peak, peak_kind = hbm_peak()
-    step_bytes = sum(4 * (12 * d * d * L + s.vocab * d + (2 * L + 1) * d) + B * 4 * (2 * d * L * (p + 1) + 2 * d * L + 2 * d)
+    tpw = ws if tp else 1  # this rank's share of the weights and heads
+    dl, fl, vl = d // tpw, 4 * d // tpw, -(-s.vocab // tpw)
+    step_bytes = sum(4 * (L * (4 * d * dl + 2 * d * fl) + vl * d + (2 * L + 1) * d)
+                     + B * 4 * (2 * dl * L * (p + 1) + 2 * dl * L + 2 * d)
                      for p in range(P, P + steps_per_pass))
     pass_ms = ms_max / args.steps
     total_prof_ms = sum(v[0] for v in prof.values())
@@ -476,7 +492,7 @@ def main():
         traffic = ncu_traffic("decode_step") if CONFIG == 3 else None
     else:
         k_ms, k_n = prof["attention"]
-        k_bytes = sum(4 * L * B * (2 * d * (p + 1) + 2 * d) for p in range(P, P + steps_per_pass))
+        k_bytes = sum(4 * L * B * (2 * dl * (p + 1) + 2 * dl) for p in range(P, P + steps_per_pass))
         k_name = "attention_kernel (split-KV decode attention)"
         traffic = ncu_traffic("attention") if CONFIG == 3 else None
     achieved = k_bytes / (k_ms / 1e3) / 1e9 if k_ms > 0 else None
@@ -485,7 +501,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": pass_ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": f"synthetic: seeded N(0,0.02) weights of the config-{CONFIG} architecture, seeded uniform prompts",
-            "config": dict(workload_config(ws, B),
+            "config": dict(workload_config(ws, B, tp),
                            engine="fused step kernel" if fused else "per-operation kernels (CUDA graph, PDL)"),
             "gpu_launches": int(launches),
             "clocks": clocks,
@@ -500,14 +516,14 @@ def main():
                               "achieved_GBps": step_bytes / (pass_ms / 1e3) / 1e9,
                               "frac": step_bytes / (pass_ms / 1e3) / 1e9 / peak},
             "kernel_ms_per_pass": {k: v[0] for k, v in prof.items()},
-            "prefill": {"ms": prefill_ms, "tokens_per_s": ws * B * P / (prefill_ms / 1e3),
+            "prefill": {"ms": prefill_ms, "tokens_per_s": dp * B * P / (prefill_ms / 1e3),
                         "algorithmic_tflop": prefill_flop / 1e12,
                         "tflops": prefill_flop / (prefill_ms / 1e3) / 1e12,
                         "math": "TF32x3 on tcgen05 (three kind::tf32 MMAs per product, fp32 accumulate in TMEM)",
                         "frac_of_tf32x3_peak": prefill_flop / (prefill_ms / 1e3) / 1e12 / (tensor_peak() / 2 / 3),
                         "peak_note": "tf32 dense = half the measured bf16 peak, / 3 for the three-pass split"},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * B * ws * steps_per_pass,
-                    "d2h_bytes_per_step": 4 * B * ws * steps_per_pass,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * B * dp * steps_per_pass,
+                    "d2h_bytes_per_step": 4 * B * dp * steps_per_pass,
                     "path": "fml_lm_step_host (host token buffers, H2D + D2H + sync every engine step)"}}
 
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and CONFIG == 3:

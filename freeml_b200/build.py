@@ -60,7 +60,7 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     if failed:
         raise RuntimeError("CUDA build failed")
     if _needs(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart", "-lcuda", "-lnccl"]
         if verbose:
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)

@@ -34,6 +34,8 @@
 #include <utility>
 #include <vector>
 
+#include <nccl.h>
+
 #include "attention.cuh"
 #include "decode_step.cuh"
 #include "fml_common.cuh"
@@ -130,6 +132,7 @@ struct GemvArgs
     uint64_t seq_stride;  // H*C*hd: one sequence's block inside a layer
     // EPI_ARGMAX
     unsigned long long* keys;
+    uint32_t n_off;  // global index of output column 0 (vocabulary-parallel lm_head)
     // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
     const float* gamma;
 };
@@ -347,7 +350,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
                 if (valid && a.y) a.y[(uint64_t)m * a.ldy + n] = v;
                 if (t < 32 * ((CNT + 31) / 32))
                 {
-                    unsigned long long key = valid ? argmax_key(v, n) : 0ull;
+                    unsigned long long key = valid ? argmax_key(v, n + a.n_off) : 0ull;
                     unsigned long long o1 = __shfl_xor_sync(FULL_MASK, key, 1);
                     key = o1 > key ? o1 : key;
                     unsigned long long o2 = __shfl_xor_sync(FULL_MASK, key, 2);
@@ -476,6 +479,14 @@ struct fml_lm
     bool pdl = true;
     int prefill_math = FML_MATH_TF32X3;  // prefill contractions on the tensor cores
 
+    // tensor parallelism: this rank's heads [h0, h0 + hl) (q/k/v width dl),
+    // fc columns [j0, j0 + fl), vocabulary rows [v0, v0 + vl); proj and mlp
+    // are row-parallel (partial sums all-reduced), the lm_head argmax keys
+    // are max-reduced.  One rank: the whole model.
+    int tp_rank = 0, tp_world = 1;
+    ncclComm_t comm = nullptr;
+    uint32_t hl = 0, dl = 0, fl = 0, h0 = 0, j0 = 0, v0 = 0, vl = 0;
+
     // fused decode step (one persistent kernel per step), opt-in: on config 3
     // it measures slower than the per-operation kernels (437 vs 337 us/step)
     bool fused = false;
@@ -511,6 +522,9 @@ uint64_t param_count(const fml_lm_config& c)
 void free_all(fml_lm* lm)
 {
     if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
+    lm->graph_exec = nullptr;
+    if (lm->comm) ncclCommDestroy(lm->comm);
+    lm->comm = nullptr;
     for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
     void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
                     lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
@@ -638,14 +652,14 @@ int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, c
     AttnArgs a{};
     a.row0 = row0;
     a.q = lm->q;
-    a.ldq = lm->cfg.d_model;
+    a.ldq = lm->dl;
     a.kc = lm->kc + (uint64_t)layer * lm->layer_stride;
     a.vc = lm->vc + (uint64_t)layer * lm->layer_stride;
     a.seq_stride = lm->seq_stride;
-    a.H = lm->cfg.n_head;
+    a.H = lm->hl;
     a.C = lm->cfg.context;
     a.out = lm->att;
-    a.ldo = lm->cfg.d_model;
+    a.ldo = lm->dl;
     a.pos = pos;
     a.P = P;
     a.S = S;
@@ -655,14 +669,32 @@ int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, c
     a.counters = lm->counters;
     a.grab = lm->grab + layer;
     FML_REQUIRE(rows <= 65535u, "attention: too many rows in one launch (%u)", rows);
-    FML_RC(launch_attention_kernel(a, lm->hd, dim3(lm->cfg.n_head, rows, S), st, pdl));
+    FML_RC(launch_attention_kernel(a, lm->hd, dim3(lm->hl, rows, S), st, pdl));
+    return FML_OK;
+}
+
+// Row-parallel partial sums: in-place NCCL all-reduce on the engine stream
+// (captured into the step's graph like the kernels).
+int all_reduce_sum(fml_lm* lm, float* buf, uint64_t n, cudaStream_t st)
+{
+    const ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, lm->comm, st);
+    if (r != ncclSuccess) return set_error(FML_ERR_CUDA, "ncclAllReduce: %s", ncclGetErrorString(r));
+    return FML_OK;
+}
+
+// Vocabulary-parallel argmax: every rank's packed (value, ~index) keys hold
+// its local best; the max over ranks is the global first-index argmax.
+int all_reduce_max_keys(fml_lm* lm, uint32_t B, cudaStream_t st)
+{
+    const ncclResult_t r = ncclAllReduce(lm->keys, lm->keys, B, ncclUint64, ncclMax, lm->comm, st);
+    if (r != ncclSuccess) return set_error(FML_ERR_CUDA, "ncclAllReduce: %s", ncclGetErrorString(r));
     return FML_OK;
 }
 
 // Plan the fused step for the active batch (once per batch size).
 bool fused_step_ready(fml_lm* lm)
 {
-    if (!lm->fused) return false;
+    if (!lm->fused || lm->tp_world > 1) return false;
     if (lm->step_batch == lm->batch) return lm->step_ok;
     const fml_lm_config& c = lm->cfg;
     StepArgs& a = lm->sa;
@@ -716,14 +748,16 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
                         (const float*)lm->pos_emb, (const uint32_t*)lm->pending, (const uint32_t*)lm->pos, B, 1u, d,
                         c.vocab, c.context, lm->grab, c.n_layer));
     }
+    const bool tp = lm->tp_world > 1;
+    const bool resid_here = lm->tp_rank == 0;  // row-parallel sums take the residual once
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         {
             ProfScope ps(lm, 2, st);
             GemvArgs a{};
-            a.x = lm->x; a.ldx = d; a.w = lm->wqkv[l]; a.M = B; a.N = 3 * d; a.K = d; a.gamma = lm->ln0[l];
+            a.x = lm->x; a.ldx = d; a.w = lm->wqkv[l]; a.M = B; a.N = 3 * lm->dl; a.K = d; a.gamma = lm->ln0[l];
             a.q = lm->q; a.kc = lm->kc + (uint64_t)l * lm->layer_stride; a.vc = lm->vc + (uint64_t)l * lm->layer_stride;
-            a.pos = lm->pos; a.d = d; a.H = c.n_head; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
+            a.pos = lm->pos; a.d = lm->dl; a.H = lm->hl; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
             FML_RC((launch_gemv<EPI_QKV, true>(a, st, pdl)));
         }
         {
@@ -733,36 +767,41 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
         {
             ProfScope ps(lm, 4, st);
             GemvArgs a{};
-            a.x = lm->att; a.ldx = d; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = d;
+            a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
+            if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
+            else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
+            if (tp) FML_RC(all_reduce_sum(lm, lm->buf, (uint64_t)B * d, st));
         }
         {
             ProfScope ps(lm, 5, st);
             GemvArgs a{};
-            a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = 4 * d; a.K = d; a.gamma = lm->ln1[l];
-            a.y = lm->hid; a.ldy = 4 * d;
-            FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl)));
+            a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = lm->fl; a.K = d; a.gamma = lm->ln1[l];
+            a.y = lm->hid; a.ldy = lm->fl;
+            FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl && !tp)));
         }
         {
             ProfScope ps(lm, 6, st);
             GemvArgs a{};
-            a.x = lm->hid; a.ldx = 4 * d; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = 4 * d;
+            a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
+            if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
+            else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
+            if (tp) FML_RC(all_reduce_sum(lm, lm->x, (uint64_t)B * d, st));
         }
     }
     {
         ProfScope ps(lm, 7, st);
         GemvArgs a{};
-        a.x = lm->x; a.ldx = d; a.w = lm->tok; a.M = B; a.N = c.vocab; a.K = d; a.gamma = lm->lnf;
-        a.y = logits; a.ldy = c.vocab; a.keys = lm->keys;
-        FML_RC((launch_gemv<EPI_ARGMAX, true>(a, st, pdl)));
+        a.x = lm->x; a.ldx = d; a.w = lm->tok + (uint64_t)lm->v0 * d; a.M = B; a.N = lm->vl; a.K = d;
+        a.gamma = lm->lnf; a.y = logits; a.ldy = lm->vl; a.keys = lm->keys; a.n_off = lm->v0;
+        FML_RC((launch_gemv<EPI_ARGMAX, true>(a, st, pdl && !tp)));
+        if (tp) FML_RC(all_reduce_max_keys(lm, B, st));
     }
     {
         ProfScope ps(lm, 8, st);
-        FML_RC(launch_k(finalize_kernel, dim3((B + 127) / 128), dim3(128), st, pdl, lm->keys, lm->pending, lm->pos,
-                        next_out, B, 0u));
+        FML_RC(launch_k(finalize_kernel, dim3((B + 127) / 128), dim3(128), st, pdl && !tp, lm->keys, lm->pending,
+                        lm->pos, next_out, B, 0u));
     }
     return FML_OK;
 }
@@ -832,6 +871,10 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     lm->device = device;
     lm->hd = hd;
     lm->hpos.assign(c.max_batch, 0);
+    lm->hl = c.n_head;
+    lm->dl = c.d_model;
+    lm->fl = 4 * c.d_model;
+    lm->vl = c.vocab;
 
     const uint64_t d = c.d_model, B = c.max_batch, Ctx = c.context, L = c.n_layer, H = c.n_head;
     lm->seq_stride = H * Ctx * hd;
@@ -937,17 +980,57 @@ int fml_lm_bind_weights(fml_lm* lm, const fml_lm_weights* w, fml_stream_t stream
         FML_LAUNCH_CHECK();
         return FML_OK;
     };
-    for (uint32_t l = 0; l < c.n_layer; ++l)
+    // tensor parallel: full transposes go through a scratch matrix, then
+    // this rank's rows (column-parallel QKV / fc) or input columns
+    // (row-parallel proj / mlp) are packed K-contiguous
+    const bool tp = lm->tp_world > 1;
+    float* scratch = nullptr;
+    if (tp) FML_CUDA_TRY(cudaMalloc(&scratch, 4 * d * d * f));
+    const uint64_t dl = lm->dl, fl = lm->fl, hoff = (uint64_t)lm->h0 * lm->hd, j0 = lm->j0;
+    int rc = FML_OK;
+    for (uint32_t l = 0; l < c.n_layer && rc == FML_OK; ++l)
     {
-        FML_REQUIRE(w->ln0[l] && w->ln1[l] && w->wproj[l], "fml_lm_bind_weights: null layer weight");
-        FML_CUDA_TRY(cudaMemcpyAsync(lm->ln0[l], w->ln0[l], d * f, cudaMemcpyDeviceToDevice, st));
-        FML_CUDA_TRY(cudaMemcpyAsync(lm->ln1[l], w->ln1[l], d * f, cudaMemcpyDeviceToDevice, st));
-        FML_CUDA_TRY(cudaMemcpyAsync(lm->wproj[l], w->wproj[l], d * d * f, cudaMemcpyDeviceToDevice, st));
-        FML_RC(tr(lm->wqkv[l], w->wqkv[l], (uint32_t)d, (uint32_t)(3 * d)));
-        FML_RC(tr(lm->wfc[l], w->wfc[l], (uint32_t)d, (uint32_t)(4 * d)));
-        FML_RC(tr(lm->wmlp[l], w->wmlp[l], (uint32_t)(4 * d), (uint32_t)d));
+        if (!(w->ln0[l] && w->ln1[l] && w->wproj[l]))
+        {
+            rc = set_error(FML_ERR_INVALID, "fml_lm_bind_weights: null layer weight");
+            break;
+        }
+        auto cp = [&](void* dst, const void* src, uint64_t bytes) {
+            if (rc == FML_OK && cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+                rc = set_error(FML_ERR_CUDA, "fml_lm_bind_weights: copy failed");
+        };
+        auto cp2d = [&](void* dst, uint64_t dpitch, const void* src, uint64_t spitch, uint64_t width, uint64_t h) {
+            if (rc == FML_OK &&
+                cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, h, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+                rc = set_error(FML_ERR_CUDA, "fml_lm_bind_weights: strided copy failed");
+        };
+        cp(lm->ln0[l], w->ln0[l], d * f);
+        cp(lm->ln1[l], w->ln1[l], d * f);
+        if (!tp)
+        {
+            cp(lm->wproj[l], w->wproj[l], d * d * f);
+            if (rc == FML_OK) rc = tr(lm->wqkv[l], w->wqkv[l], (uint32_t)d, (uint32_t)(3 * d));
+            if (rc == FML_OK) rc = tr(lm->wfc[l], w->wfc[l], (uint32_t)d, (uint32_t)(4 * d));
+            if (rc == FML_OK) rc = tr(lm->wmlp[l], w->wmlp[l], (uint32_t)(4 * d), (uint32_t)d);
+            continue;
+        }
+        // QKV [d x 3d] -> rows q|k|v of this rank's heads, each [dl x d]
+        if (rc == FML_OK) rc = tr(scratch, w->wqkv[l], (uint32_t)d, (uint32_t)(3 * d));
+        for (uint64_t part = 0; part < 3; ++part)
+            cp(lm->wqkv[l] + part * dl * d, scratch + (part * d + hoff) * d, dl * d * f);
+        // proj (out x in) -> its input columns of this rank's heads [d x dl]
+        cp2d(lm->wproj[l], dl * f, w->wproj[l] + hoff, d * f, dl * f, d);
+        // fc [d x 4d] -> this rank's fc rows [fl x d]
+        if (rc == FML_OK) rc = tr(scratch, w->wfc[l], (uint32_t)d, (uint32_t)(4 * d));
+        cp(lm->wfc[l], scratch + j0 * d, fl * d * f);
+        // mlp [4d x d] -> [d x 4d] -> its input columns [d x fl]
+        if (rc == FML_OK) rc = tr(scratch, w->wmlp[l], (uint32_t)(4 * d), (uint32_t)d);
+        cp2d(lm->wmlp[l], fl * f, scratch + j0, 4 * d * f, fl * f, d);
     }
-    FML_CUDA_TRY(cudaStreamSynchronize(st));
+    const cudaError_t se = cudaStreamSynchronize(st);
+    if (scratch) cudaFree(scratch);
+    if (rc != FML_OK) return rc;
+    if (se != cudaSuccess) return set_error(FML_ERR_CUDA, "fml_lm_bind_weights: %s", cudaGetErrorString(se));
     lm->bound = true;
     return FML_OK;
 }
@@ -1008,14 +1091,17 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     embed_kernel<<<R < 65535u ? R : 65535u, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->prompt_dev, nullptr, R, P, d,
                                                           c.vocab, c.context, nullptr, 0u);
     FML_LAUNCH_CHECK();
+    const bool tp = lm->tp_world > 1;
+    const int resid_epi = lm->tp_rank == 0 ? 2 : 0;  // row-parallel sums take the residual once
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         float* kc = lm->kc + (uint64_t)l * lm->layer_stride;
         float* vc = lm->vc + (uint64_t)l * lm->layer_stride;
+        const uint32_t dl = lm->dl, fl = lm->fl;
         FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
-        FML_RC(prefill_gemm(lm, lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * d), (int)d, 0, nullptr, st));
-        qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * d, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, d, lm->hd,
-                                                                              c.context, lm->seq_stride);
+        FML_RC(prefill_gemm(lm, lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * dl), (int)d, 0, nullptr, st));
+        qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * dl, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, dl, lm->hd,
+                                                                               c.context, lm->seq_stride);
         FML_LAUNCH_CHECK();
         // prefill attention: one query row per (b, t), the whole causal key
         // range in one CTA, launched in slabs of at most 65535 rows
@@ -1025,18 +1111,21 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
             FML_RC(launch_attention(lm, l, r0, R - r0 < 65535u ? R - r0 : 65535u, nullptr, P, 1, c.context, st));
         }
         // buf = x + att . Wproj^T ; hid = gelu(LN1(buf) . Wfc^T) ; x = buf + hid . Wmlp^T
-        FML_RC(prefill_gemm(lm, lm->buf, lm->att, lm->wproj[l], (int)R, (int)d, (int)d, 2, lm->x, st));
+        FML_RC(prefill_gemm(lm, lm->buf, lm->att, lm->wproj[l], (int)R, (int)d, (int)dl, resid_epi, lm->x, st));
+        if (tp) FML_RC(all_reduce_sum(lm, lm->buf, (uint64_t)R * d, st));
         FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
-        FML_RC(prefill_gemm(lm, lm->hid, lm->ln, lm->wfc[l], (int)R, (int)(4 * d), (int)d, 1, nullptr, st));
-        FML_RC(prefill_gemm(lm, lm->x, lm->hid, lm->wmlp[l], (int)R, (int)d, (int)(4 * d), 2, lm->buf, st));
+        FML_RC(prefill_gemm(lm, lm->hid, lm->ln, lm->wfc[l], (int)R, (int)fl, (int)d, 1, nullptr, st));
+        FML_RC(prefill_gemm(lm, lm->x, lm->hid, lm->wmlp[l], (int)R, (int)d, (int)fl, resid_epi, lm->buf, st));
+        if (tp) FML_RC(all_reduce_sum(lm, lm->x, (uint64_t)R * d, st));
     }
     // last prompt row of each sequence -> ln_f -> lm_head argmax
     FML_RC(launch_layernorm(lm->ln, lm->x + (uint64_t)(P - 1) * d, lm->lnf, nullptr, nullptr, batch, d,
                             (uint64_t)P * d, d, 1e-5f, st));
     GemvArgs a{};
-    a.x = lm->ln; a.ldx = d; a.w = lm->tok; a.M = batch; a.N = c.vocab; a.K = d; a.y = nullptr; a.ldy = c.vocab;
-    a.keys = lm->keys;
+    a.x = lm->ln; a.ldx = d; a.w = lm->tok + (uint64_t)lm->v0 * d; a.M = batch; a.N = lm->vl; a.K = d; a.y = nullptr;
+    a.ldy = lm->vl; a.keys = lm->keys; a.n_off = lm->v0;
     FML_RC((launch_gemv<EPI_ARGMAX, false>(a, st, false)));
+    if (tp) FML_RC(all_reduce_max_keys(lm, batch, st));
     finalize_kernel<<<(batch + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, nullptr, batch, P);
     FML_LAUNCH_CHECK();
     for (uint32_t b = 0; b < batch; ++b) lm->hpos[b] = P;
@@ -1049,6 +1138,60 @@ int fml_lm_set_prefill_math(fml_lm* lm, int mode)
     FML_REQUIRE(mode == FML_MATH_FP32 || mode == FML_MATH_TF32X3 || mode == FML_MATH_TF32, "unknown math mode %d",
                 mode);
     lm->prefill_math = mode;
+    return FML_OK;
+}
+
+int fml_nccl_unique_id(void* out)
+{
+    FML_REQUIRE(out, "fml_nccl_unique_id: null argument");
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) return set_error(FML_ERR_CUDA, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    std::memcpy(out, &id, sizeof(id));
+    return FML_OK;
+}
+
+int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl_id)
+{
+    FML_REQUIRE(lm && world >= 1 && rank >= 0 && rank < world, "fml_lm_set_tensor_parallel: bad rank/world");
+    FML_REQUIRE(!lm->bound, "fml_lm_set_tensor_parallel: call before binding weights");
+    FML_REQUIRE(!lm->comm, "fml_lm_set_tensor_parallel: already set");
+    const fml_lm_config& c = lm->cfg;
+    FML_REQUIRE(c.n_head % (uint32_t)world == 0 && (4 * c.d_model) % (uint32_t)world == 0 &&
+                    c.vocab >= (uint32_t)world,
+                "fml_lm_set_tensor_parallel: %u heads / 4*%u fc columns / vocab %u do not split over %d ranks",
+                c.n_head, c.d_model, c.vocab, world);
+    if (world == 1) return FML_OK;
+    FML_REQUIRE(nccl_id, "fml_lm_set_tensor_parallel: null NCCL id");
+    FML_CUDA_TRY(cudaSetDevice(lm->device));
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof(id));
+    const ncclResult_t r = ncclCommInitRank(&lm->comm, world, id, rank);
+    if (r != ncclSuccess)
+    {
+        lm->comm = nullptr;
+        return set_error(FML_ERR_CUDA, "ncclCommInitRank: %s", ncclGetErrorString(r));
+    }
+    lm->tp_rank = rank;
+    lm->tp_world = world;
+    lm->hl = c.n_head / world;
+    lm->h0 = rank * lm->hl;
+    lm->dl = lm->hl * lm->hd;
+    lm->fl = 4 * c.d_model / world;
+    lm->j0 = rank * lm->fl;
+    lm->vl = (c.vocab + world - 1) / world;
+    lm->v0 = rank * lm->vl;
+    if (lm->v0 + lm->vl > c.vocab) lm->vl = c.vocab - lm->v0;
+    // this rank's heads only in the cache and in the attention splits
+    lm->seq_stride = (uint64_t)lm->hl * c.context * lm->hd;
+    lm->layer_stride = (uint64_t)c.max_batch * lm->seq_stride;
+    attention_splits((uint64_t)c.max_batch * lm->hl, c.context, &lm->S, &lm->chunk);
+    if (lm->part) cudaFree(lm->part);
+    lm->part = nullptr;
+    FML_CUDA_TRY(cudaMalloc(&lm->part, (uint64_t)c.max_batch * lm->hl * lm->S * (lm->hd + 2) * sizeof(float)));
+    lm->step_batch = 0;
+    if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
+    lm->graph_exec = nullptr;
     return FML_OK;
 }
 
@@ -1181,13 +1324,14 @@ uint64_t fml_lm_step_bytes(fml_lm* lm)
 {
     if (!lm) return 0;
     const fml_lm_config& c = lm->cfg;
-    const uint64_t d = c.d_model, L = c.n_layer, f = 4;
-    uint64_t bytes = f * (12 * d * d * L + (uint64_t)c.vocab * d + (2 * L + 1) * d);  // weights once
+    const uint64_t d = c.d_model, L = c.n_layer, f = 4, dl = lm->dl, fl = lm->fl;
+    // this rank's weights once (all of them on one rank)
+    uint64_t bytes = f * (L * (4 * d * dl + 2 * d * fl) + (uint64_t)lm->vl * d + (2 * L + 1) * d);
     for (uint32_t b = 0; b < lm->batch; ++b)
     {
         const uint64_t len = lm->hpos[b] + 1;  // keys/values read this step, including the new row
-        bytes += f * 2 * d * L * len;          // K and V rows read
-        bytes += f * 2 * d * L;                // the new K and V rows written
+        bytes += f * 2 * dl * L * len;         // K and V rows read (this rank's heads)
+        bytes += f * 2 * dl * L;               // the new K and V rows written
         bytes += f * 2 * d;                    // token + position rows
     }
     return bytes;

@@ -102,11 +102,19 @@ class NanoLM:
         logits_ptr = None
         if want_logits:
             if self._logits is None:
-                self._logits = torch.empty(self.max_batch, self.shape.vocab, dtype=torch.float32,
+                self._logits = torch.empty(self.max_batch, self.vocab_slice()[1], dtype=torch.float32,
                                            device=torch.device("cuda", self.device))
             logits_ptr = self._logits.data_ptr()
         call("fml_lm_step", self._h, self._next.data_ptr(), logits_ptr, self._stream())
         return self._next[: self.batch], (self._logits[: self.batch] if want_logits else None)
+
+    def vocab_slice(self):
+        """(first row, rows) of the vocabulary this engine's logits cover:
+        all of it, or the rank's share under tensor parallelism."""
+        rank, world = getattr(self, "tp", (0, 1))
+        vl = -(-self.shape.vocab // world)
+        v0 = rank * vl
+        return v0, min(vl, self.shape.vocab - v0)
 
     def step_host(self, tokens_in: np.ndarray, tokens_out: np.ndarray) -> None:
         """The host-buffer step: tokens_in -> device, step, next tokens -> tokens_out."""
@@ -139,6 +147,14 @@ class NanoLM:
         buf = torch.empty(self.batch, dtype=torch.int32, device=torch.device("cuda", self.device))
         call("fml_lm_pending", self._h, buf.data_ptr(), self._stream())
         return buf
+
+    def set_tensor_parallel(self, rank: int, world: int, nccl_id: bytes) -> None:
+        """Join a tensor-parallel group of `world` engines (one per GPU and
+        process); `nccl_id` comes from nccl_unique_id() on one rank.  Call
+        before bind()."""
+        buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+        call("fml_lm_set_tensor_parallel", self._h, int(rank), int(world), buf)
+        self.tp = (int(rank), int(world))
 
     def set_fused_step(self, on: bool) -> None:
         """Fused decode step (one persistent kernel per step) on or off."""
@@ -185,6 +201,14 @@ class NanoLM:
         call("fml_lm_get_profile", self._h, ctypes.cast(ms, ctypes.c_void_p), ctypes.cast(n, ctypes.c_void_p),
              FML_LM_NCLASS)
         return {PROFILE_CLASSES[i]: (float(ms[i]), int(n[i])) for i in range(FML_LM_NCLASS)}
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL id for set_tensor_parallel (make it on one rank
+    and share it with the others)."""
+    buf = ctypes.create_string_buffer(128)
+    call("fml_nccl_unique_id", buf)
+    return buf.raw
 
 
 def random_params(shape: NanoLLMShape, seed: int, device: int = 0) -> torch.Tensor:

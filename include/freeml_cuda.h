@@ -252,6 +252,23 @@ FML_API uint64_t fml_lm_param_count(const fml_lm_config* cfg);
 FML_API int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t prompt_len,
                    fml_stream_t stream);
 
+/* Tensor parallelism over `world` GPUs (one process and one engine each),
+ * for models too slow or too large for one GPU.  Call
+ * on every rank after fml_lm_create and before binding weights, with the
+ * same 128-byte NCCL id on all ranks (from fml_nccl_unique_id on one rank,
+ * shared by the caller).  Rank r then keeps heads [r*H/w, (r+1)*H/w) of
+ * QKV and attention (column-parallel) and the matching input columns of
+ * the attention projection (row-parallel), fc columns [r*4d/w, ...) and the
+ * matching mlp inputs, and vocabulary rows [r*ceil(V/w), ...) of the tied
+ * lm_head; the row-parallel partial sums are all-reduced (ncclSum, in
+ * place) and the argmax keys max-reduced, so every rank ends each step with
+ * the same tokens.  Logits returned by fml_lm_step are this rank's
+ * vocabulary slice [B x ceil(V/w)].  Weights are given whole to
+ * fml_lm_bind_weights / fml_lm_bind_packed; each rank packs its share. */
+#define FML_NCCL_ID_BYTES 128
+FML_API int fml_nccl_unique_id(void* id_out);
+FML_API int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl_id);
+
 /* Precision of the prefill contractions (FML_MATH_*; default
  * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy). */
 FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
