@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1 GPUs: tensor parallelism over all ranks (each runs every sequence) "
                          "instead of sequence sharding (BASELINE config 5's scheme)")
+    ap.add_argument("--tp-fused", action="store_true",
+                    help="with --tp: the all-reduce fused into the projection GEMVs over NVLink peer memory "
+                         "instead of NCCL calls (measured slower at TP=2)")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=3,
                     help="BASELINE config (3 is the headline metric's; 4 and 5 add a timed prefill; 2 is the "
                          "per-operator microbench through the C ABI)")
@@ -71,7 +74,7 @@ def workload_config(n_gpus, b_local, tp=False):
             "sequences": c["batch"], "sequences_per_gpu": b_local, "prompt": c["prompt"], "decode_tokens": c["new"],
             "step": f"one greedy decode pass ({c['new'] - 1} engine steps) of every sequence",
             "l2": "per engine step the working set (all weights + the K/V rows read) exceeds the 126 MB L2",
-            "parallelism": (f"tp{n_gpus} (heads / fc columns / vocabulary split, NCCL all-reduce after each "
+            "parallelism": (f"tp{n_gpus} (heads / fc columns / vocabulary split, all-reduce after each "
                             f"row-parallel projection)") if tp else f"dp{n_gpus} (sequence sharding, no collective)"}
 
 
@@ -371,6 +374,11 @@ def main():
             nid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
         pg.broadcast(nid, src=0)
         lm.set_tensor_parallel(rank, ws, bytes(nid.cpu().numpy().tobytes()))
+        if args.tp_fused:
+            mine = torch.frombuffer(bytearray(lm.tp_ipc_handles()), dtype=torch.uint8).cuda()
+            allh = [torch.empty_like(mine) for _ in range(ws)]
+            pg.all_gather(allh, mine)
+            lm.tp_connect([h.cpu().numpy().tobytes() for h in allh])
     lm.bind(params)
     del params
     lm.prefill(prompts)
@@ -502,6 +510,8 @@ def main():
             "vs_baseline": None, "dtype": "f32",
             "data": f"synthetic: seeded N(0,0.02) weights of the config-{CONFIG} architecture, seeded uniform prompts",
             "config": dict(workload_config(ws, B, tp),
+                           allreduce=("fused into the projection GEMVs over NVLink peer memory (prefill: NCCL)"
+                                      if args.tp_fused else "NCCL") if tp else None,
                            engine="fused step kernel" if fused else "per-operation kernels (CUDA graph, PDL)"),
             "gpu_launches": int(launches),
             "clocks": clocks,

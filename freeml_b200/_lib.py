@@ -82,6 +82,9 @@ SIGNATURES = {
     "fml_lm_set_fused_step": (_I, [_P, _I]),
     "fml_nccl_unique_id": (_I, [_P]),
     "fml_lm_set_tensor_parallel": (_I, [_P, _I, _I, _P]),
+    "fml_lm_tp_ipc_handles": (_I, [_P, _P]),
+    "fml_lm_tp_connect": (_I, [_P, _P]),
+    "fml_lm_tp_error_count": (_I, [_P]),
     "fml_lm_get_fused_step": (_I, [_P, _P]),
     "fml_lm_pending": (_I, [_P, _P, _P]),
     "fml_lm_get_position": (_I, [_P, _U32, ctypes.POINTER(_U32)]),

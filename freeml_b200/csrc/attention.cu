@@ -330,10 +330,12 @@ int fml_device_error_count(uint64_t* count)
 {
     FML_REQUIRE(count, "fml_device_error_count: null argument");
     int v = 0, g = 0, f = 0;
+    uint64_t tpw = 0;
     FML_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_attention_timeouts, sizeof(int)));
     FML_RC(gemm_tc_error_count(&g));
     FML_RC(decode_step_error_count(&f));
-    *count = (uint64_t)v + (uint64_t)g + (uint64_t)f;
+    FML_RC(fml_lm_tp_error_count(&tpw));
+    *count = (uint64_t)v + (uint64_t)g + (uint64_t)f + tpw;
     return FML_OK;
 }
 

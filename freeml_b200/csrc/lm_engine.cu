@@ -99,7 +99,13 @@ __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ to
     }
 }
 
-enum GemvEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_ARGMAX = 4 };
+enum GemvEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_ARGMAX = 4, EPI_ARSUM = 5 };
+
+// Tensor-parallel all-reduce fused into the row-parallel GEMV: flag slots
+// per rank (one per CTA of the GEMV grid) and the wait bound.
+constexpr uint32_t AR_FLAGS = 4096;
+constexpr uint64_t AR_WAIT_NS = 1000000000ull;
+__device__ unsigned int g_tp_timeouts = 0;
 
 // Weight stream load: each weight is read once per step, so it bypasses L1
 // and leaves L1 to the activation rows that every column group re-reads
@@ -133,6 +139,17 @@ struct GemvArgs
     // EPI_ARGMAX
     unsigned long long* keys;
     uint32_t n_off;  // global index of output column 0 (vocabulary-parallel lm_head)
+    // EPI_ARSUM: y = r + sum over ranks of every rank's partial x.W^T.  This
+    // rank writes its partial into every rank's receive buffer (peer stores
+    // over NVLink), raises its flag for this CTA on every rank, waits for
+    // the flags of all ranks for this CTA, then sums the partials in rank
+    // order, so all ranks hold bit-identical results.
+    float* const* peer_recv;     // [world] receive buffers [world][bmax][N]
+    uint32_t* const* peer_flags; // [world] flag arrays [world][AR_FLAGS]
+    const float* recv;           // this rank's receive buffer
+    const uint32_t* flags;       // this rank's flag array
+    const uint32_t* epoch;       // steps completed (tags the flags)
+    uint32_t world, rank, bmax, slot;
     // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
     const float* gamma;
 };
@@ -343,6 +360,12 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
                     }
                 }
             }
+            else if constexpr (EPI == EPI_ARSUM)
+            {
+                if (valid)
+                    for (uint32_t r = 0; r < a.world; ++r)
+                        a.peer_recv[r][((uint64_t)a.rank * a.bmax + m) * a.N + n] = v;
+            }
             else if constexpr (EPI == EPI_ARGMAX)
             {
                 // logits (optional) and the per-row argmax over these 4
@@ -357,6 +380,55 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
                     key = o2 > key ? o2 : key;
                     if (valid && (t % NW) == 0) atomicMax(a.keys + m, key);
                 }
+            }
+        }
+    }
+
+    if constexpr (EPI == EPI_ARSUM)
+    {
+        // publish this CTA's partial columns on every rank, then wait for
+        // every rank's partial of the same columns (the same CTA there)
+        const uint32_t cta = blockIdx.y * gridDim.x + blockIdx.x;
+        const uint32_t tag = __ldcg(a.epoch) * 128u + a.slot + 1u;
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0)
+        {
+            for (uint32_t r = 0; r < a.world; ++r)
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.peer_flags[r] + a.rank * AR_FLAGS + cta),
+                             "r"(tag)
+                             : "memory");
+            uint64_t t0 = 0;
+            for (uint32_t r = 0; r < a.world; ++r)
+            {
+                const uint32_t* f = a.flags + r * AR_FLAGS + cta;
+                for (uint32_t it = 0;; ++it)
+                {
+                    uint32_t v;
+                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                    if (v >= tag) break;
+                    uint64_t now;
+                    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+                    if (it == 0) t0 = now;
+                    else if (now - t0 > AR_WAIT_NS)
+                    {
+                        atomicAdd(&g_tp_timeouts, 1u);  // the result is wrong; nothing waits forever
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
+        __syncthreads();
+        for (uint32_t g = blockIdx.y; g < ngroups; g += gridDim.y)
+        {
+            const int t = threadIdx.x;
+            const uint32_t m = m0 + t / NW, n = g * NW + t % NW;
+            if (t < CNT && m < a.M && n < a.N)
+            {
+                float sum = 0.f;
+                for (uint32_t r = 0; r < a.world; ++r) sum += __ldcg(a.recv + ((uint64_t)r * a.bmax + m) * a.N + n);
+                a.y[(uint64_t)m * a.ldy + n] = a.r[(uint64_t)m * a.ldr + n] + sum;
             }
         }
     }
@@ -383,11 +455,12 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
 
 // After lm_head: pending token = argmax, advance the position, reset keys.
 __global__ void finalize_kernel(unsigned long long* keys, uint32_t* pending, uint32_t* pos, uint32_t* next_out,
-                                uint32_t B, uint32_t set_pos)
+                                uint32_t B, uint32_t set_pos, uint32_t* epoch)
 {
     FML_TIMELINE_SCOPE(30);
     griddep_wait();
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b == 0 && epoch) *epoch += 1u;
     if (b >= B) return;
     const uint32_t tok = argmax_key_index(keys[b]);
     pending[b] = tok;
@@ -486,6 +559,14 @@ struct fml_lm
     int tp_rank = 0, tp_world = 1;
     ncclComm_t comm = nullptr;
     uint32_t hl = 0, dl = 0, fl = 0, h0 = 0, j0 = 0, v0 = 0, vl = 0;
+    // fused all-reduce over peer memory (after fml_lm_tp_connect)
+    bool ar_fused = false;
+    float* ar_recv = nullptr;        // [world][max_batch][d], written by every rank
+    uint32_t* ar_flags = nullptr;    // [world][AR_FLAGS]
+    uint32_t* ar_epoch = nullptr;    // steps completed
+    float** ar_peer_recv = nullptr;  // device arrays of the world's pointers
+    uint32_t** ar_peer_flags = nullptr;
+    std::vector<void*> ar_opened;    // peer mappings to close
 
     // fused decode step (one persistent kernel per step), opt-in: on config 3
     // it measures slower than the per-operation kernels (437 vs 337 us/step)
@@ -525,6 +606,11 @@ void free_all(fml_lm* lm)
     lm->graph_exec = nullptr;
     if (lm->comm) ncclCommDestroy(lm->comm);
     lm->comm = nullptr;
+    for (void* p : lm->ar_opened) cudaIpcCloseMemHandle(p);
+    lm->ar_opened.clear();
+    void* arp[] = {lm->ar_recv, lm->ar_flags, lm->ar_epoch, lm->ar_peer_recv, lm->ar_peer_flags};
+    for (void* p : arp)
+        if (p) cudaFree(p);
     for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
     void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
                     lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
@@ -626,6 +712,8 @@ int launch_gemv_mt(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
     if (gy < 1) gy = 1;
     if (gy > ngroups) gy = ngroups;
     if (gy > 65535u) gy = 65535u;
+    if (EPI == EPI_ARSUM)
+        FML_REQUIRE(gx * gy <= AR_FLAGS, "gemv: %u CTAs exceed the all-reduce flag slots", gx * gy);
     return launch_k(gemv_kernel<MT, EPI, LN>, dim3(gx, gy), dim3(128), st, pdl, a);
 }
 
@@ -680,6 +768,19 @@ int all_reduce_sum(fml_lm* lm, float* buf, uint64_t n, cudaStream_t st)
     const ncclResult_t r = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, lm->comm, st);
     if (r != ncclSuccess) return set_error(FML_ERR_CUDA, "ncclAllReduce: %s", ncclGetErrorString(r));
     return FML_OK;
+}
+
+void set_arsum(fml_lm* lm, GemvArgs& a, uint32_t slot)
+{
+    a.peer_recv = lm->ar_peer_recv;
+    a.peer_flags = lm->ar_peer_flags;
+    a.recv = lm->ar_recv;
+    a.flags = lm->ar_flags;
+    a.epoch = lm->ar_epoch;
+    a.world = (uint32_t)lm->tp_world;
+    a.rank = (uint32_t)lm->tp_rank;
+    a.bmax = lm->cfg.max_batch;
+    a.slot = slot;
 }
 
 // Vocabulary-parallel argmax: every rank's packed (value, ~index) keys hold
@@ -769,25 +870,41 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
-            else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
-            if (tp) FML_RC(all_reduce_sum(lm, lm->buf, (uint64_t)B * d, st));
+            if (lm->ar_fused)
+            {
+                set_arsum(lm, a, 2 * l);
+                FML_RC((launch_gemv<EPI_ARSUM, false>(a, st, pdl)));
+            }
+            else
+            {
+                if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
+                else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
+                if (tp) FML_RC(all_reduce_sum(lm, lm->buf, (uint64_t)B * d, st));
+            }
         }
         {
             ProfScope ps(lm, 5, st);
             GemvArgs a{};
             a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = lm->fl; a.K = d; a.gamma = lm->ln1[l];
             a.y = lm->hid; a.ldy = lm->fl;
-            FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl && !tp)));
+            FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl && (!tp || lm->ar_fused))));
         }
         {
             ProfScope ps(lm, 6, st);
             GemvArgs a{};
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
-            else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
-            if (tp) FML_RC(all_reduce_sum(lm, lm->x, (uint64_t)B * d, st));
+            if (lm->ar_fused)
+            {
+                set_arsum(lm, a, 2 * l + 1);
+                FML_RC((launch_gemv<EPI_ARSUM, false>(a, st, pdl)));
+            }
+            else
+            {
+                if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
+                else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
+                if (tp) FML_RC(all_reduce_sum(lm, lm->x, (uint64_t)B * d, st));
+            }
         }
     }
     {
@@ -801,7 +918,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
     {
         ProfScope ps(lm, 8, st);
         FML_RC(launch_k(finalize_kernel, dim3((B + 127) / 128), dim3(128), st, pdl && !tp, lm->keys, lm->pending,
-                        lm->pos, next_out, B, 0u));
+                        lm->pos, next_out, B, 0u, lm->ar_epoch));
     }
     return FML_OK;
 }
@@ -1126,7 +1243,8 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     a.ldy = lm->vl; a.keys = lm->keys; a.n_off = lm->v0;
     FML_RC((launch_gemv<EPI_ARGMAX, false>(a, st, false)));
     if (tp) FML_RC(all_reduce_max_keys(lm, batch, st));
-    finalize_kernel<<<(batch + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, nullptr, batch, P);
+    finalize_kernel<<<(batch + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, nullptr, batch, P,
+                                                         lm->ar_epoch);
     FML_LAUNCH_CHECK();
     for (uint32_t b = 0; b < batch; ++b) lm->hpos[b] = P;
     return FML_OK;
@@ -1189,9 +1307,70 @@ int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl
     if (lm->part) cudaFree(lm->part);
     lm->part = nullptr;
     FML_CUDA_TRY(cudaMalloc(&lm->part, (uint64_t)c.max_batch * lm->hl * lm->S * (lm->hd + 2) * sizeof(float)));
+    // buffers the fused all-reduce shares with the other ranks (fml_lm_tp_connect)
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_recv, (uint64_t)world * c.max_batch * c.d_model * sizeof(float)));
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_flags, (uint64_t)world * AR_FLAGS * sizeof(uint32_t)));
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_epoch, sizeof(uint32_t)));
+    FML_CUDA_TRY(cudaMemset(lm->ar_flags, 0, (uint64_t)world * AR_FLAGS * sizeof(uint32_t)));
+    FML_CUDA_TRY(cudaMemset(lm->ar_epoch, 0, sizeof(uint32_t)));
     lm->step_batch = 0;
     if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
     lm->graph_exec = nullptr;
+    return FML_OK;
+}
+
+int fml_lm_tp_ipc_handles(fml_lm* lm, void* out)
+{
+    FML_REQUIRE(lm && out, "fml_lm_tp_ipc_handles: null argument");
+    FML_REQUIRE(lm->tp_world > 1 && lm->ar_recv, "fml_lm_tp_ipc_handles: call fml_lm_set_tensor_parallel first");
+    cudaIpcMemHandle_t h[2];
+    FML_CUDA_TRY(cudaIpcGetMemHandle(&h[0], lm->ar_recv));
+    FML_CUDA_TRY(cudaIpcGetMemHandle(&h[1], lm->ar_flags));
+    std::memcpy(out, h, sizeof(h));
+    return FML_OK;
+}
+
+int fml_lm_tp_connect(fml_lm* lm, const void* all)
+{
+    FML_REQUIRE(lm && all, "fml_lm_tp_connect: null argument");
+    FML_REQUIRE(lm->tp_world > 1 && lm->ar_recv, "fml_lm_tp_connect: call fml_lm_set_tensor_parallel first");
+    FML_REQUIRE(!lm->ar_fused, "fml_lm_tp_connect: already connected");
+    const int world = lm->tp_world;
+    std::vector<float*> recv(world);
+    std::vector<uint32_t*> flags(world);
+    const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(all);
+    for (int r = 0; r < world; ++r)
+    {
+        if (r == lm->tp_rank)
+        {
+            recv[r] = lm->ar_recv;
+            flags[r] = lm->ar_flags;
+            continue;
+        }
+        void* p = nullptr;
+        FML_CUDA_TRY(cudaIpcOpenMemHandle(&p, h[2 * r], cudaIpcMemLazyEnablePeerAccess));
+        lm->ar_opened.push_back(p);
+        recv[r] = static_cast<float*>(p);
+        FML_CUDA_TRY(cudaIpcOpenMemHandle(&p, h[2 * r + 1], cudaIpcMemLazyEnablePeerAccess));
+        lm->ar_opened.push_back(p);
+        flags[r] = static_cast<uint32_t*>(p);
+    }
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_peer_recv, world * sizeof(float*)));
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_peer_flags, world * sizeof(uint32_t*)));
+    FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_recv, recv.data(), world * sizeof(float*), cudaMemcpyHostToDevice));
+    FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_flags, flags.data(), world * sizeof(uint32_t*), cudaMemcpyHostToDevice));
+    lm->ar_fused = true;
+    if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
+    lm->graph_exec = nullptr;
+    return FML_OK;
+}
+
+int fml_lm_tp_error_count(uint64_t* out)
+{
+    FML_REQUIRE(out, "fml_lm_tp_error_count: null argument");
+    unsigned int v = 0;
+    FML_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tp_timeouts, sizeof(v)));
+    *out = v;
     return FML_OK;
 }
 

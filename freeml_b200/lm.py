@@ -156,6 +156,19 @@ class NanoLM:
         call("fml_lm_set_tensor_parallel", self._h, int(rank), int(world), buf)
         self.tp = (int(rank), int(world))
 
+    def tp_ipc_handles(self) -> bytes:
+        """This rank's 128 bytes of CUDA IPC handles for the fused all-reduce."""
+        buf = ctypes.create_string_buffer(128)
+        call("fml_lm_tp_ipc_handles", self._h, buf)
+        return buf.raw
+
+    def tp_connect(self, handles_by_rank) -> None:
+        """Open every rank's buffers (the handles of all ranks, rank order);
+        the decode step then all-reduces inside its projection kernels."""
+        blob = b"".join(bytes(h) for h in handles_by_rank)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        call("fml_lm_tp_connect", self._h, buf)
+
     def set_fused_step(self, on: bool) -> None:
         """Fused decode step (one persistent kernel per step) on or off."""
         call("fml_lm_set_fused_step", self._h, int(bool(on)))

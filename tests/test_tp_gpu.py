@@ -20,7 +20,7 @@ SHAPE = (4096, 512, 512, 8, 8)  # config 3: V C d H L
 NSEQ, N = 4, 24
 
 
-def _rank(rank, world, q_id, q_out):
+def _rank(rank, world, q_id, q_out, fused, q_h):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     try:
         torch.cuda.set_device(rank)
@@ -37,21 +37,39 @@ def _rank(rank, world, q_id, q_out):
         prompts = prompt_tokens(c["pseed"], s.V, c["batch"], c["prompt"])[:NSEQ]
         lm = NanoLM(NanoLLMShape(*SHAPE), NSEQ, device=rank)
         lm.set_tensor_parallel(rank, world, nid)
+        if fused:
+            # every rank's IPC handles, in rank order, to every rank
+            mine = lm.tp_ipc_handles()
+            for _ in range(world - 1):
+                q_h[1 - rank].put((rank, mine))
+            got = {rank: mine}
+            while len(got) < world:
+                r, hnd = q_h[rank].get(timeout=120)
+                got[r] = hnd
+            lm.tp_connect([got[r] for r in range(world)])
         lm.bind(w)
         toks, logits = lm.generate(prompts, N, want_logits=True)
         v0, vl = lm.vocab_slice()
+        import ctypes
+        from freeml_b200 import _lib
+        errs = ctypes.c_uint64(0)
+        _lib.call("fml_device_error_count", ctypes.byref(errs))
         lm.close()
-        q_out.put((rank, toks, logits, v0, vl))
+        q_out.put((rank, toks, logits, v0, vl) if errs.value == 0 else (rank, None, f"{errs.value} device errors", 0, 0))
     except Exception as e:  # reported to the parent
         q_out.put((rank, None, repr(e), 0, 0))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_two_gpus_matches_reference():
+@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "fused_allreduce"])
+def test_tensor_parallel_two_gpus_matches_reference(fused):
+    """NCCL all-reduce, and the all-reduce fused into the projection GEMVs
+    over NVLink peer memory."""
     world = 2
     ctx = mp.get_context("spawn")
     q_id, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, q_id, q_out)) for r in range(world)]
+    q_h = [ctx.Queue() for _ in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, q_id, q_out, fused, q_h)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
