@@ -729,8 +729,13 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
         FML_CUDA_TRY(cudaGetDevice(&dev));
         FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     }
-    if (a.M <= 4) return launch_gemv_mt<4, EPI, LN>(a, st, pdl, sms);
-    if (a.M <= 8) return launch_gemv_mt<8, EPI, LN>(a, st, pdl, sms);
+    // rows per CTA: the batch up to 16 (tuning override FML_GEMV_MT = 4, 8 or 16
+    // caps it; smaller caps trade W re-reads for registers and occupancy)
+    const char* mt_env = getenv("FML_GEMV_MT");
+    const long mt_v = mt_env ? strtol(mt_env, nullptr, 10) : 16;
+    const uint32_t mt_cap = (uint32_t)(mt_v == 4 || mt_v == 8 ? mt_v : 16);
+    if (a.M <= 4 || mt_cap == 4) return launch_gemv_mt<4, EPI, LN>(a, st, pdl, sms);
+    if (a.M <= 8 || mt_cap == 8) return launch_gemv_mt<8, EPI, LN>(a, st, pdl, sms);
     return launch_gemv_mt<16, EPI, LN>(a, st, pdl, sms);
 }
 
