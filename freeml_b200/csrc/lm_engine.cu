@@ -99,11 +99,10 @@ __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ to
     }
 }
 
-enum GemvEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_ARGMAX = 4, EPI_ARSUM = 5 };
+enum GemvEpi { EPI_STORE = 0, EPI_GELU = 1, EPI_RESID = 2, EPI_QKV = 3, EPI_ARGMAX = 4 };
 
-// Tensor-parallel all-reduce fused into the row-parallel GEMV: flag slots
-// per rank (one per CTA of the GEMV grid) and the wait bound.
-constexpr uint32_t AR_FLAGS = 4096;
+// One-shot all-reduce over NVLink peer memory (tensor parallel decode).
+constexpr uint32_t AR_CTAS = 16;  // CTAs of the all-reduce kernel = flags per rank
 constexpr uint64_t AR_WAIT_NS = 1000000000ull;
 __device__ unsigned int g_tp_timeouts = 0;
 
@@ -139,17 +138,7 @@ struct GemvArgs
     // EPI_ARGMAX
     unsigned long long* keys;
     uint32_t n_off;  // global index of output column 0 (vocabulary-parallel lm_head)
-    // EPI_ARSUM: y = r + sum over ranks of every rank's partial x.W^T.  This
-    // rank writes its partial into every rank's receive buffer (peer stores
-    // over NVLink), raises its flag for this CTA on every rank, waits for
-    // the flags of all ranks for this CTA, then sums the partials in rank
-    // order, so all ranks hold bit-identical results.
-    float* const* peer_recv;     // [world] receive buffers [world][bmax][N]
-    uint32_t* const* peer_flags; // [world] flag arrays [world][AR_FLAGS]
-    const float* recv;           // this rank's receive buffer
-    const uint32_t* flags;       // this rank's flag array
-    const uint32_t* epoch;       // steps completed (tags the flags)
-    uint32_t world, rank, bmax, slot;
+
     // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
     const float* gamma;
 };
@@ -360,12 +349,6 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
                     }
                 }
             }
-            else if constexpr (EPI == EPI_ARSUM)
-            {
-                if (valid)
-                    for (uint32_t r = 0; r < a.world; ++r)
-                        a.peer_recv[r][((uint64_t)a.rank * a.bmax + m) * a.N + n] = v;
-            }
             else if constexpr (EPI == EPI_ARGMAX)
             {
                 // logits (optional) and the per-row argmax over these 4
@@ -384,53 +367,66 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
         }
     }
 
-    if constexpr (EPI == EPI_ARSUM)
+}
+
+// y = resid + sum over ranks (in rank order) of every rank's partial, for the
+// row-parallel projections of a tensor-parallel decode step.  Each rank's
+// projection GEMV wrote its partial into its own buffer `part` (mapped by
+// every rank, double-buffered by use parity so that a rank one all-reduce
+// ahead never overwrites a buffer a slower rank still reads).  CTA b raises
+// flag b on every rank (release, system scope), waits until every rank has
+// raised its flag b (acquire; bounded, expirations counted in
+// g_tp_timeouts), then reads its 1/AR_CTAS slice of every rank's partial
+// over NVLink and sums.  Every rank adds in the same order, so all ranks hold
+// bit-identical activations.
+__global__ void __launch_bounds__(256) ar_oneshot_kernel(float* __restrict__ y, const float* __restrict__ resid,
+                                                         const float* const* parts, uint64_t part_off,
+                                                         uint32_t* const* peer_flags, const uint32_t* flags,
+                                                         const uint32_t* epoch, uint32_t slot, uint32_t world,
+                                                         uint32_t rank, uint64_t n)
+{
+    griddep_wait();  // this rank's partial is complete
+    griddep_launch_dependents();
+    const uint32_t b = blockIdx.x;
+    const uint32_t tag = __ldcg(epoch) * 128u + slot + 1u;
+    if (threadIdx.x < world)
     {
-        // publish this CTA's partial columns on every rank, then wait for
-        // every rank's partial of the same columns (the same CTA there)
-        const uint32_t cta = blockIdx.y * gridDim.x + blockIdx.x;
-        const uint32_t tag = __ldcg(a.epoch) * 128u + a.slot + 1u;
-        __threadfence_system();
-        __syncthreads();
-        if (threadIdx.x == 0)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer_flags[threadIdx.x] + rank * AR_CTAS + b),
+                     "r"(tag)
+                     : "memory");
+        const uint32_t* f = flags + threadIdx.x * AR_CTAS + b;
+        uint64_t t0 = 0;
+        for (uint32_t it = 0;; ++it)
         {
-            for (uint32_t r = 0; r < a.world; ++r)
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.peer_flags[r] + a.rank * AR_FLAGS + cta),
-                             "r"(tag)
-                             : "memory");
-            uint64_t t0 = 0;
-            for (uint32_t r = 0; r < a.world; ++r)
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (v >= tag) break;
+            uint64_t now;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (it == 0) t0 = now;
+            else if (now - t0 > AR_WAIT_NS)
             {
-                const uint32_t* f = a.flags + r * AR_FLAGS + cta;
-                for (uint32_t it = 0;; ++it)
-                {
-                    uint32_t v;
-                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-                    if (v >= tag) break;
-                    uint64_t now;
-                    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-                    if (it == 0) t0 = now;
-                    else if (now - t0 > AR_WAIT_NS)
-                    {
-                        atomicAdd(&g_tp_timeouts, 1u);  // the result is wrong; nothing waits forever
-                        break;
-                    }
-                    __nanosleep(64);
-                }
+                atomicAdd(&g_tp_timeouts, 1u);  // the result is wrong; nothing waits forever
+                break;
             }
+            __nanosleep(32);
         }
-        __syncthreads();
-        for (uint32_t g = blockIdx.y; g < ngroups; g += gridDim.y)
+    }
+    __syncthreads();
+    const uint64_t n4 = n / 4, per = (n4 + gridDim.x - 1) / gridDim.x;
+    const uint64_t lo = b * per, hi = lo + per < n4 ? lo + per : n4;
+    for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
+    {
+        float4 s = reinterpret_cast<const float4*>(resid)[i];
+        for (uint32_t r = 0; r < world; ++r)
         {
-            const int t = threadIdx.x;
-            const uint32_t m = m0 + t / NW, n = g * NW + t % NW;
-            if (t < CNT && m < a.M && n < a.N)
-            {
-                float sum = 0.f;
-                for (uint32_t r = 0; r < a.world; ++r) sum += __ldcg(a.recv + ((uint64_t)r * a.bmax + m) * a.N + n);
-                a.y[(uint64_t)m * a.ldy + n] = a.r[(uint64_t)m * a.ldr + n] + sum;
-            }
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(parts[r] + part_off) + i);
+            s.x += v.x;
+            s.y += v.y;
+            s.z += v.z;
+            s.w += v.w;
         }
+        reinterpret_cast<float4*>(y)[i] = s;
     }
 }
 
@@ -561,10 +557,10 @@ struct fml_lm
     uint32_t hl = 0, dl = 0, fl = 0, h0 = 0, j0 = 0, v0 = 0, vl = 0;
     // fused all-reduce over peer memory (after fml_lm_tp_connect)
     bool ar_fused = false;
-    float* ar_recv = nullptr;        // [world][max_batch][d], written by every rank
-    uint32_t* ar_flags = nullptr;    // [world][AR_FLAGS]
+    float* ar_part = nullptr;        // [2][max_batch][d]: this rank's partial sums, read by every rank
+    uint32_t* ar_flags = nullptr;    // [world][AR_CTAS]
     uint32_t* ar_epoch = nullptr;    // steps completed
-    float** ar_peer_recv = nullptr;  // device arrays of the world's pointers
+    float** ar_peer_part = nullptr;  // device arrays of the world's pointers
     uint32_t** ar_peer_flags = nullptr;
     std::vector<void*> ar_opened;    // peer mappings to close
 
@@ -608,7 +604,7 @@ void free_all(fml_lm* lm)
     lm->comm = nullptr;
     for (void* p : lm->ar_opened) cudaIpcCloseMemHandle(p);
     lm->ar_opened.clear();
-    void* arp[] = {lm->ar_recv, lm->ar_flags, lm->ar_epoch, lm->ar_peer_recv, lm->ar_peer_flags};
+    void* arp[] = {lm->ar_part, lm->ar_flags, lm->ar_epoch, lm->ar_peer_part, lm->ar_peer_flags};
     for (void* p : arp)
         if (p) cudaFree(p);
     for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
@@ -712,8 +708,6 @@ int launch_gemv_mt(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
     if (gy < 1) gy = 1;
     if (gy > ngroups) gy = ngroups;
     if (gy > 65535u) gy = 65535u;
-    if (EPI == EPI_ARSUM)
-        FML_REQUIRE(gx * gy <= AR_FLAGS, "gemv: %u CTAs exceed the all-reduce flag slots", gx * gy);
     return launch_k(gemv_kernel<MT, EPI, LN>, dim3(gx, gy), dim3(128), st, pdl, a);
 }
 
@@ -775,17 +769,19 @@ int all_reduce_sum(fml_lm* lm, float* buf, uint64_t n, cudaStream_t st)
     return FML_OK;
 }
 
-void set_arsum(fml_lm* lm, GemvArgs& a, uint32_t slot)
+// Row-parallel projection + all-reduce over peer memory: the GEMV writes this
+// rank's partial into its shared buffer (parity `slot & 1`), the one-shot
+// kernel sums the world's partials and the residual into y.
+int gemv_allreduce(fml_lm* lm, GemvArgs a, float* y, const float* resid, uint32_t slot, cudaStream_t st, bool pdl)
 {
-    a.peer_recv = lm->ar_peer_recv;
-    a.peer_flags = lm->ar_peer_flags;
-    a.recv = lm->ar_recv;
-    a.flags = lm->ar_flags;
-    a.epoch = lm->ar_epoch;
-    a.world = (uint32_t)lm->tp_world;
-    a.rank = (uint32_t)lm->tp_rank;
-    a.bmax = lm->cfg.max_batch;
-    a.slot = slot;
+    const uint64_t n = (uint64_t)a.M * a.N, off = (uint64_t)(slot & 1u) * lm->cfg.max_batch * lm->cfg.d_model;
+    a.y = lm->ar_part + off;
+    a.ldy = a.N;
+    FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
+    return launch_k(ar_oneshot_kernel, dim3(AR_CTAS), dim3(256), st, pdl, y, resid,
+                    (const float* const*)lm->ar_peer_part, off, (uint32_t* const*)lm->ar_peer_flags,
+                    (const uint32_t*)lm->ar_flags, (const uint32_t*)lm->ar_epoch, slot, (uint32_t)lm->tp_world,
+                    (uint32_t)lm->tp_rank, n);
 }
 
 // Vocabulary-parallel argmax: every rank's packed (value, ~index) keys hold
@@ -875,11 +871,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            if (lm->ar_fused)
-            {
-                set_arsum(lm, a, 2 * l);
-                FML_RC((launch_gemv<EPI_ARSUM, false>(a, st, pdl)));
-            }
+            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, st, pdl));
             else
             {
                 if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
@@ -899,11 +891,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            if (lm->ar_fused)
-            {
-                set_arsum(lm, a, 2 * l + 1);
-                FML_RC((launch_gemv<EPI_ARSUM, false>(a, st, pdl)));
-            }
+            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, st, pdl));
             else
             {
                 if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
@@ -1313,10 +1301,10 @@ int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl
     lm->part = nullptr;
     FML_CUDA_TRY(cudaMalloc(&lm->part, (uint64_t)c.max_batch * lm->hl * lm->S * (lm->hd + 2) * sizeof(float)));
     // buffers the fused all-reduce shares with the other ranks (fml_lm_tp_connect)
-    FML_CUDA_TRY(cudaMalloc(&lm->ar_recv, (uint64_t)world * c.max_batch * c.d_model * sizeof(float)));
-    FML_CUDA_TRY(cudaMalloc(&lm->ar_flags, (uint64_t)world * AR_FLAGS * sizeof(uint32_t)));
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_part, 2ull * c.max_batch * c.d_model * sizeof(float)));
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_flags, (uint64_t)world * AR_CTAS * sizeof(uint32_t)));
     FML_CUDA_TRY(cudaMalloc(&lm->ar_epoch, sizeof(uint32_t)));
-    FML_CUDA_TRY(cudaMemset(lm->ar_flags, 0, (uint64_t)world * AR_FLAGS * sizeof(uint32_t)));
+    FML_CUDA_TRY(cudaMemset(lm->ar_flags, 0, (uint64_t)world * AR_CTAS * sizeof(uint32_t)));
     FML_CUDA_TRY(cudaMemset(lm->ar_epoch, 0, sizeof(uint32_t)));
     lm->step_batch = 0;
     if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
@@ -1327,9 +1315,9 @@ int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl
 int fml_lm_tp_ipc_handles(fml_lm* lm, void* out)
 {
     FML_REQUIRE(lm && out, "fml_lm_tp_ipc_handles: null argument");
-    FML_REQUIRE(lm->tp_world > 1 && lm->ar_recv, "fml_lm_tp_ipc_handles: call fml_lm_set_tensor_parallel first");
+    FML_REQUIRE(lm->tp_world > 1 && lm->ar_part, "fml_lm_tp_ipc_handles: call fml_lm_set_tensor_parallel first");
     cudaIpcMemHandle_t h[2];
-    FML_CUDA_TRY(cudaIpcGetMemHandle(&h[0], lm->ar_recv));
+    FML_CUDA_TRY(cudaIpcGetMemHandle(&h[0], lm->ar_part));
     FML_CUDA_TRY(cudaIpcGetMemHandle(&h[1], lm->ar_flags));
     std::memcpy(out, h, sizeof(h));
     return FML_OK;
@@ -1338,7 +1326,7 @@ int fml_lm_tp_ipc_handles(fml_lm* lm, void* out)
 int fml_lm_tp_connect(fml_lm* lm, const void* all)
 {
     FML_REQUIRE(lm && all, "fml_lm_tp_connect: null argument");
-    FML_REQUIRE(lm->tp_world > 1 && lm->ar_recv, "fml_lm_tp_connect: call fml_lm_set_tensor_parallel first");
+    FML_REQUIRE(lm->tp_world > 1 && lm->ar_part, "fml_lm_tp_connect: call fml_lm_set_tensor_parallel first");
     FML_REQUIRE(!lm->ar_fused, "fml_lm_tp_connect: already connected");
     const int world = lm->tp_world;
     std::vector<float*> recv(world);
@@ -1348,7 +1336,7 @@ int fml_lm_tp_connect(fml_lm* lm, const void* all)
     {
         if (r == lm->tp_rank)
         {
-            recv[r] = lm->ar_recv;
+            recv[r] = lm->ar_part;
             flags[r] = lm->ar_flags;
             continue;
         }
@@ -1360,9 +1348,9 @@ int fml_lm_tp_connect(fml_lm* lm, const void* all)
         lm->ar_opened.push_back(p);
         flags[r] = static_cast<uint32_t*>(p);
     }
-    FML_CUDA_TRY(cudaMalloc(&lm->ar_peer_recv, world * sizeof(float*)));
+    FML_CUDA_TRY(cudaMalloc(&lm->ar_peer_part, world * sizeof(float*)));
     FML_CUDA_TRY(cudaMalloc(&lm->ar_peer_flags, world * sizeof(uint32_t*)));
-    FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_recv, recv.data(), world * sizeof(float*), cudaMemcpyHostToDevice));
+    FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_part, recv.data(), world * sizeof(float*), cudaMemcpyHostToDevice));
     FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_flags, flags.data(), world * sizeof(uint32_t*), cudaMemcpyHostToDevice));
     lm->ar_fused = true;
     if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);

@@ -269,15 +269,16 @@ FML_API int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, 
 FML_API int fml_nccl_unique_id(void* id_out);
 FML_API int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl_id);
 
-/* Fused all-reduce for the decode step's row-parallel projections: after
- * fml_lm_set_tensor_parallel, each rank exports FML_TP_IPC_BYTES of CUDA IPC
- * handles (its receive buffer and flags); the caller gathers them from all
- * ranks in rank order (world * FML_TP_IPC_BYTES) and gives them to
- * fml_lm_tp_connect on every rank.  From then on the proj and mlp GEMVs
- * push their partial sums straight into every rank's receive buffer over
- * NVLink, signal per CTA, and sum the world's partials in rank order in
- * the same kernel (no NCCL call on the decode path; prefill keeps NCCL).
- * Waits are bounded (1 s); fml_lm_tp_error_count reports expirations. */
+/* All-reduce over NVLink peer memory for the decode step's row-parallel
+ * projections: after fml_lm_set_tensor_parallel, each rank exports
+ * FML_TP_IPC_BYTES of CUDA IPC handles (its partial-sum buffer and flags);
+ * the caller gathers them from all ranks in rank order (world *
+ * FML_TP_IPC_BYTES) and gives them to fml_lm_tp_connect on every rank.  From
+ * then on each proj / mlp GEMV writes its partial sums locally and a
+ * one-shot kernel of 16 CTAs signals every rank, waits for every rank, reads
+ * all ranks' partials over NVLink and adds them in rank order plus the
+ * residual (no NCCL call on the decode path; prefill keeps NCCL).  Waits are
+ * bounded (1 s); fml_lm_tp_error_count reports expirations. */
 #define FML_TP_IPC_BYTES 128
 FML_API int fml_lm_tp_ipc_handles(fml_lm* lm, void* out);
 FML_API int fml_lm_tp_connect(fml_lm* lm, const void* all_handles);
