@@ -45,9 +45,9 @@ def parse():
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1 GPUs: tensor parallelism over all ranks (each runs every sequence) "
                          "instead of sequence sharding (BASELINE config 5's scheme)")
-    ap.add_argument("--tp-fused", action="store_true",
-                    help="with --tp: the all-reduce fused into the projection GEMVs over NVLink peer memory "
-                         "instead of NCCL calls (measured slower at TP=2)")
+    ap.add_argument("--tp-nccl", action="store_true",
+                    help="with --tp: NCCL all-reduce calls instead of the one-shot all-reduce over NVLink peer "
+                         "memory")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=3,
                     help="BASELINE config (3 is the headline metric's; 4 and 5 add a timed prefill; 2 is the "
                          "per-operator microbench through the C ABI)")
@@ -374,7 +374,7 @@ def main():
             nid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
         pg.broadcast(nid, src=0)
         lm.set_tensor_parallel(rank, ws, bytes(nid.cpu().numpy().tobytes()))
-        if args.tp_fused:
+        if not args.tp_nccl:
             mine = torch.frombuffer(bytearray(lm.tp_ipc_handles()), dtype=torch.uint8).cuda()
             allh = [torch.empty_like(mine) for _ in range(ws)]
             pg.all_gather(allh, mine)
@@ -510,8 +510,8 @@ def main():
             "vs_baseline": None, "dtype": "f32",
             "data": f"synthetic: seeded N(0,0.02) weights of the config-{CONFIG} architecture, seeded uniform prompts",
             "config": dict(workload_config(ws, B, tp),
-                           allreduce=("fused into the projection GEMVs over NVLink peer memory (prefill: NCCL)"
-                                      if args.tp_fused else "NCCL") if tp else None,
+                           allreduce=("NCCL" if args.tp_nccl else "one-shot kernel over NVLink peer memory "
+                                      "(decode; prefill: NCCL)") if tp else None,
                            engine="fused step kernel" if fused else "per-operation kernels (CUDA graph, PDL)"),
             "gpu_launches": int(launches),
             "clocks": clocks,
