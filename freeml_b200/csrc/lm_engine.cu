@@ -66,6 +66,9 @@ int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int 
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
             int epi, const float* R, cudaStream_t st);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
+int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
+                             uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
+                             float scale, cudaStream_t st);
 
 // ---------------------------------------------------------------- kernels --
 
@@ -1217,13 +1220,9 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
         qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * dl, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, dl, lm->hd,
                                                                                c.context, lm->seq_stride);
         FML_LAUNCH_CHECK();
-        // prefill attention: one query row per (b, t), the whole causal key
-        // range in one CTA, launched in slabs of at most 65535 rows
-        for (uint32_t r0 = 0; r0 < R; r0 += 65535u)
-        {
-            FML_CUDA_TRY(cudaMemsetAsync(lm->grab + l, 0, sizeof(uint32_t), st));
-            FML_RC(launch_attention(lm, l, r0, R - r0 < 65535u ? R - r0 : 65535u, nullptr, P, 1, c.context, st));
-        }
+        // prefill attention: 64-query tiles sharing each K/V tile
+        FML_RC(launch_prefill_attention(lm->q, dl, kc, vc, lm->seq_stride, c.context, lm->att, dl, batch, lm->hl, P,
+                                        lm->hd, 1.0f / sqrtf((float)lm->hd), st));
         // buf = x + att . Wproj^T ; hid = gelu(LN1(buf) . Wfc^T) ; x = buf + hid . Wmlp^T
         FML_RC(prefill_gemm(lm, lm->buf, lm->att, lm->wproj[l], (int)R, (int)d, (int)dl, resid_epi, lm->x, st));
         if (tp) FML_RC(all_reduce_sum(lm, lm->buf, (uint64_t)R * d, st));

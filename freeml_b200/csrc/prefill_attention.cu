@@ -1,0 +1,219 @@
+// Causal attention over whole prompts (the engine's prefill):
+// CausalSelfAttentionLayer::Forward (CausalSelfAttentionLayer.h:424-499) for
+// all P rows of every sequence and head, Q K^T * 1/sqrt(hd) with the causal
+// mask, softmax, times V, as tiles: one CTA per (64 query rows, head,
+// sequence) walks the key tiles 0..(its last row) with an online softmax, so
+// every K/V row of a (sequence, head) is read once per 64 queries instead of
+// once per query.
+//
+// CTA = 256 threads, 16 x 16.  Thread (ty, tx) owns query rows
+// ty + 16i and keys tx + 16j (i, j < 4) of the 64 x 64 score tile, and output
+// columns tx + 16c of its rows.  Strided ownership keeps the float4 reads of
+// the padded Q and K tiles bank-conflict free.  A row's 64 scores live in the
+// 16 lanes of one half-warp: max and sum are 4-step shuffles.  P goes through
+// shared memory for the P . V product.  fp32 throughout; expf.
+#include <cmath>
+
+#include "fml_common.cuh"
+
+namespace fml {
+namespace {
+
+constexpr int PQ = 64, PK = 64;
+
+template <int HD>
+__global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __restrict__ q, uint32_t ldq,
+                                                                const float* __restrict__ kc,
+                                                                const float* __restrict__ vc, uint64_t seq_stride,
+                                                                uint32_t C, float* __restrict__ out, uint32_t ldo,
+                                                                uint32_t P, float scale)
+{
+    constexpr int HP = HD + 4;  // padded row (floats)
+    constexpr int OC = HD / 16; // output columns per thread
+    extern __shared__ __align__(16) float sm[];
+    float* Qs = sm;              // [PQ][HP]
+    float* Ks = Qs + PQ * HP;    // [PK][HP]
+    float* Vs = Ks + PK * HP;    // [PK][HP]
+    float* Ps = Vs + PK * HP;    // [PQ][PK + 4]
+
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const uint32_t qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const uint32_t q0 = qt * PQ;
+    const uint32_t nq = P - q0 < (uint32_t)PQ ? P - q0 : (uint32_t)PQ;
+    const float* kbase = kc + (uint64_t)b * seq_stride + (uint64_t)h * C * HD;
+    const float* vbase = vc + (uint64_t)b * seq_stride + (uint64_t)h * C * HD;
+
+    // Q tile, pre-scaled
+    for (int i = tid; i < PQ * (HD / 4); i += 256)
+    {
+        const int r = i / (HD / 4), c = i % (HD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if ((uint32_t)r < nq)
+        {
+            v = *reinterpret_cast<const float4*>(q + (uint64_t)(b * P + q0 + r) * ldq + h * HD + c * 4);
+            v.x *= scale;
+            v.y *= scale;
+            v.z *= scale;
+            v.w *= scale;
+        }
+        *reinterpret_cast<float4*>(Qs + r * HP + c * 4) = v;
+    }
+
+    float mrow[4], lrow[4], o[4][OC];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        mrow[i] = -INFINITY;
+        lrow[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < OC; ++c) o[i][c] = 0.f;
+    }
+
+    const uint32_t klast = q0 + nq - 1;  // last key any row of this tile sees
+    for (uint32_t k0 = 0; k0 <= klast; k0 += PK)
+    {
+        __syncthreads();  // previous tile's K / V / P readers are done
+        for (int i = tid; i < PK * (HD / 4); i += 256)
+        {
+            const int r = i / (HD / 4), c = i % (HD / 4);
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (k0 + r <= klast)
+            {
+                kv = *reinterpret_cast<const float4*>(kbase + (uint64_t)(k0 + r) * HD + c * 4);
+                vv = *reinterpret_cast<const float4*>(vbase + (uint64_t)(k0 + r) * HD + c * 4);
+            }
+            *reinterpret_cast<float4*>(Ks + r * HP + c * 4) = kv;
+            *reinterpret_cast<float4*>(Vs + r * HP + c * 4) = vv;
+        }
+        __syncthreads();
+
+        // scores for rows ty + 16i, keys tx + 16j
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+        for (int e = 0; e < HD; e += 4)
+        {
+            float4 qv[4], kv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (ty + 16 * i) * HP + e);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(Ks + (tx + 16 * j) * HP + e);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                {
+                    float a = s[i][j];
+                    a = fmaf(qv[i].x, kv[j].x, a);
+                    a = fmaf(qv[i].y, kv[j].y, a);
+                    a = fmaf(qv[i].z, kv[j].z, a);
+                    a = fmaf(qv[i].w, kv[j].w, a);
+                    s[i][j] = a;
+                }
+        }
+        // causal mask, online softmax per row (the row's 16 lanes)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            const uint32_t qi = q0 + ty + 16 * i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+            {
+                const uint32_t kj = k0 + tx + 16 * j;
+                if (kj > qi) s[i][j] = -INFINITY;
+                mx = fmaxf(mx, s[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL_MASK, mx, off));
+            const float mnew = fmaxf(mrow[i], mx);
+            // every row sees key k0 of its last tile, so mnew is finite; the
+            // guard only keeps the arithmetic finite if that ever changed
+            const float base = mnew == -INFINITY ? 0.f : mnew;
+            const float corr = expf(mrow[i] - base);
+            float ps = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+            {
+                const float p = expf(s[i][j] - base);
+                ps += p;
+                Ps[(ty + 16 * i) * (PK + 4) + tx + 16 * j] = p;
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) ps += __shfl_xor_sync(FULL_MASK, ps, off);
+            lrow[i] = fmaf(lrow[i], corr, ps);
+#pragma unroll
+            for (int c = 0; c < OC; ++c) o[i][c] *= corr;
+            mrow[i] = mnew;
+        }
+        __syncthreads();
+        // O[rows][cols] += P[rows][keys] . V[keys][cols]
+        const uint32_t kn = klast - k0 + 1 < (uint32_t)PK ? klast - k0 + 1 : (uint32_t)PK;
+        for (uint32_t k = 0; k < kn; ++k)
+        {
+            float pv[4], vv[OC];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pv[i] = Ps[(ty + 16 * i) * (PK + 4) + k];
+#pragma unroll
+            for (int c = 0; c < OC; ++c) vv[c] = Vs[k * HP + tx + 16 * c];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int c = 0; c < OC; ++c) o[i][c] = fmaf(pv[i], vv[c], o[i][c]);
+        }
+    }
+
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        const uint32_t r = ty + 16 * i;
+        if (r >= nq) continue;
+        const float inv = 1.0f / lrow[i];
+        float* dst = out + (uint64_t)(b * P + q0 + r) * ldo + h * HD;
+#pragma unroll
+        for (int c = 0; c < OC; ++c) dst[tx + 16 * c] = o[i][c] * inv;
+    }
+}
+
+template <int HD>
+int launch_hd(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride, uint32_t C,
+              float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, float scale, cudaStream_t st)
+{
+    const size_t smem = sizeof(float) * (3 * PQ * (HD + 4) + PQ * (PK + 4));
+    static bool attr = false;
+    if (!attr)
+    {
+        FML_CUDA_TRY(
+            cudaFuncSetAttribute(prefill_attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr = true;
+    }
+    const dim3 grid((P + PQ - 1) / PQ, H, B);
+    prefill_attention_kernel<HD><<<grid, 256, smem, st>>>(q, ldq, kc, vc, seq_stride, C, out, ldo, P, scale);
+    FML_LAUNCH_CHECK();
+    return FML_OK;
+}
+
+}  // namespace
+
+// Prefill attention for rows (b, t), t < P, of B sequences and H heads:
+// q / out [B*P x ld] (head h at columns h*hd), keys and values of sequence b,
+// head h at kc/vc + b*seq_stride + h*C*hd (rows 0..P-1 filled).
+int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
+                             uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
+                             float scale, cudaStream_t st)
+{
+    FML_REQUIRE(B <= 65535u && H <= 65535u, "prefill attention: %u sequences x %u heads", B, H);
+    FML_REQUIRE(ldq % 4 == 0 && ldo % 4 == 0, "prefill attention: row strides must be multiples of 4");
+    switch (hd)
+    {
+    case 32: return launch_hd<32>(q, ldq, kc, vc, seq_stride, C, out, ldo, B, H, P, scale, st);
+    case 64: return launch_hd<64>(q, ldq, kc, vc, seq_stride, C, out, ldo, B, H, P, scale, st);
+    case 128: return launch_hd<128>(q, ldq, kc, vc, seq_stride, C, out, ldo, B, H, P, scale, st);
+    default: return set_error(FML_ERR_UNSUPPORTED, "prefill attention: head dim %u", hd);
+    }
+}
+
+}  // namespace fml
