@@ -92,6 +92,7 @@ __device__ int g_attention_timeouts;  // wait limits hit (read by fml_device_err
 struct AttnUnit
 {
     uint32_t r, b, begin, end, nsplit;
+    uint32_t newest;  // key written by the previous kernel (decode), else none
 };
 
 __device__ __forceinline__ AttnUnit attention_unit(const AttnArgs& a, uint32_t r, uint32_t s)
@@ -99,8 +100,9 @@ __device__ __forceinline__ AttnUnit attention_unit(const AttnArgs& a, uint32_t r
     AttnUnit t;
     t.r = r;
     uint32_t len;
+    t.newest = 0xffffffffu;
     if (a.lens) { t.b = r; len = a.lens[r]; }
-    else if (a.pos) { t.b = r; len = a.pos[r] + 1; }
+    else if (a.pos) { t.b = r; len = a.pos[r] + 1; t.newest = len - 1; }
     else { t.b = r / a.P; len = r % a.P + 1; }
     // keys per split: fixed, or an even share of this row's keys
     const uint32_t chunk = a.chunk ? a.chunk : max(32u, ((len + a.S - 1) / a.S + 31u) & ~31u);
@@ -145,30 +147,69 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
     const uint32_t h = blockIdx.x, r = a.row0 + blockIdx.y, s = blockIdx.z;
 
     griddep_launch_dependents();
-    griddep_wait();  // q and the newest K/V rows come from the previous kernel
 
+    // Positions were set by the previous step's last kernel, which finished
+    // before this step's first (non-overlapped) kernel began, and every cached
+    // row below the newest was written by earlier steps: this CTA's first
+    // batch of K/V rows is requested before waiting for the previous kernel.
+    // Only the newest row (key len - 1) comes from that kernel; it is
+    // re-read after the wait if the first batch holds it.
     const AttnUnit cu = attention_unit(a, r, s);
     const float* K = a.kc + (uint64_t)cu.b * a.seq_stride + (uint64_t)h * a.C * HD + lig * 4;
     const float* V = a.vc + (uint64_t)cu.b * a.seq_stride + (uint64_t)h * a.C * HD + lig * 4;
+    constexpr uint32_t STEP = 4 * KPW;  // keys per CTA step (4 warps)
+    const uint32_t last = cu.end > 0 ? cu.end - 1 : 0;
+    const uint32_t kw0 = cu.begin + warp * KPW;
+    const uint32_t newest = cu.newest;
+    // prefill rows (no positions, no lengths) read keys the previous kernel
+    // wrote: no early loads there
+    const bool early = a.pos != nullptr || a.lens != nullptr;
+    if (!early) griddep_wait();
+    float4 kk[U], vv[U];
+    if (kw0 < cu.end)
+    {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const uint32_t j = min(kw0 + grp + u * STEP, last);
+            kk[u] = *reinterpret_cast<const float4*>(K + (uint64_t)j * HD);
+            vv[u] = *reinterpret_cast<const float4*>(V + (uint64_t)j * HD);
+        }
+    }
+    if (early) griddep_wait();  // q and the newest K/V rows come from the previous kernel
+    if (kw0 < cu.end)
+    {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const uint32_t j = min(kw0 + grp + u * STEP, last);
+            if (j == newest)
+            {
+                kk[u] = __ldcg(reinterpret_cast<const float4*>(K + (uint64_t)j * HD));
+                vv[u] = __ldcg(reinterpret_cast<const float4*>(V + (uint64_t)j * HD));
+            }
+        }
+    }
+
     float4 q = *reinterpret_cast<const float4*>(a.q + (uint64_t)r * a.ldq + h * HD + lig * 4);
     q.x *= a.scale; q.y *= a.scale; q.z *= a.scale; q.w *= a.scale;
 
     float m = -INFINITY, l = 0.0f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    constexpr uint32_t STEP = 4 * KPW;  // keys per CTA step (4 warps)
-    const uint32_t last = cu.end > 0 ? cu.end - 1 : 0;
     // the trip count depends on the warp only (never on the lane group): the
     // loop body has full-warp shuffles, so every lane must run every step
-    for (uint32_t kw = cu.begin + warp * KPW; kw < cu.end; kw += U * STEP)
+    for (uint32_t kw = kw0; kw < cu.end; kw += U * STEP)
     {
         const uint32_t kb = kw + grp;  // this group's first key of the step
-        float4 kk[U], vv[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u)
+        if (kw != kw0)
         {
-            const uint32_t j = min(kb + u * STEP, last);  // clamped in range, masked below
-            kk[u] = *reinterpret_cast<const float4*>(K + (uint64_t)j * HD);
-            vv[u] = *reinterpret_cast<const float4*>(V + (uint64_t)j * HD);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+                const uint32_t j = min(kb + u * STEP, last);  // clamped in range, masked below
+                kk[u] = *reinterpret_cast<const float4*>(K + (uint64_t)j * HD);
+                vv[u] = *reinterpret_cast<const float4*>(V + (uint64_t)j * HD);
+            }
         }
         float sc[U];
         float smax = -INFINITY;

@@ -706,6 +706,8 @@ int launch_gemv_mt(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
     const unsigned gx = (a.M + MT - 1) / MT;
     const unsigned ngroups = (a.N + 3) / 4;
     // one wave: every CTA resident at once, each walking several column groups
+    // (measured: capping the CTAs per SM to leave room for the next kernel's
+    // early-launched CTAs only slows the step)
     const unsigned slots = (unsigned)(gemv_blocks_per_sm<MT, EPI, LN>() * sms);
     unsigned gy = slots / gx;
     if (gy < 1) gy = 1;
