@@ -73,6 +73,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
     return false;
 }
 
+#ifdef FML_TIMELINE
+int timeline_bind_attention(TimelineRec* p, uint32_t cap) { return timeline_bind_unit(p, cap); }
+#endif
+
 __device__ int g_attention_timeouts;  // wait limits hit (read by fml_device_error_count)
 
 // Causal attention for one query row over the cached keys 0..len-1
@@ -177,6 +181,7 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
         }
     }
     if (early) griddep_wait();  // q and the newest K/V rows come from the previous kernel
+    FML_TIMELINE_MARK(1);
     if (kw0 < cu.end)
     {
 #pragma unroll
@@ -241,6 +246,7 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
         }
     }
 
+    FML_TIMELINE_MARK(2);
     // merge the KPW groups of the warp (xor across groups)
 #pragma unroll
     for (int o = G; o < 32; o <<= 1)

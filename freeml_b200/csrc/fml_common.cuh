@@ -93,12 +93,24 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 #ifdef FML_TIMELINE
 struct TimelineRec
 {
-    unsigned long long start, end;
+    unsigned long long start, mark1, mark2, end;  // marks: 0 when not set
     uint32_t kernel, cta;
 };
-extern __device__ TimelineRec* g_fml_timeline;
-extern __device__ uint32_t g_fml_timeline_cap;
-extern __device__ uint32_t g_fml_timeline_n;
+// one ring per translation unit (device variables are not shared across
+// units without relocatable device code); the host binds each to its own
+// part of the caller's buffer
+static __device__ TimelineRec* g_fml_timeline = nullptr;
+static __device__ uint32_t g_fml_timeline_cap = 0;
+static __device__ uint32_t g_fml_timeline_n = 0;
+static inline int timeline_bind_unit(TimelineRec* p, uint32_t cap)
+{
+    const uint32_t zero = 0;
+    if (cudaMemcpyToSymbol(g_fml_timeline, &p, sizeof(p)) != cudaSuccess) return 2;
+    if (cudaMemcpyToSymbol(g_fml_timeline_cap, &cap, sizeof(cap)) != cudaSuccess) return 2;
+    if (cudaMemcpyToSymbol(g_fml_timeline_n, &zero, sizeof(zero)) != cudaSuccess) return 2;
+    return 0;
+}
+int timeline_bind_attention(TimelineRec* p, uint32_t cap);
 __device__ __forceinline__ unsigned long long fml_globaltimer()
 {
     unsigned long long t;
@@ -107,24 +119,30 @@ __device__ __forceinline__ unsigned long long fml_globaltimer()
 }
 struct TimelineScope
 {
-    unsigned long long t0;
+    unsigned long long t0, t1 = 0, t2 = 0;
     uint32_t id;
     __device__ explicit TimelineScope(uint32_t k) : t0(fml_globaltimer()), id(k) {}
+    __device__ void mark(int i) { (i == 1 ? t1 : t2) = fml_globaltimer(); }
     __device__ ~TimelineScope()
     {
         if (threadIdx.x == 0 && threadIdx.y == 0 && g_fml_timeline)
         {
             const uint32_t i = atomicAdd(&g_fml_timeline_n, 1u);
             if (i < g_fml_timeline_cap)
-                g_fml_timeline[i] = {t0, fml_globaltimer(), id,
+                g_fml_timeline[i] = {t0, t1, t2, fml_globaltimer(), id,
                                      blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)};
         }
     }
 };
 #define FML_TIMELINE_SCOPE(k) ::fml::TimelineScope _fml_tl_scope(k)
+// stamp 1 (typically: past griddepcontrol.wait) or 2 (prologue done)
+#define FML_TIMELINE_MARK(i) _fml_tl_scope.mark(i)
 #else
 #define FML_TIMELINE_SCOPE(k) \
     do {                      \
+    } while (0)
+#define FML_TIMELINE_MARK(i) \
+    do {                     \
     } while (0)
 #endif
 

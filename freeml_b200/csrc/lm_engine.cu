@@ -41,19 +41,14 @@
 #include "fml_common.cuh"
 
 #ifdef FML_TIMELINE
-namespace fml {
-__device__ TimelineRec* g_fml_timeline = nullptr;
-__device__ uint32_t g_fml_timeline_cap = 0;
-__device__ uint32_t g_fml_timeline_n = 0;
-}  // namespace fml
+// debug builds only: bind (buf, cap) as the kernels' timeline ring, this
+// unit's kernels in the first half and the attention unit's in the second
 extern "C" __attribute__((visibility("default"))) int fml_debug_timeline(void* buf, uint32_t cap)
 {
     fml::TimelineRec* p = static_cast<fml::TimelineRec*>(buf);
-    const uint32_t zero = 0;
-    if (cudaMemcpyToSymbol(fml::g_fml_timeline, &p, sizeof(p)) != cudaSuccess) return 2;
-    if (cudaMemcpyToSymbol(fml::g_fml_timeline_cap, &cap, sizeof(cap)) != cudaSuccess) return 2;
-    if (cudaMemcpyToSymbol(fml::g_fml_timeline_n, &zero, sizeof(zero)) != cudaSuccess) return 2;
-    return 0;
+    const uint32_t half = cap / 2;
+    if (fml::timeline_bind_unit(p, half)) return 2;
+    return fml::timeline_bind_attention(p ? p + half : nullptr, cap - half);
 }
 #endif
 
@@ -82,6 +77,7 @@ __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ to
     FML_TIMELINE_SCOPE(1);
     griddep_launch_dependents();
     griddep_wait();
+    FML_TIMELINE_MARK(1);
     // the step's first kernel clears the per-layer attention work counters
     if (blockIdx.x == 0)
         for (uint32_t i = threadIdx.x; i < nzero; i += blockDim.x) zero[i] = 0u;
@@ -144,7 +140,50 @@ struct GemvArgs
 
     // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
     const float* gamma;
+
+    // L2 prefetch of bytes the step reads later, issued before
+    // griddepcontrol.wait: units [pf_lo, pf_hi) of one layer's cached K/V
+    // rows -- rows [0, min(pf_pos[b] + pf_extra, pf_C)) of every (sequence b,
+    // head), PF_CHUNK bytes per unit (pf_kc null: none)
+    const float* pf_kc;
+    const float* pf_vc;
+    const uint32_t* pf_pos;
+    uint32_t pf_B, pf_H, pf_C, pf_hd, pf_extra;
+    uint32_t pf_lo, pf_hi;
+    uint64_t pf_seq_stride;
 };
+
+constexpr uint32_t PF_CHUNK = 16384;  // bytes per bulk L2 prefetch
+
+// Asynchronous prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes
+// a multiple of 16); no registers or shared memory are held while it lands.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// The GEMV's share of a layer's K/V prefetch (see GemvArgs), spread over
+// every thread of the grid.
+__device__ __forceinline__ void gemv_prefetch(const GemvArgs& a)
+{
+    if (a.pf_kc)
+    {
+        const uint64_t row_bytes = (uint64_t)a.pf_hd * sizeof(float);
+        const uint32_t nch = (uint32_t)((a.pf_C * row_bytes + PF_CHUNK - 1) / PF_CHUNK);
+        const uint32_t nthreads = blockDim.x * gridDim.x * gridDim.y;
+        for (uint32_t u = a.pf_lo + threadIdx.x + blockDim.x * (blockIdx.x + gridDim.x * blockIdx.y); u < a.pf_hi;
+             u += nthreads)
+        {
+            const uint32_t j = u % nch, bh2 = u / nch, bh = bh2 >> 1;
+            const uint32_t b = bh / a.pf_H, h = bh % a.pf_H;
+            const uint64_t bytes = (uint64_t)min(a.pf_pos[b] + a.pf_extra, a.pf_C) * row_bytes;
+            const uint64_t o = (uint64_t)j * PF_CHUNK;
+            if (b >= a.pf_B || o >= bytes) continue;
+            const float* base = (bh2 & 1 ? a.pf_vc : a.pf_kc) + (uint64_t)b * a.pf_seq_stride + (uint64_t)h * a.pf_C * a.pf_hd;
+            prefetch_l2(reinterpret_cast<const char*>(base) + o, (uint32_t)min((uint64_t)PF_CHUNK, bytes - o));
+        }
+    }
+}
 
 // y[m, n] = sum_k xn[m, k] W[n, k] for the small-M (decode) shapes, where
 // xn = x, or LayerNormOp(x) with gamma (LN = true: LayerNorm.h:148-165 fused
@@ -190,8 +229,10 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
     for (int j = 0; j < NW; ++j)
         wv[j] = have_first ? ldw(wrow[j] + k_first) : make_float4(0, 0, 0, 0);
 
+    gemv_prefetch(a);
     griddep_launch_dependents();
     griddep_wait();
+    FML_TIMELINE_MARK(1);
 
     if constexpr (LN)
     {
@@ -249,6 +290,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
         __syncthreads();
     }
 
+    FML_TIMELINE_MARK(2);
     // column groups of this CTA: n0 = 4 * (blockIdx.y + i * gridDim.y)
     const uint32_t ngroups = (a.N + NW - 1) / NW;
     for (uint32_t g = blockIdx.y; g < ngroups; g += gridDim.y)
@@ -372,6 +414,227 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
 
 }
 
+// Named barrier over `n` threads (a team of warps inside the CTA).
+__device__ __forceinline__ void team_sync(uint32_t id, uint32_t n)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+#ifndef FML_GEMV_SB
+#define FML_GEMV_SB 4
+#endif
+
+// Decode GEMV, team layout: y[m, n] = sum_k xn[m, k] W[n, k] for MT rows per
+// CTA, xn = x or LayerNormOp(x) with gamma (LayerNorm.h:148-165, two-pass
+// mean / biased variance).
+//
+// The CTA stages its MT rows of x once in shared memory, normalised in place
+// when LN (warp w owns rows w, w + 4, ...), so the per-column-group work is
+// only loads and fused multiply-adds.  Its 4 warps form 4 / KW teams; a team
+// of KW warps owns one group of 4 output columns at a time and splits K
+// between its 32 * KW lanes in float4 slices (lane k = 4 * (32 kw + lane) +
+// 128 KW s), so each lane accumulates MT x 4 sums over S = K / (128 KW)
+// slices before one warp transpose-reduce (and, for KW > 1, one sum of the
+// team's warps through shared memory behind a named barrier).  W rows stream
+// through SB register slots: a slot is refilled with the next slice of the
+// group (or the next group's) as soon as it has been used, so SB slices per
+// lane are always in flight; the first SB are requested before
+// griddepcontrol.wait.  Measured against the one-group-per-CTA layout (every
+// output a 128-thread reduction, the LayerNorm redone per column group):
+// the per-group instruction count, not memory, bounded that kernel.
+template <int MT, int KW, int EPI, bool LN>
+__global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
+{
+    FML_TIMELINE_SCOPE(10 + EPI);
+    constexpr int NW = 4;              // output columns per group
+    constexpr int CNT = MT * NW;       // sums per lane (16 or 32)
+    constexpr int TEAMS = 4 / KW;
+    constexpr int SB = FML_GEMV_SB;    // W slices in flight per lane
+    constexpr uint32_t KSTEP = 128u * KW;  // K covered by one slice of the team
+    static_assert(CNT == 16 || CNT == 32, "MT must be 4 or 8");
+    extern __shared__ __align__(16) float xs[];  // [MT][K] x rows, then (LN) gamma [K]
+    __shared__ float red[2][TEAMS][KW][CNT];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int team = warp / KW, kw = warp % KW;
+    const uint32_t m0 = blockIdx.x * MT;
+    const uint32_t K = a.K;
+    const uint32_t k_lane = 4u * (32u * kw + lane);
+    const uint32_t S = (K + KSTEP - 1) / KSTEP;          // slices per lane
+    const uint32_t nchunk = (S + SB - 1) / SB;
+    const uint32_t ngroups = (a.N + NW - 1) / NW;
+    const uint32_t gstride = gridDim.y * TEAMS;
+    uint32_t g = blockIdx.y * TEAMS + team;
+
+    // slice (group gg, slice s) of this lane: NW float4 of W, zero past K or
+    // past the last group
+    float4 wv[SB][NW];
+    auto load_slot = [&](int b, uint32_t gg, uint32_t s) {
+        const uint32_t k = k_lane + s * KSTEP;
+        const bool ok = gg < ngroups && s < S && k < K;
+#pragma unroll
+        for (int j = 0; j < NW; ++j)
+            wv[b][j] = ok ? ldw(a.w + (uint64_t)min(gg * NW + j, a.N - 1) * K + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+#pragma unroll
+    for (int b = 0; b < SB; ++b) load_slot(b, g, b);
+
+    // gamma is a weight: staged before the wait (after the x rows in shared memory)
+    const float4* gs4 = reinterpret_cast<const float4*>(xs + (uint64_t)MT * K);
+    if constexpr (LN)
+    {
+        const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
+        for (uint32_t c = tid; c < K / 4; c += 128) const_cast<float4*>(gs4)[c] = g4[c];
+    }
+
+    gemv_prefetch(a);
+    griddep_launch_dependents();
+    griddep_wait();
+    FML_TIMELINE_MARK(1);
+
+    // warp w stages rows w, w + 4, ... (zero past M) and, for LN, normalises
+    // them in place; a lane only rereads the float4s it wrote itself
+    const float invK = 1.0f / (float)K;
+    for (int m = warp; m < MT; m += 4)
+    {
+        const bool in = m0 + m < a.M;
+        const float4* src = reinterpret_cast<const float4*>(a.x + (uint64_t)(in ? m0 + m : 0) * a.ldx);
+        float4* row = reinterpret_cast<float4*>(xs + (uint64_t)m * K);
+        float sum = 0.f;
+        for (uint32_t c = lane; c < K / 4; c += 32)
+        {
+            const float4 v = in ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            row[c] = v;
+            sum += (v.x + v.y) + (v.z + v.w);
+        }
+        if constexpr (LN)
+        {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(FULL_MASK, sum, o);
+            const float mean = sum * invK;
+            float q = 0.f;
+            for (uint32_t c = lane; c < K / 4; c += 32)
+            {
+                const float4 v = row[c];
+                const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+                q = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, fmaf(d3, d3, q))));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(FULL_MASK, q, o);
+            const float rstd = 1.0f / sqrtf(fmaf(q, invK, 1e-5f));
+            for (uint32_t c = lane; c < K / 4; c += 32)
+            {
+                float4 v = row[c];
+                const float4 gm = gs4[c];
+                v.x = (v.x - mean) * rstd * gm.x;
+                v.y = (v.y - mean) * rstd * gm.y;
+                v.z = (v.z - mean) * rstd * gm.z;
+                v.w = (v.w - mean) * rstd * gm.w;
+                row[c] = v;
+            }
+        }
+    }
+    __syncthreads();
+    FML_TIMELINE_MARK(2);
+
+    const uint32_t hd_shift = EPI == EPI_QKV ? (uint32_t)(__ffs(a.hd) - 1) : 0u;
+    uint32_t parity = 0;
+    // the loop runs per team; its trip count is the same for the team's warps
+    for (; g < ngroups; g += gstride, parity ^= 1u)
+    {
+        float acc[CNT];
+#pragma unroll
+        for (int i = 0; i < CNT; ++i) acc[i] = 0.0f;
+        for (uint32_t c = 0; c < nchunk; ++c)
+        {
+#pragma unroll
+            for (int b = 0; b < SB; ++b)
+            {
+                const uint32_t s = c * SB + b;
+                const uint32_t k = k_lane + s * KSTEP;
+                if (s < S && k < K)
+                {
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                    {
+                        const float4 xv = *reinterpret_cast<const float4*>(xs + (uint64_t)m * K + k);
+#pragma unroll
+                        for (int j = 0; j < NW; ++j)
+                        {
+                            float t = acc[m * NW + j];
+                            t = fmaf(xv.x, wv[b][j].x, t);
+                            t = fmaf(xv.y, wv[b][j].y, t);
+                            t = fmaf(xv.z, wv[b][j].z, t);
+                            t = fmaf(xv.w, wv[b][j].w, t);
+                            acc[m * NW + j] = t;
+                        }
+                    }
+                }
+                // refill the slot: this group's slice s + SB, else the next
+                // group's slice b
+                if (c + 1 < nchunk) load_slot(b, g, s + SB);
+                else load_slot(b, g + gstride, b);
+            }
+        }
+
+        warp_transpose_reduce<CNT>(acc, lane);
+        const int idx = reduce_base<CNT>(lane);  // the sum this lane holds
+        float v = acc[0];
+        if constexpr (KW > 1)
+        {
+            if (reduce_owner<CNT>(lane)) red[parity][team][kw][idx] = v;
+            team_sync(1 + team, 32 * KW);
+            if (kw != 0) continue;
+            v = red[parity][team][0][idx];
+#pragma unroll
+            for (int i = 1; i < KW; ++i) v += red[parity][team][i][idx];
+        }
+
+        const uint32_t m = m0 + idx / NW, n = g * NW + idx % NW;
+        const bool valid = reduce_owner<CNT>(lane) && m < a.M && n < a.N;
+        if constexpr (EPI == EPI_STORE)
+        {
+            if (valid) a.y[(uint64_t)m * a.ldy + n] = v;
+        }
+        else if constexpr (EPI == EPI_GELU)
+        {
+            if (valid) a.y[(uint64_t)m * a.ldy + n] = gelu_exact(v);
+        }
+        else if constexpr (EPI == EPI_RESID)
+        {
+            if (valid) a.y[(uint64_t)m * a.ldy + n] = a.r[(uint64_t)m * a.ldr + n] + v;
+        }
+        else if constexpr (EPI == EPI_QKV)
+        {
+            if (valid)
+            {
+                if (n < a.d) a.q[(uint64_t)m * a.d + n] = v;
+                else
+                {
+                    const uint32_t cc = n < 2 * a.d ? n - a.d : n - 2 * a.d;
+                    float* cache = n < 2 * a.d ? a.kc : a.vc;
+                    cache[(uint64_t)m * a.seq_stride + ((uint64_t)(cc >> hd_shift) * a.C + a.pos[m]) * a.hd +
+                          (cc & (a.hd - 1))] = v;
+                }
+            }
+        }
+        else if constexpr (EPI == EPI_ARGMAX)
+        {
+            // logits (optional), then the max key over the group's 4 columns
+            // of each row: the lanes holding row m's 4 sums differ in the
+            // lane bits that carry idx % 4
+            if (valid && a.y) a.y[(uint64_t)m * a.ldy + n] = v;
+            unsigned long long key = valid ? argmax_key(v, n + a.n_off) : 0ull;
+            constexpr int sh = CNT == 16 ? 1 : 0;
+            unsigned long long o1 = __shfl_xor_sync(FULL_MASK, key, 1 << sh);
+            key = o1 > key ? o1 : key;
+            unsigned long long o2 = __shfl_xor_sync(FULL_MASK, key, 2 << sh);
+            key = o2 > key ? o2 : key;
+            if (valid && idx % NW == 0) atomicMax(a.keys + m, key);
+        }
+    }
+}
+
 // y = resid + sum over ranks (in rank order) of every rank's partial, for the
 // row-parallel projections of a tensor-parallel decode step.  Each rank's
 // projection GEMV wrote its partial into its own buffer `part` (mapped by
@@ -458,6 +721,7 @@ __global__ void finalize_kernel(unsigned long long* keys, uint32_t* pending, uin
 {
     FML_TIMELINE_SCOPE(30);
     griddep_wait();
+    FML_TIMELINE_MARK(1);
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b == 0 && epoch) *epoch += 1u;
     if (b >= B) return;
@@ -545,6 +809,9 @@ struct fml_lm
 
     uint32_t batch = 0;                // active sequences
     std::vector<uint32_t> hpos;        // host mirror of positions
+
+    // L2 prefetch in the decode step (GemvArgs::pf_*), sized against the L2
+    uint64_t l2_bytes = 0;
 
     // graph / programmatic dependent launch
     bool use_graph = true;
@@ -667,12 +934,12 @@ int collect_profile(fml_lm* lm)
 // start while the previous one in the stream finishes (it calls
 // griddepcontrol.wait before reading that kernel's output).
 template <typename... KArgs, typename... Args>
-int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args... args)
+int launch_ks(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -683,6 +950,12 @@ int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, boo
     if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "cudaLaunchKernelEx: %s", cudaGetErrorString(e));
     FML_LAUNCH_CHECK();
     return FML_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args... args)
+{
+    return launch_ks(kern, grid, block, 0, st, pdl, std::forward<Args>(args)...);
 }
 
 // Resident CTAs per SM of a gemv instantiation (cached per instantiation).
@@ -716,6 +989,53 @@ int launch_gemv_mt(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
     return launch_k(gemv_kernel<MT, EPI, LN>, dim3(gx, gy), dim3(128), st, pdl, a);
 }
 
+constexpr size_t GEMV_TEAM_MAX_SMEM = 64 * 1024;  // staged x rows per CTA
+
+template <int MT, int KW, int EPI, bool LN>
+int launch_gemv_team(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
+{
+    auto kern = gemv_team_kernel<MT, KW, EPI, LN>;
+    const size_t smem = (size_t)(MT + (LN ? 1 : 0)) * a.K * sizeof(float);
+    static bool attr = false;
+    static size_t occ_smem = 0;
+    static int occ = 0;
+    if (!attr)
+    {
+        FML_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_TEAM_MAX_SMEM));
+        attr = true;
+    }
+    if (occ_smem != smem || occ == 0)
+    {
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, 128, smem) != cudaSuccess || b < 1) b = 1;
+        occ = b;
+        occ_smem = smem;
+    }
+    int per_sm = occ;
+    if (const char* e = getenv("FML_GEMV_OCC"))  // tuning: cap CTAs per SM
+    {
+        const long v = strtol(e, nullptr, 10);
+        if (v >= 1 && v < per_sm) per_sm = (int)v;
+    }
+    const unsigned gx = (a.M + MT - 1) / MT;
+    const unsigned ngroups = (a.N + 3) / 4;
+    const unsigned teams = 4 / KW;
+    unsigned gy = (unsigned)(per_sm * sms) / gx;  // one wave
+    gy = std::min(std::max(gy, 1u), (ngroups + teams - 1) / teams);
+    gy = std::min(gy, 65535u);
+    return launch_ks(kern, dim3(gx, gy), dim3(128), smem, st, pdl, a);
+}
+
+// K split: one warp per column group up to K = 512 (4 float4 slices per
+// lane), two up to 1024, four above.
+template <int MT, int EPI, bool LN>
+int launch_gemv_team_k(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
+{
+    if (a.K <= 512) return launch_gemv_team<MT, 1, EPI, LN>(a, st, pdl, sms);
+    if (a.K <= 1024) return launch_gemv_team<MT, 2, EPI, LN>(a, st, pdl, sms);
+    return launch_gemv_team<MT, 4, EPI, LN>(a, st, pdl, sms);
+}
+
 template <int EPI, bool LN>
 int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
 {
@@ -737,6 +1057,18 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
     const char* mt_env = getenv("FML_GEMV_MT");
     const long mt_v = mt_env ? strtol(mt_env, nullptr, 10) : (a.M > 32 ? 8 : 4);
     const uint32_t mt_cap = (uint32_t)(mt_v == 4 || mt_v == 8 ? mt_v : 16);
+    // team layout for K <= 2048 when the CTA's x rows fit in shared memory;
+    // measured on B200: config 3 decode 299 -> 265 us/step, config 4 +15 %
+    // tokens/s, but config 5's K = 4096 projection 28 us slower per launch,
+    // so larger K keeps the one-group layout (FML_GEMV_TEAM=0: always it)
+    const char* team_env = getenv("FML_GEMV_TEAM");
+    const bool team = !(team_env && strtol(team_env, nullptr, 10) == 0) && mt_cap <= 8 && a.K <= 2048;
+    const uint32_t mt_team = a.M <= 4 || mt_cap == 4 ? 4u : 8u;
+    if (team && (mt_team + (LN ? 1 : 0)) * a.K * sizeof(float) <= GEMV_TEAM_MAX_SMEM)
+    {
+        if (mt_team == 4) return launch_gemv_team_k<4, EPI, LN>(a, st, pdl, sms);
+        return launch_gemv_team_k<8, EPI, LN>(a, st, pdl, sms);
+    }
     if (a.M <= 4 || mt_cap == 4) return launch_gemv_mt<4, EPI, LN>(a, st, pdl, sms);
     if (a.M <= 8 || mt_cap == 8) return launch_gemv_mt<8, EPI, LN>(a, st, pdl, sms);
     return launch_gemv_mt<16, EPI, LN>(a, st, pdl, sms);
@@ -836,6 +1168,57 @@ bool fused_step_ready(fml_lm* lm)
     return lm->step_ok;
 }
 
+// L2 prefetch plan of a decode step.  At batch <= 64 the GEMVs between two
+// attention kernels are short latency-bound phases that leave HBM mostly
+// idle, while each attention kernel streams its layer's K/V rows at HBM
+// bandwidth.  Where one layer's K/V rows fit in L2 with room to spare, the
+// GEMVs after attention of layer l request the rows attention of layer l+1
+// will read (layer 0 of the next step after the last layer), so that stream
+// overlaps the latency-bound phases.  kv_parts = number of GEMVs that share
+// the prefetch (1: the projection, 2: + fc, 3: + mlp; 0: none); measured on
+// config 3: 1 best (318 -> 309 us/step), 2 and 3 slower than none (the
+// prefetch then delays the fc GEMV's own loads).  Prefetching each GEMV's own
+// weight rows as well measured no gain.  Override: FML_KV_PREFETCH = 0..3.
+struct PrefetchPlan
+{
+    uint32_t kv_parts = 0;  // GEMVs sharing each layer's K/V prefetch
+};
+
+PrefetchPlan prefetch_plan(const fml_lm* lm)
+{
+    PrefetchPlan p;
+    const uint64_t kv_layer = 2ull * lm->batch * lm->hl * lm->cfg.context * lm->hd * sizeof(float);
+    p.kv_parts = kv_layer * 5 <= lm->l2_bytes * 3 ? 1u : 0u;
+    if (const char* e = getenv("FML_KV_PREFETCH"))
+    {
+        const long v = strtol(e, nullptr, 10);
+        if (v >= 0 && v <= 3) p.kv_parts = (uint32_t)v;
+    }
+    return p;
+}
+
+// GEMV `part` of the K/V prefetch of layer `layer`: rows of the current
+// positions, plus the row the current step writes when the prefetch is for
+// the next step (extra = 1).
+void set_kv_prefetch(const fml_lm* lm, GemvArgs& a, const PrefetchPlan& p, uint32_t layer, uint32_t extra,
+                     uint32_t part)
+{
+    if (part >= p.kv_parts) return;
+    a.pf_kc = lm->kc + (uint64_t)layer * lm->layer_stride;
+    a.pf_vc = lm->vc + (uint64_t)layer * lm->layer_stride;
+    a.pf_pos = lm->pos;
+    a.pf_B = lm->batch;
+    a.pf_H = lm->hl;
+    a.pf_C = lm->cfg.context;
+    a.pf_hd = lm->hd;
+    a.pf_extra = extra;
+    a.pf_seq_stride = lm->seq_stride;
+    const uint64_t nch = ((uint64_t)lm->cfg.context * lm->hd * sizeof(float) + PF_CHUNK - 1) / PF_CHUNK;
+    const uint64_t total = 2ull * lm->batch * lm->hl * nch;
+    a.pf_lo = (uint32_t)(total * part / p.kv_parts);
+    a.pf_hi = (uint32_t)(total * (part + 1) / p.kv_parts);
+}
+
 // Enqueue one decode step for the active batch: embed, per layer
 // {qkv (LayerNorm fused) -> attention -> proj + residual -> fc (LayerNorm
 // fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
@@ -861,8 +1244,10 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
     }
     const bool tp = lm->tp_world > 1;
     const bool resid_here = lm->tp_rank == 0;  // row-parallel sums take the residual once
+    const PrefetchPlan pf = prefetch_plan(lm);
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
+        const uint32_t ln = (l + 1) % c.n_layer, extra = l + 1 == c.n_layer ? 1u : 0u;  // next attention
         {
             ProfScope ps(lm, 2, st);
             GemvArgs a{};
@@ -880,6 +1265,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
+            set_kv_prefetch(lm, a, pf, ln, extra, 0);
             if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, st, pdl));
             else
             {
@@ -893,6 +1279,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = lm->fl; a.K = d; a.gamma = lm->ln1[l];
             a.y = lm->hid; a.ldy = lm->fl;
+            set_kv_prefetch(lm, a, pf, ln, extra, 1);
             FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl && (!tp || lm->ar_fused))));
         }
         {
@@ -900,6 +1287,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
+            set_kv_prefetch(lm, a, pf, ln, extra, 2);
             if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, st, pdl));
             else
             {
@@ -994,6 +1382,11 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     lm->dl = c.d_model;
     lm->fl = 4 * c.d_model;
     lm->vl = c.vocab;
+    {
+        int l2 = 0;
+        if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device) == cudaSuccess && l2 > 0)
+            lm->l2_bytes = (uint64_t)l2;
+    }
 
     const uint64_t d = c.d_model, B = c.max_batch, Ctx = c.context, L = c.n_layer, H = c.n_head;
     lm->seq_stride = H * Ctx * hd;
