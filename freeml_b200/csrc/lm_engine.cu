@@ -140,50 +140,7 @@ struct GemvArgs
 
     // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
     const float* gamma;
-
-    // L2 prefetch of bytes the step reads later, issued before
-    // griddepcontrol.wait: units [pf_lo, pf_hi) of one layer's cached K/V
-    // rows -- rows [0, min(pf_pos[b] + pf_extra, pf_C)) of every (sequence b,
-    // head), PF_CHUNK bytes per unit (pf_kc null: none)
-    const float* pf_kc;
-    const float* pf_vc;
-    const uint32_t* pf_pos;
-    uint32_t pf_B, pf_H, pf_C, pf_hd, pf_extra;
-    uint32_t pf_lo, pf_hi;
-    uint64_t pf_seq_stride;
 };
-
-constexpr uint32_t PF_CHUNK = 16384;  // bytes per bulk L2 prefetch
-
-// Asynchronous prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes
-// a multiple of 16); no registers or shared memory are held while it lands.
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes)
-{
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// The GEMV's share of a layer's K/V prefetch (see GemvArgs), spread over
-// every thread of the grid.
-__device__ __forceinline__ void gemv_prefetch(const GemvArgs& a)
-{
-    if (a.pf_kc)
-    {
-        const uint64_t row_bytes = (uint64_t)a.pf_hd * sizeof(float);
-        const uint32_t nch = (uint32_t)((a.pf_C * row_bytes + PF_CHUNK - 1) / PF_CHUNK);
-        const uint32_t nthreads = blockDim.x * gridDim.x * gridDim.y;
-        for (uint32_t u = a.pf_lo + threadIdx.x + blockDim.x * (blockIdx.x + gridDim.x * blockIdx.y); u < a.pf_hi;
-             u += nthreads)
-        {
-            const uint32_t j = u % nch, bh2 = u / nch, bh = bh2 >> 1;
-            const uint32_t b = bh / a.pf_H, h = bh % a.pf_H;
-            const uint64_t bytes = (uint64_t)min(a.pf_pos[b] + a.pf_extra, a.pf_C) * row_bytes;
-            const uint64_t o = (uint64_t)j * PF_CHUNK;
-            if (b >= a.pf_B || o >= bytes) continue;
-            const float* base = (bh2 & 1 ? a.pf_vc : a.pf_kc) + (uint64_t)b * a.pf_seq_stride + (uint64_t)h * a.pf_C * a.pf_hd;
-            prefetch_l2(reinterpret_cast<const char*>(base) + o, (uint32_t)min((uint64_t)PF_CHUNK, bytes - o));
-        }
-    }
-}
 
 // y[m, n] = sum_k xn[m, k] W[n, k] for the small-M (decode) shapes, where
 // xn = x, or LayerNormOp(x) with gamma (LN = true: LayerNorm.h:148-165 fused
@@ -229,7 +186,6 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
     for (int j = 0; j < NW; ++j)
         wv[j] = have_first ? ldw(wrow[j] + k_first) : make_float4(0, 0, 0, 0);
 
-    gemv_prefetch(a);
     griddep_launch_dependents();
     griddep_wait();
     FML_TIMELINE_MARK(1);
@@ -487,7 +443,6 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
         for (uint32_t c = tid; c < K / 4; c += 128) const_cast<float4*>(gs4)[c] = g4[c];
     }
 
-    gemv_prefetch(a);
     griddep_launch_dependents();
     griddep_wait();
     FML_TIMELINE_MARK(1);
@@ -809,9 +764,6 @@ struct fml_lm
 
     uint32_t batch = 0;                // active sequences
     std::vector<uint32_t> hpos;        // host mirror of positions
-
-    // L2 prefetch in the decode step (GemvArgs::pf_*), sized against the L2
-    uint64_t l2_bytes = 0;
 
     // graph / programmatic dependent launch
     bool use_graph = true;
@@ -1168,57 +1120,6 @@ bool fused_step_ready(fml_lm* lm)
     return lm->step_ok;
 }
 
-// L2 prefetch plan of a decode step.  At batch <= 64 the GEMVs between two
-// attention kernels are short latency-bound phases that leave HBM mostly
-// idle, while each attention kernel streams its layer's K/V rows at HBM
-// bandwidth.  Where one layer's K/V rows fit in L2 with room to spare, the
-// GEMVs after attention of layer l request the rows attention of layer l+1
-// will read (layer 0 of the next step after the last layer), so that stream
-// overlaps the latency-bound phases.  kv_parts = number of GEMVs that share
-// the prefetch (1: the projection, 2: + fc, 3: + mlp; 0: none); measured on
-// config 3: 1 best (318 -> 309 us/step), 2 and 3 slower than none (the
-// prefetch then delays the fc GEMV's own loads).  Prefetching each GEMV's own
-// weight rows as well measured no gain.  Override: FML_KV_PREFETCH = 0..3.
-struct PrefetchPlan
-{
-    uint32_t kv_parts = 0;  // GEMVs sharing each layer's K/V prefetch
-};
-
-PrefetchPlan prefetch_plan(const fml_lm* lm)
-{
-    PrefetchPlan p;
-    const uint64_t kv_layer = 2ull * lm->batch * lm->hl * lm->cfg.context * lm->hd * sizeof(float);
-    p.kv_parts = kv_layer * 5 <= lm->l2_bytes * 3 ? 1u : 0u;
-    if (const char* e = getenv("FML_KV_PREFETCH"))
-    {
-        const long v = strtol(e, nullptr, 10);
-        if (v >= 0 && v <= 3) p.kv_parts = (uint32_t)v;
-    }
-    return p;
-}
-
-// GEMV `part` of the K/V prefetch of layer `layer`: rows of the current
-// positions, plus the row the current step writes when the prefetch is for
-// the next step (extra = 1).
-void set_kv_prefetch(const fml_lm* lm, GemvArgs& a, const PrefetchPlan& p, uint32_t layer, uint32_t extra,
-                     uint32_t part)
-{
-    if (part >= p.kv_parts) return;
-    a.pf_kc = lm->kc + (uint64_t)layer * lm->layer_stride;
-    a.pf_vc = lm->vc + (uint64_t)layer * lm->layer_stride;
-    a.pf_pos = lm->pos;
-    a.pf_B = lm->batch;
-    a.pf_H = lm->hl;
-    a.pf_C = lm->cfg.context;
-    a.pf_hd = lm->hd;
-    a.pf_extra = extra;
-    a.pf_seq_stride = lm->seq_stride;
-    const uint64_t nch = ((uint64_t)lm->cfg.context * lm->hd * sizeof(float) + PF_CHUNK - 1) / PF_CHUNK;
-    const uint64_t total = 2ull * lm->batch * lm->hl * nch;
-    a.pf_lo = (uint32_t)(total * part / p.kv_parts);
-    a.pf_hi = (uint32_t)(total * (part + 1) / p.kv_parts);
-}
-
 // Enqueue one decode step for the active batch: embed, per layer
 // {qkv (LayerNorm fused) -> attention -> proj + residual -> fc (LayerNorm
 // fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
@@ -1244,10 +1145,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
     }
     const bool tp = lm->tp_world > 1;
     const bool resid_here = lm->tp_rank == 0;  // row-parallel sums take the residual once
-    const PrefetchPlan pf = prefetch_plan(lm);
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
-        const uint32_t ln = (l + 1) % c.n_layer, extra = l + 1 == c.n_layer ? 1u : 0u;  // next attention
         {
             ProfScope ps(lm, 2, st);
             GemvArgs a{};
@@ -1265,7 +1164,6 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            set_kv_prefetch(lm, a, pf, ln, extra, 0);
             if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, st, pdl));
             else
             {
@@ -1279,7 +1177,6 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = lm->fl; a.K = d; a.gamma = lm->ln1[l];
             a.y = lm->hid; a.ldy = lm->fl;
-            set_kv_prefetch(lm, a, pf, ln, extra, 1);
             FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl && (!tp || lm->ar_fused))));
         }
         {
@@ -1287,7 +1184,6 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
             GemvArgs a{};
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            set_kv_prefetch(lm, a, pf, ln, extra, 2);
             if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, st, pdl));
             else
             {
@@ -1382,11 +1278,6 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     lm->dl = c.d_model;
     lm->fl = 4 * c.d_model;
     lm->vl = c.vocab;
-    {
-        int l2 = 0;
-        if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device) == cudaSuccess && l2 > 0)
-            lm->l2_bytes = (uint64_t)l2;
-    }
 
     const uint64_t d = c.d_model, B = c.max_batch, Ctx = c.context, L = c.n_layer, H = c.n_head;
     lm->seq_stride = H * Ctx * hd;

@@ -201,6 +201,27 @@ def test_attention_decode_vs_oracle(B, H, hd, C, lens):
     close(host(out), ref, 2e-5, 2e-5)
 
 
+@pytest.mark.parametrize("splits", [2, 3, 5, 8])
+def test_attention_cluster_merge_matches_global_merge(monkeypatch, splits):
+    """2..8 key splits run as one thread-block cluster per (row, head) and
+    merge through distributed shared memory; the result is bit-identical to
+    the global-partials merge (same arithmetic, same order) and matches the
+    oracle, including empty rows and splits past a short row's keys."""
+    from freeml_b200 import matrix_ops as F
+    B, H, hd, C, lens = 4, 8, 64, 512, [0, 1, 300, 512]
+    q, kc, vc, ln = _attention_case(B, H, hd, C, lens, 77)
+    scale = float(1.0 / np.sqrt(np.float32(hd)))
+    monkeypatch.setenv("FML_ATTN_SPLITS", str(splits))
+    outs = []
+    for cluster in ("1", "0"):
+        monkeypatch.setenv("FML_ATTN_CLUSTER", cluster)
+        out = torch.empty(B, H * hd, device="cuda")
+        F.attention_decode(out, cu(q), cu(kc), cu(vc), torch.from_numpy(ln).cuda(), scale)
+        outs.append(host(out))
+    np.testing.assert_array_equal(outs[0], outs[1])
+    close(outs[0], _attention_oracle(q, kc, vc, ln, np.float32(scale)), 2e-5, 2e-5)
+
+
 def test_attention_decode_rejects_small_workspace():
     from freeml_b200 import FmlError
     from freeml_b200 import matrix_ops as F
