@@ -112,7 +112,7 @@ __device__ __forceinline__ AttnUnit attention_unit(const AttnArgs& a, uint32_t r
     else if (a.pos) { t.b = r; len = a.pos[r] + 1; t.newest = len - 1; }
     else { t.b = r / a.P; len = r % a.P + 1; }
     // keys per split: fixed, or an even share of this row's keys
-    const uint32_t chunk = a.chunk ? a.chunk : max(32u, ((len + a.S - 1) / a.S + 31u) & ~31u);
+    const uint32_t chunk = a.chunk ? a.chunk : max(8u, ((len + a.S - 1) / a.S + 7u) & ~7u);
     t.begin = min(s * chunk, len);
     t.end = min(len, t.begin + chunk);
     t.nsplit = (len + chunk - 1) / chunk;  // non-empty splits of this row
@@ -156,6 +156,12 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int grp = lane / G, lig = lane % G;
     const uint32_t h = blockIdx.x, r = a.row0 + blockIdx.y, s = blockIdx.z;
+
+    // CL: first arrival on the cluster barrier; its wait, before the first
+    // write into another CTA's shared memory, guarantees every CTA of the
+    // cluster is running by then
+    [[maybe_unused]] cooperative_groups::cluster_group::arrival_token cl_started;
+    if constexpr (CL) cl_started = cooperative_groups::this_cluster().barrier_arrive();
 
     griddep_launch_dependents();
 
@@ -285,30 +291,36 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
                            : 0.0f;
     if constexpr (CL)
     {
-        // same arithmetic as the global merge below, over every split in
-        // order (an empty split has m = -inf and weight 0)
-        __shared__ __align__(16) float cl_acc[HD];
-        __shared__ float cl_ml[2];
-        if (e < HD) cl_acc[e] = A;
-        if (e == 0) { cl_ml[0] = M; cl_ml[1] = L; }
+        // every split pushes (acc, m, l) into cluster rank 0's shared memory;
+        // after the cluster barrier rank 0 merges them from its own shared
+        // memory -- the same arithmetic as the global merge below, over every
+        // split in order (an empty split has m = -inf and weight 0)
+        __shared__ __align__(16) float cl_acc[8][HD];
+        __shared__ float cl_ml[8][2];
         cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
-        cluster.sync();
-        if (cluster.block_rank() == 0)
+        cluster.barrier_wait(std::move(cl_started));
+        if (e < HD) *cluster.map_shared_rank(&cl_acc[s][e], 0) = A;
+        if (e == 0)
         {
-            const uint32_t ns = cluster.num_blocks();
+            *cluster.map_shared_rank(&cl_ml[s][0], 0) = M;
+            *cluster.map_shared_rank(&cl_ml[s][1], 0) = L;
+        }
+        cluster.sync();
+        if (s == 0)
+        {
+            const uint32_t ns = gridDim.z;
             float Mg = -INFINITY;
-            for (uint32_t i = 0; i < ns; ++i) Mg = fmaxf(Mg, *cluster.map_shared_rank(&cl_ml[0], i));
+            for (uint32_t i = 0; i < ns; ++i) Mg = fmaxf(Mg, cl_ml[i][0]);
             float Lg = 0.0f, Ag = 0.0f;
             for (uint32_t i = 0; i < ns; ++i)
             {
-                const float mi = *cluster.map_shared_rank(&cl_ml[0], i);
+                const float mi = cl_ml[i][0];
                 const float wi = mi == -INFINITY ? 0.0f : expf(mi - Mg);
-                Lg += *cluster.map_shared_rank(&cl_ml[1], i) * wi;
-                if (e < HD) Ag += *cluster.map_shared_rank(&cl_acc[e], i) * wi;
+                Lg += cl_ml[i][1] * wi;
+                if (e < HD) Ag += cl_acc[i][e] * wi;
             }
             if (e < HD) a.out[(uint64_t)r * a.ldo + h * HD + e] = Lg > 0.0f ? Ag / Lg : 0.0f;
         }
-        cluster.sync();  // every split's shared memory stays live until rank 0 has read it
         return;
     }
     if (cu.nsplit <= 1)
