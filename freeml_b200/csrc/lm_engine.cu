@@ -1380,6 +1380,13 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     return FML_OK;
 }
 
+int fml_lm_get_config(const fml_lm* lm, fml_lm_config* out)
+{
+    FML_REQUIRE(lm && out, "fml_lm_get_config: null argument");
+    *out = lm->cfg;
+    return FML_OK;
+}
+
 int fml_lm_destroy(fml_lm* lm)
 {
     if (!lm) return FML_OK;

@@ -88,6 +88,11 @@ class NanoLM:
             assert params.is_cuda and params.dtype == torch.float32 and params.numel() == n
             call("fml_lm_bind_packed", self._h, params.contiguous().data_ptr(), 0, self._stream())
 
+    def load_checkpoint(self, path: str) -> None:
+        """Bind the weights of a FreeML checkpoint directory (Model::Save of a
+        NanoLLM model) -- fml_lm_load_checkpoint; the shapes must match."""
+        call("fml_lm_load_checkpoint", self._h, str(path).encode(), self._stream())
+
     def prefill(self, prompts) -> None:
         """prompts: [B, P] uint32 (numpy or CUDA int32 tensor)."""
         if isinstance(prompts, np.ndarray):
@@ -222,6 +227,23 @@ def nccl_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     call("fml_nccl_unique_id", buf)
     return buf.raw
+
+
+def checkpoint_shape(path: str) -> NanoLLMShape:
+    """(V, C, d, H, L) of a FreeML NanoLLM checkpoint directory, read from its
+    stored shapes (fml_checkpoint_config; host only)."""
+    cfg = LMConfig()
+    call("fml_checkpoint_config", str(path).encode(), ctypes.byref(cfg))
+    return NanoLLMShape(cfg.vocab, cfg.context, cfg.d_model, cfg.n_head, cfg.n_layer)
+
+
+def checkpoint_params(path: str) -> np.ndarray:
+    """Every parameter of a FreeML NanoLLM checkpoint in the canonical packed
+    order (fml_checkpoint_pack; host only)."""
+    shape = checkpoint_shape(path)
+    out = np.empty(shape.param_count(), np.float32)
+    call("fml_checkpoint_pack", str(path).encode(), out.ctypes.data, out.size)
+    return out
 
 
 def random_params(shape: NanoLLMShape, seed: int, device: int = 0) -> torch.Tensor:

@@ -244,6 +244,22 @@ FML_API int fml_lm_bind_weights(fml_lm* lm, const fml_lm_weights* w, fml_stream_
  * order tok_emb, pos_emb, per layer {ln0, wqkv, wproj, ln1, wfc, wmlp}, lnf. */
 FML_API int fml_lm_bind_packed(fml_lm* lm, const float* params, int params_on_host, fml_stream_t stream);
 FML_API uint64_t fml_lm_param_count(const fml_lm_config* cfg);
+FML_API int fml_lm_get_config(const fml_lm* lm, fml_lm_config* out);
+
+/* FreeML checkpoints: the directory Model::Save writes for a NanoLLM model
+ * (ModelLibrary/Model.h:91-159; model.guide, *.blob_layer, *.blob_matrix,
+ * *.blob_data, Loading/SaveLoader.h:499-577, 1523-1563), read without
+ * building FreeML's layer graph.  fml_checkpoint_config gives V, C, d, H, L
+ * (max_batch 0) from the stored shapes; fml_checkpoint_pack reads every
+ * parameter into a host buffer of fml_lm_param_count floats in the packed
+ * order of fml_lm_bind_packed; fml_lm_load_checkpoint does both and binds
+ * the weights (the engine's shape must match).  A checkpoint with bias
+ * terms, an untied lm_head or another layer naming than NanoLLM's
+ * (Examples/NanoLLM/NanoLLM.cpp:268-348) is rejected (FML_ERR_UNSUPPORTED /
+ * FML_ERR_INVALID).  Host-only except the final bind. */
+FML_API int fml_checkpoint_config(const char* dir, fml_lm_config* cfg_out);
+FML_API int fml_checkpoint_pack(const char* dir, float* params_out, uint64_t count);
+FML_API int fml_lm_load_checkpoint(fml_lm* lm, const char* dir, fml_stream_t stream);
 
 /* Start `batch` sequences (batch <= max_batch) from prompts of `prompt_len`
  * tokens each (device, sequence-major [batch x prompt_len]).  Runs the

@@ -239,6 +239,14 @@ def ref_greedy(s: LMShape, wseed: int, prompt: np.ndarray, nnew: int):
         return np.fromfile(tf, np.uint32), np.fromfile(lf, np.float32).reshape(nnew, s.V)
 
 
+def ref_save(s: LMShape, wseed: int, directory: str, name: str) -> str:
+    """FreeML's own Model::Save of the built model (ModelLibrary/Model.h:91-159)
+    into directory/name; returns that path."""
+    subprocess.run([REF_BIN, "save", *_shape_args(s, wseed), "--dir", directory, "--name", name], check=True,
+                   capture_output=True)
+    return os.path.join(directory, name)
+
+
 def ref_forward(s: LMShape, wseed: int, window: np.ndarray) -> np.ndarray:
     with tempfile.TemporaryDirectory() as td:
         wf, lf = os.path.join(td, "w.bin"), os.path.join(td, "l.bin")

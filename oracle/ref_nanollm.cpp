@@ -28,6 +28,7 @@
 //   forward  --window F --out-logits F    one Run over a C-token window, all C rows
 //   time     --forwards K --warmup W      seconds per full-window Run (JSON line)
 //   op       --op NAME --in F --out F ... one generic operator on given inputs
+//   save     --dir D --name N             Model::Save of the built model into D/N
 #include <ModelLibrary/Model.h>
 #include <LayerLibrary/Layers.h>
 #include <MatrixLibrary/CPU/MatrixCPU.h>
@@ -40,6 +41,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <filesystem>
 #include <fstream>
 #include <memory>
 #include <random>
@@ -319,6 +321,22 @@ static int ModeWeights(const Args& a)
     return 0;
 }
 
+// The model saved by FreeML's own Model::Save (Model.h:91-159, SaveLoader.h:
+// 499-577, 1523-1563) into <dir>/<name>: model.guide, one .blob_layer text file
+// per (sub)layer, .blob_matrix headers and raw .blob_data payloads.
+static int ModeSave(const Args& a)
+{
+    LMConfig cfg = ConfigFrom(a);
+    Built b = BuildModel(cfg);
+    b.model->SetName(a.get("name", "nanollm"));
+    const std::filesystem::path old = std::filesystem::current_path();
+    std::filesystem::create_directories(a.get("dir", "."));
+    std::filesystem::current_path(a.get("dir", "."));
+    const bool ok = b.model->Save();
+    std::filesystem::current_path(old);
+    return ok ? 0 : 1;
+}
+
 static int ModeTime(const Args& a)
 {
     LMConfig cfg = ConfigFrom(a);
@@ -442,12 +460,13 @@ static int ModeOp(const Args& a)
 int main(int argc, char** argv)
 {
     Tools::Logger::SetMinLevel(Tools::Logger::Level::Error);
-    if (argc < 2) { std::fprintf(stderr, "usage: %s weights|greedy|forward|time|op [--key value]...\n", argv[0]); return 2; }
+    if (argc < 2) { std::fprintf(stderr, "usage: %s weights|greedy|forward|time|op|save [--key value]...\n", argv[0]); return 2; }
     const std::string mode = argv[1];
     Args a = ParseArgs(argc, argv, 2);
     if (mode == "greedy") return ModeGreedy(a);
     if (mode == "forward") return ModeForward(a);
     if (mode == "weights") return ModeWeights(a);
+    if (mode == "save") return ModeSave(a);
     if (mode == "time") return ModeTime(a);
     if (mode == "op") return ModeOp(a);
     std::fprintf(stderr, "unknown mode %s\n", mode.c_str());

@@ -3,7 +3,8 @@
 Run (in a container that has the FreeML tree and the built harness):
 
     make -C oracle all
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py              # every fixture
+    python tests/golden/make_golden.py checkpoint   # only ckpt_tiny.tgz
 
 Every number below comes from ``oracle/_ref/ref_nanollm`` -- the unmodified
 reference ``Model<float, MatrixCPU<float>>`` and its generic operators -- never
@@ -15,6 +16,8 @@ import hashlib
 import json
 import os
 import sys
+import tarfile
+import tempfile
 
 import numpy as np
 
@@ -27,6 +30,9 @@ GREEDY_CASES = [
     ("cfg1", O.LMShape(V=256, C=128, d=128, H=4, L=4), 0, 1, 16, 112),
     ("odd", O.LMShape(V=97, C=48, d=64, H=2, L=2), 11, 12, 8, 40),       # non-power-of-two vocab
 ]
+# a checkpoint written by FreeML's Model::Save, committed as a tarball
+# (name, shape, weight seed, prompt seed, prompt length, decode steps)
+CHECKPOINT_CASE = ("ckpt_tiny", O.LMShape(V=61, C=16, d=32, H=1, L=2), 11, 5, 4, 12)  # head dim 32
 # weight-init hashes only (the tensors are too big to commit)
 HASH_CASES = [
     ("cfg3", O.LMShape(V=4096, C=512, d=512, H=8, L=8), 3),
@@ -35,6 +41,24 @@ HASH_CASES = [
 
 def sha(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def make_checkpoint() -> dict:
+    """The tiny model saved by FreeML's Model::Save, as ckpt_tiny.tgz, plus its
+    reference greedy tokens."""
+    name, s, wseed, pseed, plen, nnew = CHECKPOINT_CASE
+    with tempfile.TemporaryDirectory() as td:
+        path = O.ref_save(s, wseed, td, "nanollm_tiny")
+        with tarfile.open(os.path.join(HERE, f"{name}.tgz"), "w:gz") as tar:
+            tar.add(path, arcname="nanollm_tiny")
+    prompt = np.random.RandomState(pseed).randint(0, s.V, plen).astype(np.uint32)
+    toks, _ = O.ref_greedy(s, wseed, prompt, nnew)
+    print(name, "checkpoint tokens", toks)
+    w = O.ref_weights(s, wseed)
+    return {name: {"V": s.V, "C": s.C, "d": s.d, "H": s.H, "L": s.L, "wseed": wseed,
+                                 "pseed": pseed, "plen": plen, "new": nnew, "dir": "nanollm_tiny",
+                                 "weights_sha256": sha(w), "weights_count": int(w.size),
+                                 "tokens": [int(t) for t in toks]}}
 
 
 def main():
@@ -56,6 +80,7 @@ def main():
                                 "pseed": pseed, "plen": plen, "new": nnew,
                                 "weights_sha256": sha(w), "weights_count": int(w.size)}
         print(name, "tokens", toks[:8], "...")
+    meta["checkpoint"] = make_checkpoint()
     for name, s, wseed in HASH_CASES:
         w = O.ref_weights(s, wseed)
         meta["weights_sha256"][name] = {"V": s.V, "C": s.C, "d": s.d, "H": s.H, "L": s.L, "wseed": wseed,
@@ -118,4 +143,13 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["checkpoint"]:  # refresh only the checkpoint fixture
+        assert O.ref_available(), "build oracle/_ref/ref_nanollm first (make -C oracle all)"
+        path = os.path.join(HERE, "golden.json")
+        with open(path) as f:
+            meta = json.load(f)
+        meta["checkpoint"] = make_checkpoint()
+        with open(path, "w") as f:
+            json.dump(meta, f, indent=1, sort_keys=True)
+    else:
+        main()
