@@ -247,6 +247,24 @@ def ref_save(s: LMShape, wseed: int, directory: str, name: str) -> str:
     return os.path.join(directory, name)
 
 
+REF_VOCAB_BIN = os.path.join(HERE, "_ref", "ref_vocab")
+
+
+def ref_vocab(corpus: bytes, text: bytes, ids: np.ndarray) -> dict:
+    """NanoLLM's own BuildVocab / encode / decode / DecodeMatrixTokens
+    (Examples/NanoLLM/NanoLLM.cpp:95-206) on the given inputs."""
+    with tempfile.TemporaryDirectory() as td:
+        paths = [os.path.join(td, n) for n in ("corpus.bin", "text.bin", "ids.bin")]
+        for p, data in zip(paths, (corpus, text, np.ascontiguousarray(ids, np.uint32).tobytes())):
+            with open(p, "wb") as f:
+                f.write(data)
+        subprocess.run([REF_VOCAB_BIN, *paths, td], check=True, capture_output=True)
+        rd = lambda n: open(os.path.join(td, n), "rb").read()  # noqa: E731
+        return {"unique": rd("unique.bin"), "corpus_ids": np.frombuffer(rd("corpus_ids.bin"), np.uint32).copy(),
+                "encode": np.frombuffer(rd("encode.bin"), np.uint32).copy(), "decode": rd("decode.bin"),
+                "decode_tokens": rd("decode_tokens.bin")}
+
+
 def ref_forward(s: LMShape, wseed: int, window: np.ndarray) -> np.ndarray:
     with tempfile.TemporaryDirectory() as td:
         wf, lf = os.path.join(td, "w.bin"), os.path.join(td, "l.bin")

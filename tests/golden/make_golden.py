@@ -5,6 +5,7 @@ Run (in a container that has the FreeML tree and the built harness):
     make -C oracle all
     python tests/golden/make_golden.py              # every fixture
     python tests/golden/make_golden.py checkpoint   # only ckpt_tiny.tgz
+    python tests/golden/make_golden.py vocab        # only vocab.npz
 
 Every number below comes from ``oracle/_ref/ref_nanollm`` -- the unmodified
 reference ``Model<float, MatrixCPU<float>>`` and its generic operators -- never
@@ -61,6 +62,25 @@ def make_checkpoint() -> dict:
                                  "tokens": [int(t) for t in toks]}}
 
 
+def make_vocab() -> None:
+    """NanoLLM's vocabulary code on a synthetic byte corpus (bytes on both
+    sides of 0x80, some absent), a text with absent bytes and ids past the
+    vocabulary, as vocab.npz."""
+    rs = np.random.RandomState(21)
+    alphabet = np.concatenate([np.arange(9, 14), np.arange(32, 127), np.arange(0xC0, 0xE0)]).astype(np.uint8)
+    present = rs.choice(alphabet, 90, replace=False)
+    corpus = rs.choice(present, 4000).astype(np.uint8).tobytes()
+    text = rs.choice(alphabet, 300).astype(np.uint8).tobytes()
+    ids = rs.randint(0, 100, 200).astype(np.uint32)
+    r = O.ref_vocab(corpus, text, ids)
+    np.savez_compressed(os.path.join(HERE, "vocab.npz"), corpus=np.frombuffer(corpus, np.uint8),
+                        text=np.frombuffer(text, np.uint8), ids=ids,
+                        unique=np.frombuffer(r["unique"], np.uint8), corpus_ids=r["corpus_ids"],
+                        encode=r["encode"], decode=np.frombuffer(r["decode"], np.uint8),
+                        decode_tokens=np.frombuffer(r["decode_tokens"], np.uint8))
+    print("vocab", len(r["unique"]), "symbols")
+
+
 def main():
     assert O.ref_available(), "build oracle/_ref/ref_nanollm first (make -C oracle all)"
     meta = {"greedy": {}, "weights_sha256": {}}
@@ -81,6 +101,7 @@ def main():
                                 "weights_sha256": sha(w), "weights_count": int(w.size)}
         print(name, "tokens", toks[:8], "...")
     meta["checkpoint"] = make_checkpoint()
+    make_vocab()
     for name, s, wseed in HASH_CASES:
         w = O.ref_weights(s, wseed)
         meta["weights_sha256"][name] = {"V": s.V, "C": s.C, "d": s.d, "H": s.H, "L": s.L, "wseed": wseed,
@@ -143,7 +164,10 @@ def main():
 
 
 if __name__ == "__main__":
-    if sys.argv[1:] == ["checkpoint"]:  # refresh only the checkpoint fixture
+    if sys.argv[1:] == ["vocab"]:  # refresh only vocab.npz
+        assert os.path.exists(O.REF_VOCAB_BIN), "build oracle/_ref first (make -C oracle all)"
+        make_vocab()
+    elif sys.argv[1:] == ["checkpoint"]:  # refresh only the checkpoint fixture
         assert O.ref_available(), "build oracle/_ref/ref_nanollm first (make -C oracle all)"
         path = os.path.join(HERE, "golden.json")
         with open(path) as f:
