@@ -75,6 +75,10 @@ SIGNATURES = {
     "fml_lm_bind_packed": (_I, [_P, _P, _I, _P]),
     "fml_lm_param_count": (_U64, [ctypes.POINTER(LMConfig)]),
     "fml_lm_get_config": (_I, [_P, ctypes.POINTER(LMConfig)]),
+    "fml_capture_begin": (_I, [ctypes.POINTER(_P)]),
+    "fml_capture_end": (_I, [_P, ctypes.POINTER(_P)]),
+    "fml_graph_launch": (_I, [_P, _P]),
+    "fml_graph_destroy": (_I, [_P]),
     "fml_checkpoint_config": (_I, [ctypes.c_char_p, ctypes.POINTER(LMConfig)]),
     "fml_checkpoint_pack": (_I, [ctypes.c_char_p, _P, _U64]),
     "fml_lm_load_checkpoint": (_I, [_P, ctypes.c_char_p, _P]),

@@ -7,11 +7,13 @@
 // every operator of Model::Run then runs as an sm_100a kernel.
 //
 // Modes (raw little-endian binary files):
-//   greedy  --prompt F --plen P --new N --out-tokens F --out-logits F
+//   greedy  --prompt F --plen P --new N --out-tokens F --out-logits F [--graph 1]
 //           the reference greedy loop (one full-window Model::Run per token,
 //           argmax of row P+step-1 with the first-max rule of
 //           NanoLLM.cpp:189-204); prints JSON with the host transfers and
-//           kernel launches counted inside the Run calls
+//           kernel launches counted inside the Run calls and the time per
+//           Run; --graph 1 records Model::Run once as a launch plan
+//           (freeml_cuda::RunGraph) and replays it for every token
 //   engine  --prompt F --plen P --new N --out-tokens F
 //           the KV-cached decode engine (fml_lm_*) bound to this model's
 //           weight matrices (device pointers taken from its Datablobs)
@@ -25,6 +27,7 @@
 #include <freeml_b200/MatrixCUDA.h>
 #include <freeml_b200/MatrixCUDA_Functions.h>
 
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -192,13 +195,23 @@ int Greedy(const Shape& s, const Args& a)
     b.window->Flush();
     b.model->Run(b.window.get(), nullptr);
     fml_synchronize();
+    // --graph 1: Model::Run recorded once as a launch plan and replayed
+    const bool graph = a.u("graph", 0) != 0;
+    freeml_cuda::RunGraph plan;
+    if (graph) plan.Record([&] { b.model->Run(b.window.get(), nullptr); });
     uint64_t run_transfers = 0, run_launches = 0;
+    double run_seconds = 0.0;
     for (uint32_t step = 0; step < nnew; ++step)
     {
         b.window->Flush();
+        fml_synchronize();
         const auto t0 = Mat::HostTransfers();
         const uint64_t l0 = fml_kernel_launch_count();
-        b.model->Run(b.window.get(), nullptr);
+        const auto c0 = std::chrono::steady_clock::now();
+        if (graph) plan.Replay();
+        else b.model->Run(b.window.get(), nullptr);
+        fml_synchronize();
+        run_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - c0).count();
         const auto t1 = Mat::HostTransfers();
         run_launches += fml_kernel_launch_count() - l0;
         run_transfers += (t1.downloads - t0.downloads) + (t1.uploads - t0.uploads);
@@ -215,8 +228,10 @@ int Greedy(const Shape& s, const Args& a)
     }
     WriteRaw(a.get("out-tokens"), tokens);
     if (a.has("out-logits")) WriteRaw(a.get("out-logits"), rows);
-    std::printf("{\"runs\": %u, \"host_transfers_in_run\": %llu, \"kernel_launches_in_run\": %llu}\n", nnew,
-                (unsigned long long)run_transfers, (unsigned long long)run_launches);
+    std::printf("{\"runs\": %u, \"graph\": %d, \"host_transfers_in_run\": %llu, \"kernel_launches_in_run\": %llu, "
+                "\"ms_per_run\": %.4f}\n",
+                nnew, graph ? 1 : 0, (unsigned long long)run_transfers, (unsigned long long)run_launches,
+                1e3 * run_seconds / nnew);
     return 0;
 }
 

@@ -56,6 +56,23 @@ inline Counters& GlobalCounters()
     return c;
 }
 
+struct Storage;
+
+// Buffers the operators read and write while a RunGraph records (see
+// MatrixCUDA_Functions.h): a replay must upload pending host writes to the
+// first and mark the host mirrors of the second stale, since the recorded
+// calls -- and their DevIn() / DevOut() bookkeeping -- do not run again.
+struct Recording
+{
+    std::vector<Storage*> read, written;
+};
+
+inline Recording*& ActiveRecording()
+{
+    static Recording* r = nullptr;
+    return r;
+}
+
 // One device buffer and its host mirror, shared by the owner and all views.
 struct Storage
 {
@@ -153,6 +170,7 @@ public:
     {
         if (!m_storage) return nullptr;
         m_storage->Upload();
+        if (auto* r = freeml_cuda::ActiveRecording()) r->read.push_back(m_storage);
         return m_storage->dev + m_offset;
     }
 
@@ -164,6 +182,7 @@ public:
         if (!m_storage) return nullptr;
         m_storage->Upload();
         m_storage->host_valid = false;
+        if (auto* r = freeml_cuda::ActiveRecording()) r->written.push_back(m_storage);
         return m_storage->dev + m_offset;
     }
 

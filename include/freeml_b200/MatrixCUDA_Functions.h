@@ -12,6 +12,9 @@
 // transfers so a test can assert that Model::Run performed none.
 #pragma once
 
+#include <algorithm>
+#include <vector>
+
 #include <MatrixLibrary/MatrixBase_Functions.h>
 #include <MatrixLibrary/MatrixBase_Mul.h>
 
@@ -19,10 +22,85 @@
 #include "MatrixCUDA.h"
 
 namespace freeml_cuda {
-inline fml_stream_t Stream() { return nullptr; }  // the legacy default stream: ops run in call order
+// The stream the operators are issued on: the legacy default stream (ops run
+// in call order), or the capture stream while a RunGraph records.
+inline fml_stream_t& StreamSlot()
+{
+    static fml_stream_t s = nullptr;
+    return s;
+}
+inline fml_stream_t Stream() { return StreamSlot(); }
 }  // namespace freeml_cuda
 
 #define FML_CALL(expr) ::freeml_cuda::Check((expr), #expr)
+
+namespace freeml_cuda {
+
+// A pre-resolved launch plan for a host runtime that repeats the same
+// operator calls every step, such as Model::Run over a fixed window
+// (ModelLibrary/Model.h:764-788: string-keyed blob lookups, view set-up and
+// one C-ABI call per operator).  Record(f) calls f() once with every
+// operator captured into a CUDA graph -- nothing executes then; Replay()
+// uploads pending host writes of the buffers the recorded calls read (the
+// token window written through DataWrite()), launches the graph in call
+// order on the legacy default stream and marks the host mirrors of the
+// buffers they wrote stale.  The recorded calls must not touch the host
+// mirror (Model::Run does not once its inputs are flushed) and every buffer
+// they use must stay allocated while the RunGraph lives.
+class RunGraph
+{
+public:
+    RunGraph() = default;
+    RunGraph(const RunGraph&) = delete;
+    RunGraph& operator=(const RunGraph&) = delete;
+    ~RunGraph()
+    {
+        if (m_graph) fml_graph_destroy(m_graph);
+    }
+
+    template <class F>
+    void Record(F&& f)
+    {
+        if (m_graph)
+        {
+            fml_graph_destroy(m_graph);
+            m_graph = nullptr;
+        }
+        Recording rec;
+        fml_stream_t s = nullptr;
+        FML_CALL(fml_capture_begin(&s));
+        StreamSlot() = s;
+        ActiveRecording() = &rec;
+        f();
+        ActiveRecording() = nullptr;
+        StreamSlot() = nullptr;
+        FML_CALL(fml_capture_end(s, &m_graph));
+        m_read = Unique(rec.read);
+        m_written = Unique(rec.written);
+    }
+
+    void Replay()
+    {
+        for (Storage* s : m_read) s->Upload();
+        FML_CALL(fml_graph_launch(m_graph, nullptr));
+        for (Storage* s : m_written) s->host_valid = false;
+    }
+
+    bool Recorded() const { return m_graph != nullptr; }
+
+private:
+    static std::vector<Storage*> Unique(std::vector<Storage*> v)
+    {
+        std::sort(v.begin(), v.end());
+        v.erase(std::unique(v.begin(), v.end()), v.end());
+        return v;
+    }
+
+    fml_graph* m_graph = nullptr;
+    std::vector<Storage*> m_read, m_written;
+};
+
+}  // namespace freeml_cuda
 
 // GatherRows  MatrixBase_Functions.h:203-242 (token ids stored as floats)
 template <class T>

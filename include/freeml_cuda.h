@@ -58,6 +58,20 @@ enum fml_status
     FML_ERR_STATE = 5        /* engine used out of order */
 };
 
+/* Recorded launch plans: fml_capture_begin creates a stream and starts
+ * capturing it (CUDA stream capture, relaxed mode); every entry point then
+ * given that stream records its kernels instead of running them, in call
+ * order.  fml_capture_end stops, instantiates the record as one CUDA graph
+ * and releases the stream; fml_graph_launch replays it on `stream` (kernel
+ * launch counts include the replayed kernels).  For host runtimes that issue
+ * the same operator calls every step (FreeML's Model::Run over MatrixCUDA:
+ * freeml_cuda::RunGraph in include/freeml_b200/MatrixCUDA_Functions.h). */
+typedef struct fml_graph fml_graph;
+FML_API int fml_capture_begin(fml_stream_t* stream_out);
+FML_API int fml_capture_end(fml_stream_t stream, fml_graph** graph_out);
+FML_API int fml_graph_launch(fml_graph* graph, fml_stream_t stream);
+FML_API int fml_graph_destroy(fml_graph* graph);
+
 /* Library / device information. */
 FML_API const char* fml_last_error(void);
 FML_API const char* fml_version(void);

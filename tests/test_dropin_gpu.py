@@ -8,6 +8,8 @@ against the golden vectors of FreeML's MatrixCPU path:
   * greedy tokens: identical; logits within 1e-3 abs + 1e-3 rel;
   * no host fallback inside Model::Run: zero host<->device transfers, and the
     operators ran as kernels of this library;
+  * Model::Run recorded once as a launch plan (freeml_cuda::RunGraph) and
+    replayed per token: bit-identical to the eager Run;
   * the KV-cached engine bound to the same model's device weights gives the
     same token stream.
 """
@@ -49,23 +51,43 @@ def test_dropin_weights_are_the_reference_weights(golden, dropin, name):
     assert hashlib.sha256(w.tobytes()).hexdigest() == m["weights_sha256"]
 
 
-@pytest.mark.parametrize("name", ["cfg1", "odd"])
-def test_dropin_model_run_greedy_matches_reference(golden, dropin, name):
-    meta, g, _ = golden
-    m = meta["greedy"][name]
+def _greedy(dropin, g, m, name, graph):
     with tempfile.TemporaryDirectory() as td:
         pf, tf, lf = (os.path.join(td, n) for n in ("p.bin", "t.bin", "l.bin"))
         g[f"{name}_prompt"].astype(np.uint32).tofile(pf)
         p = subprocess.run([dropin, "greedy", *_args(m), "--prompt", pf, "--plen", str(m["plen"]),
-                            "--new", str(m["new"]), "--out-tokens", tf, "--out-logits", lf],
+                            "--new", str(m["new"]), "--out-tokens", tf, "--out-logits", lf, "--graph", str(graph)],
                            check=True, capture_output=True, text=True, timeout=600)
         stats = json.loads(p.stdout.strip().splitlines()[-1])
-        toks = np.fromfile(tf, np.uint32)
-        logits = np.fromfile(lf, np.float32).reshape(m["new"], m["V"])
+        return np.fromfile(tf, np.uint32), np.fromfile(lf, np.float32).reshape(m["new"], m["V"]), stats
+
+
+@pytest.mark.parametrize("graph", [0, 1], ids=["eager", "launch_plan"])
+@pytest.mark.parametrize("name", ["cfg1", "odd"])
+def test_dropin_model_run_greedy_matches_reference(golden, dropin, name, graph):
+    """Model::Run per token, either dispatching every operator (eager) or
+    replaying the Run recorded once as a CUDA graph (launch plan)."""
+    meta, g, _ = golden
+    m = meta["greedy"][name]
+    toks, logits, stats = _greedy(dropin, g, m, name, graph)
     np.testing.assert_array_equal(toks, g[f"{name}_tokens"])
     np.testing.assert_allclose(logits, g[f"{name}_logits"], rtol=1e-3, atol=1e-3)
     assert stats["host_transfers_in_run"] == 0, stats
     assert stats["kernel_launches_in_run"] > 0, stats
+    assert stats["graph"] == graph
+
+
+def test_dropin_launch_plan_is_bit_identical_to_eager_run(golden, dropin):
+    """The recorded plan replays exactly the operator sequence Model::Run
+    issues: identical logits, bit for bit, and the same kernel count."""
+    meta, g, _ = golden
+    m = meta["greedy"]["cfg1"]
+    t0, l0, s0 = _greedy(dropin, g, m, "cfg1", 0)
+    t1, l1, s1 = _greedy(dropin, g, m, "cfg1", 1)
+    np.testing.assert_array_equal(t0, t1)
+    np.testing.assert_array_equal(l0.view(np.uint32), l1.view(np.uint32))
+    assert s0["kernel_launches_in_run"] == s1["kernel_launches_in_run"], (s0, s1)
+    print(f"Model::Run per token, config 1: eager {s0['ms_per_run']:.3f} ms, launch plan {s1['ms_per_run']:.3f} ms")
 
 
 def test_engine_bound_to_dropin_model_weights(golden, dropin):
