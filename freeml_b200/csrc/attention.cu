@@ -111,6 +111,7 @@ __device__ __forceinline__ AttnUnit attention_unit(const AttnArgs& a, uint32_t r
     if (a.lens) { t.b = r; len = a.lens[r]; }
     else if (a.pos) { t.b = r; len = a.pos[r] + 1; t.newest = len - 1; }
     else { t.b = r / a.P; len = r % a.P + 1; }
+    len = min(len, a.C);  // never past the (sequence, head) block
     // keys per split: fixed, or an even share of this row's keys
     const uint32_t chunk = a.chunk ? a.chunk : max(8u, ((len + a.S - 1) / a.S + 7u) & ~7u);
     t.begin = min(s * chunk, len);

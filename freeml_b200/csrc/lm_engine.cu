@@ -442,12 +442,14 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
 #pragma unroll
     for (int b = 0; b < SB; ++b) load_slot(b, g, b);
 
-    // gamma is a weight: staged before the wait (after the x rows in shared memory)
+    // gamma is a weight: staged before the wait (after the x rows in shared
+    // memory); every warp reads all of it, so a barrier follows
     const float4* gs4 = reinterpret_cast<const float4*>(xs + (uint64_t)MT * K);
     if constexpr (LN)
     {
         const float4* g4 = reinterpret_cast<const float4*>(a.gamma);
         for (uint32_t c = tid; c < K / 4; c += 128) const_cast<float4*>(gs4)[c] = g4[c];
+        __syncthreads();
     }
 
     griddep_launch_dependents();

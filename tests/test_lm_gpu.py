@@ -98,6 +98,28 @@ def test_checkpoint_loaded_engine_matches_reference_loop(golden, tmp_path):
     np.testing.assert_array_equal(toks[0, :meta["plen"] + n], ref_toks[:meta["plen"] + n])
 
 
+@pytest.mark.parametrize("batch", [32, 8])
+def test_decode_is_deterministic(batch):
+    """Two engines decoding config 3's shape from the same prompts give
+    bit-identical logits at every step: no kernel of the step depends on
+    timing (a cross-warp read of shared memory staged without a barrier, or
+    a split merge order, would show here long before it moves a token)."""
+    from freeml_b200.lm import CONFIGS, NanoLM, prompt_tokens, random_params
+    c = CONFIGS[3]
+    s = c["shape"]
+    params = random_params(s, c["wseed"], 0)
+    prompts = prompt_tokens(c["pseed"], s.vocab, batch, c["prompt"])
+    runs = []
+    for _ in range(2):
+        lm = NanoLM(s, batch)
+        lm.bind(params)
+        toks, logits = lm.generate(prompts, 96, want_logits=True)
+        lm.close()
+        runs.append((toks, logits))
+    np.testing.assert_array_equal(runs[0][0], runs[1][0])
+    np.testing.assert_array_equal(runs[0][1].view(np.uint32), runs[1][1].view(np.uint32))
+
+
 def test_graph_and_eager_steps_are_identical(golden):
     meta, g, _ = golden
     m = meta["greedy"]["cfg1"]
