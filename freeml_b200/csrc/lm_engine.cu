@@ -1010,8 +1010,14 @@ int launch_gemv_team(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 template <int MT, int EPI, bool LN>
 int launch_gemv_team_k(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 {
-    if (a.K <= 512) return launch_gemv_team<MT, 1, EPI, LN>(a, st, pdl, sms);
-    if (a.K <= 1024) return launch_gemv_team<MT, 2, EPI, LN>(a, st, pdl, sms);
+    uint32_t kw = a.K <= 512 ? 1u : (a.K <= 1024 ? 2u : 4u);
+    if (const char* e = getenv("FML_GEMV_KW"))  // tuning override: 1, 2 or 4
+    {
+        const long v = strtol(e, nullptr, 10);
+        if (v == 1 || v == 2 || v == 4) kw = (uint32_t)v;
+    }
+    if (kw == 1) return launch_gemv_team<MT, 1, EPI, LN>(a, st, pdl, sms);
+    if (kw == 2) return launch_gemv_team<MT, 2, EPI, LN>(a, st, pdl, sms);
     return launch_gemv_team<MT, 4, EPI, LN>(a, st, pdl, sms);
 }
 
