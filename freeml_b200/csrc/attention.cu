@@ -14,74 +14,6 @@
 
 namespace fml {
 
-// Causal attention for one query row over the cached keys 0..t
-// (CausalSelfAttentionLayer.h:424-499: Q_h K_h^T, * 1/sqrt(hd) + causal
-// mask, Softmax, P V_h), as one pass with an online softmax.
-// grid = (H, rows, S); 4 warps per CTA take 32-key tiles in turn.  Per tile a
-// lane holds HD/32 dims of q; the 32 partial dot products are summed by a
-// transpose-reduce, so lane j ends with key j's score; p_j is then
-// broadcast for the P.V update.  With S > 1 each CTA writes (m, l, acc) and
-// the last CTA of the (row, head) to finish merges the S partials.
-// ---- TMA bulk-copy + mbarrier helpers (sm_90+ PTX) -------------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p)
-{
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_fence_init()
-{
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-// One contiguous global -> shared copy by the TMA unit, completing on `bar`.
-// dst, src 16-byte aligned; bytes a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
-{
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-// Bounded wait for phase `parity` of `bar`: false if it did not complete
-// within the iteration limit (the caller reports a device error and stops).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity)
-{
-    const uint32_t addr = smem_u32(bar);
-    for (uint32_t it = 0; it < (1u << 24); ++it)
-    {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
-}
-
-#ifdef FML_TIMELINE
-int timeline_bind_attention(TimelineRec* p, uint32_t cap) { return timeline_bind_unit(p, cap); }
-#endif
-
-__device__ int g_attention_timeouts;  // wait limits hit (read by fml_device_error_count)
-
 // Causal attention for one query row over the cached keys 0..len-1
 // (CausalSelfAttentionLayer.h:424-499: Q_h K_h^T, * 1/sqrt(hd) + causal
 // mask, Softmax, P V_h) as one pass with an online softmax.
@@ -445,13 +377,13 @@ extern "C" {
 int fml_device_error_count(uint64_t* count)
 {
     FML_REQUIRE(count, "fml_device_error_count: null argument");
-    int v = 0, g = 0, f = 0;
+    int g = 0, f = 0;
     uint64_t tpw = 0;
-    FML_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_attention_timeouts, sizeof(int)));
+    FML_CUDA_TRY(cudaDeviceSynchronize());
     FML_RC(gemm_tc_error_count(&g));
     FML_RC(decode_step_error_count(&f));
     FML_RC(fml_lm_tp_error_count(&tpw));
-    *count = (uint64_t)v + (uint64_t)g + (uint64_t)f + tpw;
+    *count = (uint64_t)g + (uint64_t)f + tpw;
     return FML_OK;
 }
 

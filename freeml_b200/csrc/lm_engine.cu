@@ -990,12 +990,7 @@ int launch_gemv_team(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
         occ = b;
         occ_smem = smem;
     }
-    int per_sm = occ;
-    if (const char* e = getenv("FML_GEMV_OCC"))  // tuning: cap CTAs per SM
-    {
-        const long v = strtol(e, nullptr, 10);
-        if (v >= 1 && v < per_sm) per_sm = (int)v;
-    }
+    const int per_sm = occ;
     const unsigned gx = (a.M + MT - 1) / MT;
     const unsigned ngroups = (a.N + 3) / 4;
     const unsigned teams = 4 / KW;
