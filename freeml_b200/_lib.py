@@ -75,6 +75,14 @@ SIGNATURES = {
     "fml_lm_bind_packed": (_I, [_P, _P, _I, _P]),
     "fml_lm_param_count": (_U64, [ctypes.POINTER(LMConfig)]),
     "fml_lm_get_config": (_I, [_P, ctypes.POINTER(LMConfig)]),
+    "fml_matmul_left": (_I, [_P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _U64, _U64, _U64, _P]),
+    "fml_merge_qkv": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _P]),
+    "fml_gelu_derivative": (_I, [_P, _P, _U64, _P]),
+    "fml_softmax_backward": (_I, [_P, _P, _P, _U32, _U32, _P]),
+    "fml_scatter_add_rows": (_I, [_P, _P, _P, _U32, _U32, _U32, _U32, _U32, _P]),
+    "fml_layernorm_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _U32, _U32, ctypes.c_float, _P, _P]),
+    "fml_adamw_update": (_I, [_P, _P, _P, _P, _U64] + [ctypes.c_float] * 7 + [_P]),
+    "fml_xent_with_logits": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _I, _P, _P]),
     "fml_capture_begin": (_I, [ctypes.POINTER(_P)]),
     "fml_capture_end": (_I, [_P, ctypes.POINTER(_P)]),
     "fml_graph_launch": (_I, [_P, _P]),
@@ -114,6 +122,10 @@ def load(path: str | None = None):
     if _lib is not None:
         return _lib
     path = path or LIB_PATH
+    # torch first: the library links NCCL, and torch's own NCCL build must be
+    # the one the process resolves (loading ours first binds an older system
+    # copy that torch's CUDA library cannot use)
+    import torch  # noqa: F401
     if not os.path.exists(path):
         raise FmlError(2, "load", f"{path} not found -- build it with `python -m freeml_b200.build`")
     lib = ctypes.CDLL(path)

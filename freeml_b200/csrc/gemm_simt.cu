@@ -16,7 +16,7 @@ namespace fml {
 
 constexpr int GB_M = 128, GB_N = 128, GB_K = 16, GT_M = 8, GT_N = 8;
 
-template <bool TRANS_B>
+template <bool TRANS_B, bool TRANS_A = false>
 __global__ void __launch_bounds__(256) gemm_f32_kernel(float* __restrict__ C, const float* __restrict__ A,
                                                        const float* __restrict__ B, int M, int N, int K, int lda,
                                                        int ldb, int ldc, uint64_t plane_a, uint64_t plane_b,
@@ -41,9 +41,18 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(float* __restrict__ C, co
         for (int i = 0; i < 8; ++i)
         {
             const int e = tid + i * 256;           // 0..2047
-            const int am = e / GB_K, ak = e % GB_K;  // A tile row-major [128][16]
-            const int gm = m0 + am, gk = k0 + ak;
-            ra[i] = (gm < M && gk < K) ? A[(uint64_t)gm * lda + gk] : 0.0f;
+            if (TRANS_A)
+            {
+                const int ak = e / GB_M, am = e % GB_M;  // A^T rows are k, contiguous in m
+                const int gm = m0 + am, gk = k0 + ak;
+                ra[i] = (gm < M && gk < K) ? A[(uint64_t)gk * lda + gm] : 0.0f;
+            }
+            else
+            {
+                const int am = e / GB_K, ak = e % GB_K;  // A tile row-major [128][16]
+                const int gm = m0 + am, gk = k0 + ak;
+                ra[i] = (gm < M && gk < K) ? A[(uint64_t)gm * lda + gk] : 0.0f;
+            }
             if (TRANS_B)
             {
                 const int bn = e / GB_K, bk = e % GB_K;  // B rows are n, contiguous in k
@@ -63,7 +72,8 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(float* __restrict__ C, co
         for (int i = 0; i < 8; ++i)
         {
             const int e = tid + i * 256;
-            As[buf][e % GB_K][e / GB_K] = ra[i];
+            if (TRANS_A) As[buf][e / GB_M][e % GB_M] = ra[i];
+            else As[buf][e % GB_K][e / GB_K] = ra[i];
             if (TRANS_B) Bs[buf][e % GB_K][e / GB_K] = rb[i];
             else Bs[buf][e / GB_N][e % GB_N] = rb[i];
         }
@@ -135,6 +145,27 @@ int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int 
     }
     if (trans_b) gemm_f32_kernel<true><<<grid, 256, 0, st>>>(C, A, B, M, N, K, lda, ldb, ldc, pa, pb, pc);
     else gemm_f32_kernel<false><<<grid, 256, 0, st>>>(C, A, B, M, N, K, lda, ldb, ldc, pa, pb, pc);
+    FML_LAUNCH_CHECK();
+    return FML_OK;
+}
+
+// C = A^T . B with A [K x M] (row stride lda), B [K x N] (row stride ldb):
+// Mul<Left> / MatMul_Strided<Left> (MatrixBase_Mul.h:478-589, 617-722), one
+// accumulator per output summed over k in ascending order.
+int gemm_f32_ta(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, int batch,
+                uint64_t pa, uint64_t pb, uint64_t pc, cudaStream_t st)
+{
+    if (M <= 0 || N <= 0 || batch <= 0) return FML_OK;
+    dim3 grid((N + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M, batch);
+    FML_REQUIRE(grid.y <= 65535u && grid.z <= 65535u, "gemm: grid too large (M=%d batch=%d)", M, batch);
+    if (K <= 0)
+    {
+        for (int z = 0; z < batch; ++z)
+            for (int m = 0; m < M; ++m)
+                FML_CUDA_TRY(cudaMemsetAsync(C + z * pc + (uint64_t)m * ldc, 0, sizeof(float) * N, st));
+        return FML_OK;
+    }
+    gemm_f32_kernel<false, true><<<grid, 256, 0, st>>>(C, A, B, M, N, K, lda, ldb, ldc, pa, pb, pc);
     FML_LAUNCH_CHECK();
     return FML_OK;
 }

@@ -18,9 +18,13 @@
 //           the KV-cached decode engine (fml_lm_*) bound to this model's
 //           weight matrices (device pointers taken from its Datablobs)
 //   weights --out F    every parameter in the canonical order
+//   train   --tokens F --iters N [--lr X] --out-losses F --out F
+//           N NanoLLM training iterations (forward, loss, backward, AdamW)
 // Shape flags: --vocab --ctx --d --heads --layers --wseed
 #include <ModelLibrary/Model.h>
 #include <LayerLibrary/Layers.h>
+#include <LossLibrary/Losses.h>
+#include <OptimiserLibrary/Optimisers.h>
 #include <MatrixLibrary/MatrixBase_Functions.h>
 #include <ToolsLibrary/Tools.h>
 
@@ -89,11 +93,10 @@ struct Built
 
 // NanoLLM.cpp:268-358 and :383-399, inference flavour (initForTraining =
 // false: the same weight draws, no gradient buffers), dropout 0, no bias.
-Built Build(const Shape& s)
+Built Build(const Shape& s, bool train = false, float lr = 1e-4f)
 {
     Mgr& inst = Mgr::Instance();
     RandomUtils::GetGenerator().seed(s.wseed);
-    const bool train = false;
     Built b;
     b.model = std::make_unique<Model<T, Mat>>();
     Model<T, Mat>* m = b.model.get();
@@ -142,6 +145,11 @@ Built Build(const Shape& s)
     m->AddLayer(head, headBlob);
     m->AddDependency(head, 0, flat, 0);
     m->SetFinalOutputLayer(head);
+    if (train)  // NanoLLM.cpp:350-352
+    {
+        m->SetOptimiser(new AdamWOptimiser<T, Mat>(lr, 0.9f, 0.999f, 1e-8f, 0.01f));
+        m->SetLoss(new CategoricalCrossEntropyWithLogits<T, Mat>());
+    }
     m->SetExpectedInputDims({1u, s.C, 1u});
     m->Init();
 
@@ -281,9 +289,8 @@ int Engine(const Shape& s, const Args& a)
     return 0;
 }
 
-int DumpWeights(const Shape& s, const Args& a)
+std::vector<float> PackWeights(Built& b, const Shape& s)
 {
-    Built b = Build(s);
     LayerWeights lw = Weights(b.model.get(), s.L);
     std::vector<float> out;
     auto app = [&](Mat* m) { const float* p = m->DataRead(); out.insert(out.end(), p, p + m->GetElementCount()); };
@@ -294,7 +301,67 @@ int DumpWeights(const Shape& s, const Args& a)
         app(lw.ln0[i]); app(lw.wqkv[i]); app(lw.wproj[i]); app(lw.ln1[i]); app(lw.wfc[i]); app(lw.wmlp[i]);
     }
     app(lw.lnf);
-    WriteRaw(a.get("out"), out);
+    return out;
+}
+
+int DumpWeights(const Shape& s, const Args& a)
+{
+    Built b = Build(s);
+    WriteRaw(a.get("out"), PackWeights(b, s));
+    return 0;
+}
+
+// NanoLLM's training iteration (NanoLLM.cpp:404-440): Model::Run(window,
+// target) = forward, CategoricalCrossEntropyWithLogits gradient and loss,
+// backward, AdamW step, on consecutive windows of the stream --tokens F
+// (C + iters ids): iteration i trains on [i, i + C) -> [i + 1, i + C + 1).
+// Writes the losses (float64) and the parameters after the last step;
+// prints the host transfers and kernel launches inside the Run calls after
+// the first (which also uploads the host-written init data) and their time
+// per iteration.
+int Train(const Shape& s, const Args& a)
+{
+    const uint32_t iters = a.u("iters", 2);
+    const float lr = a.has("lr") ? std::strtof(a.get("lr").c_str(), nullptr) : 1e-4f;
+    std::vector<uint32_t> toks = ReadU32(a.get("tokens"));
+    if (toks.size() < (size_t)s.C + iters) { std::fprintf(stderr, "need C + iters tokens\n"); return 2; }
+    Built b = Build(s, true, lr);
+    auto target = Mgr::Instance().AllocateMatrix({1u, s.C, 1u}, "Target");
+    std::vector<double> losses;
+    uint64_t transfers = 0, launches = 0;
+    double seconds = 0.0;
+    for (uint32_t it = 0; it < iters; ++it)
+    {
+        float* w = b.window->DataWrite();
+        float* tg = target->DataWrite();
+        for (uint32_t t = 0; t < s.C; ++t)
+        {
+            w[t] = (float)toks[it + t];
+            tg[t] = (float)toks[it + t + 1];
+        }
+        b.window->Flush();
+        target->Flush();
+        fml_synchronize();
+        const auto t0 = Mat::HostTransfers();
+        const uint64_t l0 = fml_kernel_launch_count();
+        const auto c0 = std::chrono::steady_clock::now();
+        b.model->Run(b.window.get(), target.get(), true);
+        fml_synchronize();
+        if (it > 0) seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - c0).count();
+        const auto t1 = Mat::HostTransfers();
+        if (it > 0)  // the first Run also uploads the host-written init data
+        {
+            launches += fml_kernel_launch_count() - l0;
+            transfers += (t1.downloads - t0.downloads) + (t1.uploads - t0.uploads);
+        }
+        losses.push_back(b.model->GetLastLoss());
+    }
+    if (a.has("out-losses")) WriteRaw(a.get("out-losses"), losses);
+    if (a.has("out")) WriteRaw(a.get("out"), PackWeights(b, s));
+    std::printf("{\"iters\": %u, \"host_transfers_in_run\": %llu, \"kernel_launches_in_run\": %llu, "
+                "\"ms_per_iter\": %.4f}\n",
+                iters, (unsigned long long)transfers, (unsigned long long)launches,
+                iters > 1 ? 1e3 * seconds / (iters - 1) : 0.0);
     return 0;
 }
 
@@ -303,7 +370,7 @@ int DumpWeights(const Shape& s, const Args& a)
 int main(int argc, char** argv)
 {
     Tools::Logger::SetMinLevel(Tools::Logger::Level::Error);
-    if (argc < 2) { std::fprintf(stderr, "usage: %s greedy|engine|weights [--key value]...\n", argv[0]); return 2; }
+    if (argc < 2) { std::fprintf(stderr, "usage: %s greedy|engine|weights|train [--key value]...\n", argv[0]); return 2; }
     Args a;
     for (int i = 2; i + 1 < argc; i += 2)
         if (std::string(argv[i]).rfind("--", 0) == 0) a.kv[std::string(argv[i]).substr(2)] = argv[i + 1];
@@ -312,6 +379,7 @@ int main(int argc, char** argv)
     if (mode == "greedy") return Greedy(s, a);
     if (mode == "engine") return Engine(s, a);
     if (mode == "weights") return DumpWeights(s, a);
+    if (mode == "train") return Train(s, a);
     std::fprintf(stderr, "unknown mode %s\n", mode.c_str());
     return 2;
 }

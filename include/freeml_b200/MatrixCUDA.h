@@ -196,9 +196,20 @@ public:
     static freeml_cuda::Counters HostTransfers() { return freeml_cuda::GlobalCounters(); }
 
     // ---- host access ----------------------------------------------------
+    // FML_TRACE_HOST=1: name every matrix whose host access moves data
+    // (debugging aid for finding operators that run on the host mirror)
+    void TraceHost(const char* what) const
+    {
+        static const bool on = std::getenv("FML_TRACE_HOST") != nullptr;
+        if (on && m_storage && !m_storage->host_valid)
+            std::fprintf(stderr, "freeml_b200 host %s: %s [%u x %u x %u]\n", what, this->m_name.c_str(),
+                         this->GetDimsX(), this->GetDimsY(), this->GetDimsZ());
+    }
+
     T* DataWrite() override
     {
         if (!m_storage) return nullptr;
+        TraceHost("write");
         m_storage->Download();
         m_storage->host_dirty = true;
         return reinterpret_cast<T*>(m_storage->host.data()) + m_offset;
@@ -207,6 +218,7 @@ public:
     const T* DataRead() override
     {
         if (!m_storage) return nullptr;
+        TraceHost("read");
         m_storage->Download();
         return reinterpret_cast<const T*>(m_storage->host.data()) + m_offset;
     }

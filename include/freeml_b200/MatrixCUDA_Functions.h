@@ -5,18 +5,21 @@
 // MatrixLibrary/MatrixBase_Functions.h and MatrixBase_Mul.h -- the same
 // mechanism as MatrixLibrary/GPU/DirectX11/MatrixDX11_Functions.h.
 //
-// Every operator the NanoLLM inference forward reaches runs on the device.
-// Training-only forms (Mul<Left|Both>, MatMul_Strided with column strides
-// other than 1, the backward operators) are not overloaded and run FreeML's
-// own host templates through the host mirror; MatrixCUDA counts those
-// transfers so a test can assert that Model::Run performed none.
+// Every operator the NanoLLM forward and training iteration (backward,
+// CategoricalCrossEntropyWithLogits, AdamW) reach runs on the device.
+// Other forms (Mul<Both>, MatMul_Strided with column strides other than 1)
+// run FreeML's own host templates through the host mirror; MatrixCUDA counts
+// those transfers so a test can assert that Model::Run performed none.
 #pragma once
 
 #include <algorithm>
+#include <cmath>
 #include <vector>
 
 #include <MatrixLibrary/MatrixBase_Functions.h>
 #include <MatrixLibrary/MatrixBase_Mul.h>
+#include <LossLibrary/CategoricalCrossEntropyWithLogits.h>
+#include <OptimiserLibrary/AdamWOptimiser.h>
 
 #include "../freeml_cuda.h"
 #include "MatrixCUDA.h"
@@ -239,8 +242,9 @@ void SplitQKV(MatrixCUDA<T>* _q, MatrixCUDA<T>* _k, MatrixCUDA<T>* _v, MatrixCUD
                            _q->GetDimsX(), freeml_cuda::Stream()));
 }
 
-// Mul<Mode>  MatrixBase_Mul.h:591-615.  None and Right run on the device;
-// Left / Both (gradient products) use FreeML's host template.
+// Mul<Mode>  MatrixBase_Mul.h:591-615.  None, Right and Left (the weight
+// gradients, Dense.h:258-275) run on the device; Both uses FreeML's host
+// template.
 template <TransposeMode Mode = TransposeMode::None, class T>
 void Mul(MatrixCUDA<T>* _out, MatrixCUDA<T>* _L, MatrixCUDA<T>* _R, uint32_t blockSize = 32, uint32_t numThreads = 12,
          ThreadPool* pool = nullptr)
@@ -254,6 +258,13 @@ void Mul(MatrixCUDA<T>* _out, MatrixCUDA<T>* _L, MatrixCUDA<T>* _R, uint32_t blo
         const float* r = _R->DevIn();
         FML_CALL(fml_matmul(_out->DevOut(), l, r, M, N, K, tb ? 1 : 0, freeml_cuda::Stream()));
     }
+    else if constexpr (Mode == TransposeMode::Left)
+    {
+        const uint32_t M = _L->GetDimsX(), K = _L->GetDimsY(), N = _R->GetDimsX();
+        const float* l = _L->DevIn();
+        const float* r = _R->DevIn();
+        FML_CALL(fml_matmul_left(_out->DevOut(), l, r, M, N, K, M, N, N, 1, 0, 0, 0, freeml_cuda::Stream()));
+    }
     else
     {
         Mul<Mode, T>(static_cast<MatrixBase<T>*>(_out), static_cast<MatrixBase<T>*>(_L),
@@ -261,7 +272,7 @@ void Mul(MatrixCUDA<T>* _out, MatrixCUDA<T>* _L, MatrixCUDA<T>* _R, uint32_t blo
     }
 }
 
-// MatMul_Strided<Mode>  MatrixBase_Mul.h:617-722 for None / Right with column
+// MatMul_Strided<Mode>  MatrixBase_Mul.h:617-722 for None / Right / Left with column
 // strides of 1 (the form CausalSelfAttentionLayer.h:445-497 uses), one
 // contraction per z plane with the reference's plane strides (row stride x
 // rows).  Other forms use FreeML's host template.
@@ -271,6 +282,20 @@ void MatMul_Strided(MatrixCUDA<T>* _out, MatrixCUDA<T>* _L, MatrixCUDA<T>* _R, u
                     uint32_t outColStride, uint32_t blockSize = 32, uint32_t numThreads = 12,
                     ThreadPool* pool = nullptr)
 {
+    if constexpr (Mode == TransposeMode::Left)
+    {
+        if (L_colStride == 1 && R_colStride == 1 && outColStride == 1)
+        {
+            const uint32_t M = _L->GetDimsX(), K = _L->GetDimsY(), N = _R->GetDimsX();
+            const uint32_t batch = _L->GetDimsZ() ? _L->GetDimsZ() : 1;
+            const float* l = _L->DevIn();
+            const float* r = _R->DevIn();
+            FML_CALL(fml_matmul_left(_out->DevOut(), l, r, M, N, K, L_rowStride, R_rowStride, outRowStride, batch,
+                                     (uint64_t)L_rowStride * _L->GetDimsY(), (uint64_t)R_rowStride * _R->GetDimsY(),
+                                     (uint64_t)outRowStride * _out->GetDimsY(), freeml_cuda::Stream()));
+            return;
+        }
+    }
     if constexpr (Mode == TransposeMode::None || Mode == TransposeMode::Right)
     {
         if (L_colStride == 1 && R_colStride == 1 && outColStride == 1)
@@ -291,6 +316,162 @@ void MatMul_Strided(MatrixCUDA<T>* _out, MatrixCUDA<T>* _L, MatrixCUDA<T>* _R, u
     MatMul_Strided<Mode, T>(static_cast<MatrixBase<T>*>(_out), static_cast<MatrixBase<T>*>(_L),
                             static_cast<MatrixBase<T>*>(_R), L_rowStride, L_colStride, R_rowStride, R_colStride,
                             outRowStride, outColStride, blockSize, numThreads, pool);
+}
+
+// ---- training: backward operators, the loss and the optimiser step -------
+
+namespace freeml_cuda {
+// Grow-only device scratch for operators that need temporary space (slot:
+// one per operator kind); the C ABI itself never allocates.
+inline float* Scratch(size_t floats, int slot)
+{
+    static float* ptr[4] = {};
+    static size_t have[4] = {};
+    if (have[slot] < floats)
+    {
+        if (ptr[slot]) fml_device_free(ptr[slot]);
+        ptr[slot] = nullptr;
+        Check(fml_device_alloc(reinterpret_cast<void**>(&ptr[slot]), floats * sizeof(float)), "fml_device_alloc");
+        have[slot] = floats;
+    }
+    return ptr[slot];
+}
+}  // namespace freeml_cuda
+
+// MergeQKV  MatrixBase_Functions.h:369-431 (CausalSelfAttentionLayer.h backward)
+template <class T>
+void MergeQKV(MatrixCUDA<T>* _packedQKV, MatrixCUDA<T>* _qHeads, MatrixCUDA<T>* _kHeads, MatrixCUDA<T>* _vHeads)
+{
+    const float* q = _qHeads->DevIn();
+    const float* k = _kHeads->DevIn();
+    const float* v = _vHeads->DevIn();
+    FML_CALL(fml_merge_qkv(_packedQKV->DevOut(), q, k, v, _qHeads->GetDimsX(), _qHeads->GetDimsY(),
+                           _qHeads->GetDimsZ() ? _qHeads->GetDimsZ() : 1, freeml_cuda::Stream()));
+}
+
+// GeluDerivtiveMat  MatrixBase_Functions.h:1003-1018 (Gelu.h:40-46)
+template <class T>
+void GeluDerivtiveMat(MatrixCUDA<T>* _out, MatrixCUDA<T>* _in)
+{
+    const float* in = _in->DevIn();
+    FML_CALL(fml_gelu_derivative(_out->DevOut(), in, _in->GetElementCount(), freeml_cuda::Stream()));
+}
+
+// SoftmaxBackwards  MatrixBase_Functions.h:82-111 (rows = dims y, as there)
+template <class T>
+void SoftmaxBackwards(MatrixCUDA<T>* _out, MatrixCUDA<T>* _softmaxOut, MatrixCUDA<T>* _gradIn)
+{
+    const float* y = _softmaxOut->DevIn();
+    const float* g = _gradIn->DevIn();
+    FML_CALL(fml_softmax_backward(_out->DevOut(), y, g, _softmaxOut->GetDimsY(), _softmaxOut->GetDimsX(),
+                                  freeml_cuda::Stream()));
+}
+
+// ScatterAddRows  MatrixBase_Functions.h:285-320 (Embedding.h backward)
+template <class T>
+void ScatterAddRows(MatrixCUDA<T>* _out, MatrixCUDA<T>* _src, MatrixCUDA<T>* _indices)
+{
+    const float* src = _src->DevIn();
+    const float* idx = _indices->DevIn();
+    // the output accumulates: read-modify-write on the device
+    float* out = const_cast<float*>(_out->DevIn());
+    _out->DevOut();
+    FML_CALL(fml_scatter_add_rows(out, src, idx, _src->GetDimsY(), _src->GetDimsX(), _out->GetDimsY(),
+                                  _src->GetDimsZ() ? _src->GetDimsZ() : 1, _out->GetDimsZ() ? _out->GetDimsZ() : 1,
+                                  freeml_cuda::Stream()));
+}
+
+// LayerNormBackwardsOp  MatrixBase_Functions.h:552-705
+template <class T>
+void LayerNormBackwardsOp(MatrixCUDA<T>* _dX, MatrixCUDA<T>* _dY, MatrixCUDA<T>* _in, MatrixCUDA<T>* _gamma,
+                          MatrixCUDA<T>* _dGamma, MatrixCUDA<T>* _dBeta = nullptr, MatrixCUDA<T>* _xHat = nullptr,
+                          T _eps = static_cast<T>(1e-5))
+{
+    const uint32_t rows = _in->GetDimsY() * _in->GetDimsZ(), cols = _in->GetDimsX();
+    const float* dy = _dY->DevIn();
+    const float* in = _in->DevIn();
+    const float* g = _gamma->DevIn();
+    const float* xh = _xHat ? _xHat->DevIn() : nullptr;
+    float* db = _dBeta ? _dBeta->DevOut() : nullptr;
+    FML_CALL(fml_layernorm_backward(_dX->DevOut(), dy, in, g, _dGamma->DevOut(), db, xh, rows, cols, _eps,
+                                    xh ? nullptr : freeml_cuda::Scratch(2 * (size_t)rows, 0), freeml_cuda::Stream()));
+}
+
+// AdamWUpdate  MatrixBase_Functions.h:1498-1545 (AdamWOptimiser::Step)
+template <class T>
+void AdamWUpdate(MatrixCUDA<T>* _param, MatrixCUDA<T>* _grad, MatrixCUDA<T>* _mt, MatrixCUDA<T>* _vt, T _lr,
+                 T _beta1, T _beta2, T _beta1_pow_t, T _beta2_pow_t, T _eps, T _weightDecay)
+{
+    const float* g = _grad->DevIn();
+    FML_CALL(fml_adamw_update(_param->DevOut(), g, _mt->DevOut(), _vt->DevOut(), _param->GetElementCount(), _lr,
+                              _beta1, _beta2, _beta1_pow_t, _beta2_pow_t, _eps, _weightDecay, freeml_cuda::Stream()));
+}
+
+// CategoricalCrossEntropyWithLogits for MatrixCUDA: the loss and its
+// (negative) gradient on the device -- the same class specialisation
+// mechanism as the DirectX11 backend's
+// (LossLibrary/CategoricalCrossEntropyWithLogits.h:219-222).
+template <class T>
+class CategoricalCrossEntropyWithLogits<T, MatrixCUDA<T>> : public LossBase<T, MatrixCUDA<T>>
+{
+public:
+    const char* GetName() const override { return "CategoricalCrossEntropyWithLogits"; }
+
+    T Loss(MatrixCUDA<T>* target, MatrixCUDA<T>* logits) override
+    {
+        float loss = 0.0f;
+        Run(nullptr, target, logits, &loss);
+        return loss;
+    }
+
+    void Gradient(MatrixCUDA<T>* out, MatrixCUDA<T>* target, MatrixCUDA<T>* logits) override
+    {
+        Run(out, target, logits, nullptr);
+    }
+
+private:
+    static void Run(MatrixCUDA<T>* out, MatrixCUDA<T>* target, MatrixCUDA<T>* logits, float* loss)
+    {
+        const uint32_t vocab = logits->GetDimsX(), steps = logits->GetDimsY();
+        const uint32_t planes = logits->GetDimsZ() ? logits->GetDimsZ() : 1;
+        if (!vocab || !steps) return;
+        const size_t rows = (size_t)steps * planes;
+        const float* tg = target->DevIn();
+        const float* lg = logits->DevIn();
+        // the loss alone still computes the gradient rows: into scratch
+        float* grad = out ? out->DevOut() : freeml_cuda::Scratch(rows * vocab, 1);
+        FML_CALL(fml_xent_with_logits(grad, loss, tg, lg, vocab, steps, planes,
+                                      target->GetDimsZ() ? target->GetDimsZ() : 1, target->GetDimsX() == 1u ? 1 : 0,
+                                      loss ? freeml_cuda::Scratch(rows + 1, 2) : nullptr, freeml_cuda::Stream()));
+    }
+};
+
+// AdamWOptimiser::Step (OptimiserLibrary/AdamWOptimiser.h:131-196) for
+// MatrixCUDA: the reference's state handling (lazy moments cleared to zero,
+// a step count per parameter, bias-correction powers) with the update on
+// the device -- its generic branch casts to MatrixBase<T>*, which would
+// select FreeML's host AdamWUpdate.
+template <>
+inline void AdamWOptimiser<float, MatrixCUDA<float>>::Step(MatrixCUDA<float>* param, MatrixCUDA<float>* grad)
+{
+    MatrixCUDA<float>* key = param;
+    if (m_momentzero.find(key) == m_momentzero.end())
+    {
+        MatrixManager<float, MatrixCUDA<float>>& inst = MatrixManager<float, MatrixCUDA<float>>::Instance();
+        m_momentzero[key] = inst.AllocateMatrix(param->GetDims(), "adamw_m");
+        m_momentone[key] = inst.AllocateMatrix(param->GetDims(), "adamw_v");
+        Clear(m_momentzero[key].get());
+        Clear(m_momentone[key].get());
+        m_timestep[key] = 0;
+    }
+    auto& mt = m_momentzero[key];
+    auto& vt = m_momentone[key];
+    uint64_t& t = m_timestep[key];
+    ++t;
+    const float beta1_pow_t = std::pow(m_beta1, t);
+    const float beta2_pow_t = std::pow(m_beta2, t);
+    AdamWUpdate(param, grad, mt.get(), vt.get(), m_learningRate, m_beta1, m_beta2, beta1_pow_t, beta2_pow_t, m_epsilon,
+                m_weightDecay);
 }
 
 #undef FML_CALL

@@ -160,6 +160,50 @@ FML_API int fml_matmul_strided(float* out, const float* a, const float* b, uint3
                        uint32_t lda, uint32_t ldb, uint32_t ldc, int trans_b, uint32_t batch,
                        uint64_t plane_a, uint64_t plane_b, uint64_t plane_c, fml_stream_t stream);
 
+/* ---- Training (Model::Run(input, target), ModelLibrary/Model.h:785-840) ----
+ * Mul<Left>(out, L, R) and MatMul_Strided<Left> with column strides of 1
+ * (MatrixBase_Mul.h:478-589, 617-722): out[M x N] = L^T . R with L [K x M]
+ * (row stride lda) and R [K x N] (row stride ldb), `batch` planes. */
+FML_API int fml_matmul_left(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K,
+                    uint32_t lda, uint32_t ldb, uint32_t ldc, uint32_t batch, uint64_t plane_a, uint64_t plane_b,
+                    uint64_t plane_c, fml_stream_t stream);
+/* MergeQKV(packed, qHeads, kHeads, vHeads)  MatrixBase_Functions.h:369-431:
+ * per-head [heads][tokens][head_dim] back into [tokens][3 * heads * head_dim] */
+FML_API int fml_merge_qkv(float* packed, const float* q, const float* k, const float* v, uint32_t head_dim,
+                  uint32_t tokens, uint32_t heads, fml_stream_t stream);
+/* GeluDerivtiveMat  MatrixBase_Functions.h:1003-1018 */
+FML_API int fml_gelu_derivative(float* out, const float* in, uint64_t n, fml_stream_t stream);
+/* SoftmaxBackwards(out, softmaxOut, gradIn)  MatrixBase_Functions.h:82-111 (row-wise) */
+FML_API int fml_softmax_backward(float* out, const float* y, const float* g, uint32_t rows, uint32_t cols,
+                         fml_stream_t stream);
+/* ScatterAddRows(out, src, indices)  MatrixBase_Functions.h:285-320: out row
+ * indices[r] += src row r for `planes` planes of src_rows rows; out has 1 or
+ * `planes` planes of out_rows rows; indices are token ids stored as floats;
+ * rows are added with atomics (the sum order is not the reference's). */
+FML_API int fml_scatter_add_rows(float* out, const float* src, const float* indices, uint32_t src_rows,
+                         uint32_t width, uint32_t out_rows, uint32_t planes, uint32_t out_planes,
+                         fml_stream_t stream);
+/* LayerNormBackwardsOp(dX, dY, in, gamma, dGamma, dBeta, xHat, eps)
+ * MatrixBase_Functions.h:552-705 over rows x cols (dBeta, xHat optional);
+ * without xHat, `workspace` holds 2 floats per row. */
+FML_API int fml_layernorm_backward(float* dx, const float* dy, const float* in, const float* gamma, float* dgamma,
+                           float* dbeta, const float* xhat, uint32_t rows, uint32_t cols, float eps,
+                           void* workspace, fml_stream_t stream);
+/* AdamWUpdate  MatrixBase_Functions.h:1498-1545 (param += update - decay) */
+FML_API int fml_adamw_update(float* param, const float* grad, float* mt, float* vt, uint64_t n, float lr,
+                     float beta1, float beta2, float beta1_pow_t, float beta2_pow_t, float eps,
+                     float weight_decay, fml_stream_t stream);
+/* CategoricalCrossEntropyWithLogits  LossLibrary/CategoricalCrossEntropyWithLogits.h:
+ * 29-217 over `planes` x `steps` rows of `vocab` logits: the negative
+ * gradient into `grad` and, when loss_out is not null, the loss into
+ * *loss_out (host; synchronises the stream; `workspace` = rows + 1 floats).
+ * target_ids = 1: target [target_planes][steps] token ids as floats (-1
+ * ignored; gradient scaled by 1 / valid rows, loss = mean); 0: dense target
+ * rows [target_planes][steps][vocab] (loss = sum). */
+FML_API int fml_xent_with_logits(float* grad, float* loss_out, const float* target, const float* logits,
+                         uint32_t vocab, uint32_t steps, uint32_t planes, uint32_t target_planes, int target_ids,
+                         void* workspace, fml_stream_t stream);
+
 /* Causal attention of one query row per sequence over a KV cache -- the
  * attention core of CausalSelfAttentionLayer::Forward
  * (LayerLibrary/CausalSelfAttentionLayer.h:424-499: MatMul_Strided<Right>

@@ -265,6 +265,17 @@ def ref_vocab(corpus: bytes, text: bytes, ids: np.ndarray) -> dict:
                 "decode_tokens": rd("decode_tokens.bin")}
 
 
+def ref_train(s: LMShape, wseed: int, pseed: int, iters: int, lr: float = 1e-4):
+    """NanoLLM training iterations on FreeML's CPU path (Model::Run(window,
+    target): forward, cross-entropy, backward, AdamW) over the seeded token
+    stream; returns (losses [iters] float64, parameters after the last step)."""
+    with tempfile.TemporaryDirectory() as td:
+        lf, wf = os.path.join(td, "l.bin"), os.path.join(td, "w.bin")
+        subprocess.run([REF_BIN, "train", *_shape_args(s, wseed), "--iters", str(iters), "--pseed", str(pseed),
+                        "--lr", repr(float(lr)), "--out-losses", lf, "--out", wf], check=True, capture_output=True)
+        return np.fromfile(lf, np.float64), np.fromfile(wf, np.float32)
+
+
 def ref_forward(s: LMShape, wseed: int, window: np.ndarray) -> np.ndarray:
     with tempfile.TemporaryDirectory() as td:
         wf, lf = os.path.join(td, "w.bin"), os.path.join(td, "l.bin")

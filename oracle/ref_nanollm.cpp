@@ -29,8 +29,12 @@
 //   time     --forwards K --warmup W      seconds per full-window Run (JSON line)
 //   op       --op NAME --in F --out F ... one generic operator on given inputs
 //   save     --dir D --name N             Model::Save of the built model into D/N
+//   train    --iters N --pseed S [--lr X] --out-losses F --out F
+//            N training iterations of Model::Run(window, target)
 #include <ModelLibrary/Model.h>
 #include <LayerLibrary/Layers.h>
+#include <LossLibrary/Losses.h>
+#include <OptimiserLibrary/Optimisers.h>
 #include <MatrixLibrary/CPU/MatrixCPU.h>
 #include <MatrixLibrary/MatrixBase_Functions.h>
 #include <MatrixLibrary/MatrixBase_Mul.h>
@@ -140,11 +144,10 @@ struct Built
 // Mirrors BuildOrLoadModel (NanoLLM.cpp:268-358) and AllocateTrainingMatrices
 // (NanoLLM.cpp:383-399) for inference: initForTraining = false (the same
 // weight draws, no gradient buffers), dropout 0, use_bias false.
-static Built BuildModel(const LMConfig& cfg)
+static Built BuildModel(const LMConfig& cfg, bool train = false, float lr = 1e-4f)
 {
     Mgr& inst = Mgr::Instance();
     RandomUtils::GetGenerator().seed(cfg.wseed);
-    const bool train = false;
     Built b;
     b.model = std::make_unique<Model<T, Mat>>();
     Model<T, Mat>* model = b.model.get();
@@ -204,6 +207,11 @@ static Built BuildModel(const LMConfig& cfg)
     model->AddDependency(head, 0, flat, 0);
     model->SetFinalOutputLayer(head);
 
+    if (train)  // NanoLLM.cpp:350-352
+    {
+        model->SetOptimiser(new AdamWOptimiser<T, Mat>(lr, 0.9f, 0.999f, 1e-8f, 0.01f));
+        model->SetLoss(new CategoricalCrossEntropyWithLogits<T, Mat>());
+    }
     model->SetExpectedInputDims({1u, cfg.C, 1u});
     model->Init();
 
@@ -318,6 +326,37 @@ static int ModeWeights(const Args& a)
     LMConfig cfg = ConfigFrom(a);
     Built b = BuildModel(cfg);
     WriteRaw(a.get("out"), DumpWeights(b, cfg));
+    return 0;
+}
+
+// NanoLLM's training iteration (NanoLLM.cpp:404-440: Model::Run(input,
+// target) = forward, CategoricalCrossEntropyWithLogits gradient and loss,
+// backward, AdamW step) on consecutive windows of one seeded token stream:
+// iteration i trains on tokens [i, i + C) -> [i + 1, i + C + 1).  Writes the
+// per-iteration losses (float64) and the parameters after the last step.
+static int ModeTrain(const Args& a)
+{
+    LMConfig cfg = ConfigFrom(a);
+    const uint32_t iters = a.u("iters", 2);
+    const float lr = a.has("lr") ? std::strtof(a.get("lr").c_str(), nullptr) : 1e-4f;
+    Built b = BuildModel(cfg, true, lr);
+    const std::vector<uint32_t> toks = PromptTokens(a.u("pseed", 1), cfg.V, (size_t)cfg.C + iters);
+    auto target = Mgr::Instance().AllocateMatrix({1u, cfg.C, 1u}, "Target");
+    std::vector<double> losses;
+    for (uint32_t it = 0; it < iters; ++it)
+    {
+        float* w = b.window->DataWrite();
+        float* tg = target->DataWrite();
+        for (uint32_t t = 0; t < cfg.C; ++t)
+        {
+            w[t] = (float)toks[it + t];
+            tg[t] = (float)toks[it + t + 1];
+        }
+        b.model->Run(b.window.get(), target.get(), true);
+        losses.push_back(b.model->GetLastLoss());
+    }
+    if (a.has("out-losses")) WriteRaw(a.get("out-losses"), losses);
+    if (a.has("out")) WriteRaw(a.get("out"), DumpWeights(b, cfg));
     return 0;
 }
 
@@ -460,13 +499,14 @@ static int ModeOp(const Args& a)
 int main(int argc, char** argv)
 {
     Tools::Logger::SetMinLevel(Tools::Logger::Level::Error);
-    if (argc < 2) { std::fprintf(stderr, "usage: %s weights|greedy|forward|time|op|save [--key value]...\n", argv[0]); return 2; }
+    if (argc < 2) { std::fprintf(stderr, "usage: %s weights|greedy|forward|time|op|save|train [--key value]...\n", argv[0]); return 2; }
     const std::string mode = argv[1];
     Args a = ParseArgs(argc, argv, 2);
     if (mode == "greedy") return ModeGreedy(a);
     if (mode == "forward") return ModeForward(a);
     if (mode == "weights") return ModeWeights(a);
     if (mode == "save") return ModeSave(a);
+    if (mode == "train") return ModeTrain(a);
     if (mode == "time") return ModeTime(a);
     if (mode == "op") return ModeOp(a);
     std::fprintf(stderr, "unknown mode %s\n", mode.c_str());

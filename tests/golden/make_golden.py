@@ -6,6 +6,7 @@ Run (in a container that has the FreeML tree and the built harness):
     python tests/golden/make_golden.py              # every fixture
     python tests/golden/make_golden.py checkpoint   # only ckpt_tiny.tgz
     python tests/golden/make_golden.py vocab        # only vocab.npz
+    python tests/golden/make_golden.py train        # only train_tiny.npz
 
 Every number below comes from ``oracle/_ref/ref_nanollm`` -- the unmodified
 reference ``Model<float, MatrixCPU<float>>`` and its generic operators -- never
@@ -62,6 +63,19 @@ def make_checkpoint() -> dict:
                                  "tokens": [int(t) for t in toks]}}
 
 
+# NanoLLM training iterations on the reference CPU path (losses and the
+# parameters after the last AdamW step), committed as train_tiny.npz
+TRAIN_CASE = ("train_tiny", O.LMShape(V=61, C=16, d=32, H=1, L=2), 11, 5, 3)
+
+
+def make_train() -> None:
+    name, s, wseed, pseed, iters = TRAIN_CASE
+    losses, w = O.ref_train(s, wseed, pseed, iters)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), losses=losses, weights=w,
+                        shape=np.array([s.V, s.C, s.d, s.H, s.L, wseed, pseed, iters], np.int64))
+    print(name, "losses", losses)
+
+
 def make_vocab() -> None:
     """NanoLLM's vocabulary code on a synthetic byte corpus (bytes on both
     sides of 0x80, some absent), a text with absent bytes and ids past the
@@ -102,6 +116,7 @@ def main():
         print(name, "tokens", toks[:8], "...")
     meta["checkpoint"] = make_checkpoint()
     make_vocab()
+    make_train()
     for name, s, wseed in HASH_CASES:
         w = O.ref_weights(s, wseed)
         meta["weights_sha256"][name] = {"V": s.V, "C": s.C, "d": s.d, "H": s.H, "L": s.L, "wseed": wseed,
@@ -164,7 +179,10 @@ def main():
 
 
 if __name__ == "__main__":
-    if sys.argv[1:] == ["vocab"]:  # refresh only vocab.npz
+    if sys.argv[1:] == ["train"]:  # refresh only train_tiny.npz
+        assert O.ref_available(), "build oracle/_ref first (make -C oracle all)"
+        make_train()
+    elif sys.argv[1:] == ["vocab"]:  # refresh only vocab.npz
         assert os.path.exists(O.REF_VOCAB_BIN), "build oracle/_ref first (make -C oracle all)"
         make_vocab()
     elif sys.argv[1:] == ["checkpoint"]:  # refresh only the checkpoint fixture
