@@ -15,7 +15,8 @@
 //
 // Precision: kind::tf32 reads only the top 19 bits of each fp32 operand.
 // TF32x3 (default) splits x = hi + lo with hi = x with the low 13 bits
-// cleared (written back in place) and lo = x - hi (exact in fp32), then sums
+// cleared -- which is what the MMA reads from the staged tile itself, so hi
+// is never written -- and lo = x - hi (exact in fp32), then sums
 // hi*hi + hi*lo + lo*hi in the fp32 accumulator -- fp32-level results at
 // three MMAs per k-step.  TF32 (one MMA, hardware truncation) is the fast,
 // looser mode.
@@ -249,19 +250,23 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
             if (!__all_sync(FULL_MASK, mbar_wait(&full[s], (kb / STAGES) & 1))) { ok = false; break; }
             if constexpr (SPLIT3)
             {
+                // kind::tf32 reads only the top 19 bits of each staged fp32
+                // value, so the TMA tile itself is the hi operand; the
+                // converters write lo = x - hi, hi = x with its low 13
+                // mantissa bits cleared (measured: writing hi back as well
+                // cost 9 % of the config-4 prefill)
                 for (int which = 0; which < 2; ++which)
                 {
-                    float4* hi = reinterpret_cast<float4*>(tile_ptr(s, which));
+                    const float4* x4 = reinterpret_cast<const float4*>(tile_ptr(s, which));
                     float4* lo = reinterpret_cast<float4*>(tile_ptr(s, which + 2));
                     for (int i = ct; i < (int)(TILE_BYTES / 16); i += 128)
                     {
-                        const float4 x = hi[i];
-                        float4 h, l;
-                        h.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u); l.x = x.x - h.x;
-                        h.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u); l.y = x.y - h.y;
-                        h.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u); l.z = x.z - h.z;
-                        h.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u); l.w = x.w - h.w;
-                        hi[i] = h;
+                        const float4 x = x4[i];
+                        float4 l;
+                        l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+                        l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+                        l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+                        l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
                         lo[i] = l;
                     }
                 }
