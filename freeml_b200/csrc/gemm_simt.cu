@@ -173,7 +173,7 @@ int gemm_f32_ta(float* C, const float* A, const float* B, int M, int N, int K, i
 static int g_math_mode = FML_MATH_FP32;
 
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
-            int epi, const float* R, cudaStream_t st);
+            int epi, const float* R, cudaStream_t st, const float* B_lo = nullptr);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 bool skinny_nn_ok(const float* C, const float* A, const float* B, int M, int N, int K, int ldb, int ldc);
 int skinny_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc,

@@ -152,9 +152,12 @@ struct TcArgs
 
 // Shared memory: STAGES x {A, B, A_lo, B_lo} tiles (1024-byte aligned), then
 // barriers and the TMEM base address.
-template <bool SPLIT3, int EPI>
+// BLO (TF32x3 only): B's lo part is given in memory (map_blo, same geometry
+// as map_b) and loaded by TMA into the B_lo tile; the converters split A only.
+template <bool SPLIT3, int EPI, bool BLO = false>
 __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a,
-                                                              const __grid_constant__ CUtensorMap map_b, TcArgs args)
+                                                              const __grid_constant__ CUtensorMap map_b,
+                                                              const __grid_constant__ CUtensorMap map_blo, TcArgs args)
 {
     using namespace tc;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -206,9 +209,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
             {
                 const int s = kb % STAGES;
                 if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { ok = false; break; }
-                mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+                mbar_arrive_expect_tx(&full[s], (BLO ? 3 : 2) * TILE_BYTES);
                 tma_load_2d(tile_ptr(s, 0), &map_a, kb * BK, m0, &full[s]);
                 tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
+                if constexpr (BLO) tma_load_2d(tile_ptr(s, 3), &map_blo, kb * BK, n0, &full[s]);
             }
         }
     }
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
                 // converters write lo = x - hi, hi = x with its low 13
                 // mantissa bits cleared (measured: writing hi back as well
                 // cost 9 % of the config-4 prefill)
-                for (int which = 0; which < 2; ++which)
+                for (int which = 0; which < (BLO ? 1 : 2); ++which)
                 {
                     const float4* x4 = reinterpret_cast<const float4*>(tile_ptr(s, which));
                     float4* lo = reinterpret_cast<float4*>(tile_ptr(s, which + 2));
@@ -352,47 +356,73 @@ static int make_map(CUtensorMap* map, const float* base, int rows, int K, int ld
     return FML_OK;
 }
 
-template <bool SPLIT3, int EPI>
-static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcArgs& args, cudaStream_t st)
+template <bool SPLIT3, int EPI, bool BLO = false>
+static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo, const TcArgs& args,
+                     cudaStream_t st)
 {
     constexpr int NT = SPLIT3 ? 4 : 2;
     const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 16 * 8;
     static bool attr = false;
     if (!attr)
     {
-        FML_CUDA_TRY(cudaFuncSetAttribute(gemm_tcgen05_kernel<SPLIT3, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem));
+        FML_CUDA_TRY(cudaFuncSetAttribute(gemm_tcgen05_kernel<SPLIT3, EPI, BLO>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr = true;
     }
     dim3 grid((args.N + tc::BN - 1) / tc::BN, (args.M + tc::BM - 1) / tc::BM);
-    gemm_tcgen05_kernel<SPLIT3, EPI><<<grid, 192, smem, st>>>(ma, mb, args);
+    gemm_tcgen05_kernel<SPLIT3, EPI, BLO><<<grid, 192, smem, st>>>(ma, mb, mblo, args);
     FML_LAUNCH_CHECK();
     return FML_OK;
 }
 
 // C = A . B^T (+ epilogue) on the tensor cores.  A [M x K] (row stride lda),
 // B [N x K] (row stride ldb), both 16-byte aligned with lda, ldb multiples of
-// 4 (TMA's rules); split3 selects TF32x3.
+// 4 (TMA's rules); split3 selects TF32x3.  B_lo (optional, TF32x3): B's lo
+// part B - hi(B) in B's layout, so that only A is split in the kernel.
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
-            int epi, const float* R, cudaStream_t st)
+            int epi, const float* R, cudaStream_t st, const float* B_lo)
 {
     if (M <= 0 || N <= 0) return FML_OK;
     FML_REQUIRE(K > 0, "gemm_tc: K must be positive");
-    FML_REQUIRE(aligned16(A) && aligned16(B) && lda % 4 == 0 && ldb % 4 == 0,
+    FML_REQUIRE(aligned16(A) && aligned16(B) && lda % 4 == 0 && ldb % 4 == 0 && (!B_lo || aligned16(B_lo)),
                 "gemm_tc: operands must be 16-byte aligned with row strides that are multiples of 4");
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mblo;
     FML_RC(make_map(&ma, A, M, K, lda));
     FML_RC(make_map(&mb, B, N, K, ldb));
+    const bool blo = split3 && B_lo;
+    if (blo) FML_RC(make_map(&mblo, B_lo, N, K, ldb));
+    else mblo = mb;
     TcArgs args{M, N, K, C, ldc, R};
+    if (blo)
+    {
+        if (epi == TC_GELU) return launch_tc<true, TC_GELU, true>(ma, mb, mblo, args, st);
+        if (epi == TC_RESID) return launch_tc<true, TC_RESID, true>(ma, mb, mblo, args, st);
+        return launch_tc<true, TC_STORE, true>(ma, mb, mblo, args, st);
+    }
     if (split3)
     {
-        if (epi == TC_GELU) return launch_tc<true, TC_GELU>(ma, mb, args, st);
-        if (epi == TC_RESID) return launch_tc<true, TC_RESID>(ma, mb, args, st);
-        return launch_tc<true, TC_STORE>(ma, mb, args, st);
+        if (epi == TC_GELU) return launch_tc<true, TC_GELU>(ma, mb, mblo, args, st);
+        if (epi == TC_RESID) return launch_tc<true, TC_RESID>(ma, mb, mblo, args, st);
+        return launch_tc<true, TC_STORE>(ma, mb, mblo, args, st);
     }
-    if (epi == TC_GELU) return launch_tc<false, TC_GELU>(ma, mb, args, st);
-    if (epi == TC_RESID) return launch_tc<false, TC_RESID>(ma, mb, args, st);
-    return launch_tc<false, TC_STORE>(ma, mb, args, st);
+    if (epi == TC_GELU) return launch_tc<false, TC_GELU>(ma, mb, mblo, args, st);
+    if (epi == TC_RESID) return launch_tc<false, TC_RESID>(ma, mb, mblo, args, st);
+    return launch_tc<false, TC_STORE>(ma, mb, mblo, args, st);
+}
+
+// lo = x - hi(x) (hi = x with the low 13 mantissa bits cleared), for B_lo.
+__global__ void tf32_lo_kernel(float* __restrict__ lo, const float* __restrict__ x, uint64_t n)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        lo[i] = x[i] - __uint_as_float(__float_as_uint(x[i]) & 0xFFFFE000u);
+}
+
+int tf32_lo(float* lo, const float* x, uint64_t n, cudaStream_t st)
+{
+    if (n == 0) return FML_OK;
+    tf32_lo_kernel<<<grid_for(n, 256), 256, 0, st>>>(lo, x, n);
+    FML_LAUNCH_CHECK();
+    return FML_OK;
 }
 
 int gemm_tc_error_count(int* out)

@@ -59,7 +59,8 @@ int launch_layernorm(float* out, const float* in, const float* gamma, const floa
 int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool trans_b,
              int batch, uint64_t pa, uint64_t pb, uint64_t pc, cudaStream_t st);
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
-            int epi, const float* R, cudaStream_t st);
+            int epi, const float* R, cudaStream_t st, const float* B_lo = nullptr);
+int tf32_lo(float* lo, const float* x, uint64_t n, cudaStream_t st);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
                              uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
@@ -768,6 +769,12 @@ struct fml_lm
 
     // weights
     float* wbuf = nullptr;  // one allocation for every parameter
+    // TF32x3 prefill: each layer weight's lo part (W - hi(W)) in W's layout,
+    // so that the tensor-core kernel splits only the activations; made at
+    // the first TF32x3 prefill after binding, when the memory is there
+    float* wlo = nullptr;
+    bool wlo_valid = false, wlo_failed = false;
+    std::vector<float*> wqkv_lo, wproj_lo, wfc_lo, wmlp_lo;
     float *tok = nullptr, *pos_emb = nullptr, *lnf = nullptr;
     std::vector<float*> ln0, ln1, wqkv, wproj, wfc, wmlp;
 
@@ -857,6 +864,8 @@ void free_all(fml_lm* lm)
     for (void* p : arp)
         if (p) cudaFree(p);
     for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
+    if (lm->wlo) cudaFree(lm->wlo);
+    lm->wlo = nullptr;
     void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
                     lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
                     lm->counters, lm->prompt_dev, lm->grab, lm->step_sync};
@@ -1237,15 +1246,57 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
     return FML_OK;
 }
 
+// The lo parts of the layer weights for TF32x3 prefill (see fml_lm::wlo):
+// allocated once, recomputed after every bind; without the memory the
+// kernel keeps splitting W itself.
+int ensure_weight_lo(fml_lm* lm, cudaStream_t st)
+{
+    if (lm->wlo_valid || lm->wlo_failed || lm->prefill_math != FML_MATH_TF32X3) return FML_OK;
+    const fml_lm_config& c = lm->cfg;
+    const uint64_t d = c.d_model, dl = lm->dl, fl = lm->fl;
+    const uint64_t per_layer = 3 * dl * d + d * dl + fl * d + d * fl;
+    if (!lm->wlo)
+    {
+        size_t free_b = 0, total_b = 0;
+        const uint64_t need = per_layer * c.n_layer * sizeof(float);
+        if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess || free_b < need + (4ull << 30) ||
+            cudaMalloc(&lm->wlo, need) != cudaSuccess)
+        {
+            cudaGetLastError();
+            lm->wlo = nullptr;
+            lm->wlo_failed = true;
+            return FML_OK;
+        }
+        float* p = lm->wlo;
+        for (uint32_t l = 0; l < c.n_layer; ++l)
+        {
+            lm->wqkv_lo.push_back(p); p += 3 * dl * d;
+            lm->wproj_lo.push_back(p); p += d * dl;
+            lm->wfc_lo.push_back(p); p += fl * d;
+            lm->wmlp_lo.push_back(p); p += d * fl;
+        }
+    }
+    for (uint32_t l = 0; l < c.n_layer; ++l)
+    {
+        FML_RC(tf32_lo(lm->wqkv_lo[l], lm->wqkv[l], 3 * dl * d, st));
+        FML_RC(tf32_lo(lm->wproj_lo[l], lm->wproj[l], d * dl, st));
+        FML_RC(tf32_lo(lm->wfc_lo[l], lm->wfc[l], fl * d, st));
+        FML_RC(tf32_lo(lm->wmlp_lo[l], lm->wmlp[l], d * fl, st));
+    }
+    lm->wlo_valid = true;
+    return FML_OK;
+}
+
 // Prefill contraction C = A . W^T (W [N x K] K-contiguous) with an epilogue:
 // 0 store, 1 GELU, 2 C = R + A . W^T.  Tensor cores (tcgen05, TF32x3 or
 // TF32) unless the engine is set to fp32 CUDA-core math or the rows are not
 // 16-byte multiples (a TMA row stride must be).
 int prefill_gemm(fml_lm* lm, float* C, const float* A, const float* W, int M, int N, int K, int epi, const float* R,
-                 cudaStream_t st)
+                 cudaStream_t st, const float* W_lo = nullptr)
 {
     if (lm->prefill_math != FML_MATH_FP32 && K % 4 == 0)
-        return gemm_tc(C, A, W, M, N, K, K, K, N, lm->prefill_math == FML_MATH_TF32X3, epi, R, st);
+        return gemm_tc(C, A, W, M, N, K, K, K, N, lm->prefill_math == FML_MATH_TF32X3, epi, R, st,
+                       lm->wlo_valid ? W_lo : nullptr);
     FML_RC(gemm_f32(C, A, W, M, N, K, K, K, N, true, 1, 0, 0, 0, st));
     const uint64_t n = (uint64_t)M * N;
     if (epi == 1) gelu_inplace_kernel<<<grid_for(n, 256), 256, 0, st>>>(C, n);
@@ -1408,6 +1459,7 @@ int fml_lm_bind_weights(fml_lm* lm, const fml_lm_weights* w, fml_stream_t stream
     cudaStream_t st = as_stream(stream);
     const fml_lm_config& c = lm->cfg;
     const uint64_t d = c.d_model, f = sizeof(float);
+    lm->wlo_valid = false;  // the lo parts follow the new weights at the next prefill
     FML_CUDA_TRY(cudaMemcpyAsync(lm->tok, w->tok_emb, (uint64_t)c.vocab * d * f, cudaMemcpyDeviceToDevice, st));
     FML_CUDA_TRY(cudaMemcpyAsync(lm->pos_emb, w->pos_emb, (uint64_t)c.context * d * f, cudaMemcpyDeviceToDevice, st));
     FML_CUDA_TRY(cudaMemcpyAsync(lm->lnf, w->lnf, d * f, cudaMemcpyDeviceToDevice, st));
@@ -1531,13 +1583,15 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     FML_LAUNCH_CHECK();
     const bool tp = lm->tp_world > 1;
     const int resid_epi = lm->tp_rank == 0 ? 2 : 0;  // row-parallel sums take the residual once
+    FML_RC(ensure_weight_lo(lm, st));
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         float* kc = lm->kc + (uint64_t)l * lm->layer_stride;
         float* vc = lm->vc + (uint64_t)l * lm->layer_stride;
         const uint32_t dl = lm->dl, fl = lm->fl;
         FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
-        FML_RC(prefill_gemm(lm, lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * dl), (int)d, 0, nullptr, st));
+        FML_RC(prefill_gemm(lm, lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * dl), (int)d, 0, nullptr, st,
+                            lm->wlo_valid ? lm->wqkv_lo[l] : nullptr));
         qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * dl, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, dl, lm->hd,
                                                                                c.context, lm->seq_stride);
         FML_LAUNCH_CHECK();
@@ -1545,11 +1599,14 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
         FML_RC(launch_prefill_attention(lm->q, dl, kc, vc, lm->seq_stride, c.context, lm->att, dl, batch, lm->hl, P,
                                         lm->hd, 1.0f / sqrtf((float)lm->hd), st));
         // buf = x + att . Wproj^T ; hid = gelu(LN1(buf) . Wfc^T) ; x = buf + hid . Wmlp^T
-        FML_RC(prefill_gemm(lm, lm->buf, lm->att, lm->wproj[l], (int)R, (int)d, (int)dl, resid_epi, lm->x, st));
+        FML_RC(prefill_gemm(lm, lm->buf, lm->att, lm->wproj[l], (int)R, (int)d, (int)dl, resid_epi, lm->x, st,
+                            lm->wlo_valid ? lm->wproj_lo[l] : nullptr));
         if (tp) FML_RC(all_reduce_sum(lm, lm->buf, (uint64_t)R * d, st));
         FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
-        FML_RC(prefill_gemm(lm, lm->hid, lm->ln, lm->wfc[l], (int)R, (int)fl, (int)d, 1, nullptr, st));
-        FML_RC(prefill_gemm(lm, lm->x, lm->hid, lm->wmlp[l], (int)R, (int)d, (int)fl, resid_epi, lm->buf, st));
+        FML_RC(prefill_gemm(lm, lm->hid, lm->ln, lm->wfc[l], (int)R, (int)fl, (int)d, 1, nullptr, st,
+                            lm->wlo_valid ? lm->wfc_lo[l] : nullptr));
+        FML_RC(prefill_gemm(lm, lm->x, lm->hid, lm->wmlp[l], (int)R, (int)d, (int)fl, resid_epi, lm->buf, st,
+                            lm->wlo_valid ? lm->wmlp_lo[l] : nullptr));
         if (tp) FML_RC(all_reduce_sum(lm, lm->x, (uint64_t)R * d, st));
     }
     // last prompt row of each sequence -> ln_f -> lm_head argmax
