@@ -458,18 +458,13 @@ def main():
 
     # ---- e2e: the same passes through the host-buffer step (H2D + D2H) ----
     first_host = first.cpu().numpy().view(np.uint32).copy()
-    tok_in = np.empty(B, np.uint32)
-    tok_out = np.empty(B, np.uint32)
     e2e_passes = max(1, min(args.steps, 5))
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(e2e_passes):
         lm.rewind(P, first)
-        tok_in[:] = first_host
-        for _ in range(steps_per_pass):
-            lm.step_host(tok_in, tok_out)
-            tok_in, tok_out = tok_out, tok_in
+        lm.generate_host(first_host, steps_per_pass)
     torch.cuda.synchronize()
     e2e_s = max_over_ranks(time.perf_counter() - t0, pg, "cuda")
     e2e_value = dp * B * steps_per_pass * e2e_passes / e2e_s
@@ -534,7 +529,8 @@ def main():
                         "peak_note": "tf32 dense = half the measured bf16 peak, / 3 for the three-pass split"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * B * dp * steps_per_pass,
                     "d2h_bytes_per_step": 4 * B * dp * steps_per_pass,
-                    "path": "fml_lm_step_host (host token buffers, H2D + D2H + sync every engine step)"}}
+                    "path": "fml_lm_generate_host (host token buffers: every engine step copies its tokens "
+                            "H2D from pinned memory, runs, copies the next tokens D2H and synchronises)"}}
 
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and CONFIG == 3:
         try:

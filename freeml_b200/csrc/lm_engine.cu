@@ -794,6 +794,7 @@ struct fml_lm
     uint32_t* counters = nullptr;
     uint32_t* grab = nullptr;  // [L] attention work-unit counters
     uint32_t* host_io = nullptr;  // pinned [2 * max_batch]
+    uint32_t* host_io_dev = nullptr;  // host_io as the device addresses it (null: not mapped)
     uint32_t S = 1, chunk = 0;
 
     uint32_t batch = 0;                // active sequences
@@ -834,6 +835,10 @@ struct fml_lm
     uint32_t* graph_next = nullptr;
     float* graph_logits = nullptr;
     uint32_t graph_batch = 0;
+    // the host-buffer step (H2D of the tokens, the step, D2H of the next
+    // tokens) as one graph: one launch per step instead of three calls
+    cudaGraphExec_t host_graph_exec = nullptr;
+    uint32_t host_graph_batch = 0;
 
     // profiling
     bool profiling = false;
@@ -852,10 +857,18 @@ uint64_t param_count(const fml_lm_config& c)
     return (uint64_t)c.vocab * d + (uint64_t)c.context * d + (uint64_t)c.n_layer * (2 * d + 12 * d * d) + d;
 }
 
-void free_all(fml_lm* lm)
+// Forget the recorded step graphs (their launch plan no longer holds).
+void drop_graphs(fml_lm* lm)
 {
     if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
     lm->graph_exec = nullptr;
+    if (lm->host_graph_exec) cudaGraphExecDestroy(lm->host_graph_exec);
+    lm->host_graph_exec = nullptr;
+}
+
+void free_all(fml_lm* lm)
+{
+    drop_graphs(lm);
     if (lm->comm) ncclCommDestroy(lm->comm);
     lm->comm = nullptr;
     for (void* p : lm->ar_opened) cudaIpcCloseMemHandle(p);
@@ -1161,7 +1174,8 @@ bool fused_step_ready(fml_lm* lm)
 // {qkv (LayerNorm fused) -> attention -> proj + residual -> fc (LayerNorm
 // fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
 // finalize.  Every launch after the first uses programmatic dependent launch.
-int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
+// ids: the tokens the step consumes (default: the pending tokens).
+int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st, const uint32_t* ids = nullptr)
 {
     const fml_lm_config& c = lm->cfg;
     const uint32_t B = lm->batch, d = c.d_model;
@@ -1177,7 +1191,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st)
     {
         ProfScope ps(lm, 0, st);
         FML_RC(launch_k(embed_kernel, dim3(B), dim3(128), st, false, lm->x, (const float*)lm->tok,
-                        (const float*)lm->pos_emb, (const uint32_t*)lm->pending, (const uint32_t*)lm->pos, B, 1u, d,
+                        (const float*)lm->pos_emb, ids ? ids : (const uint32_t*)lm->pending, (const uint32_t*)lm->pos,
+                        B, 1u, d,
                         c.vocab, c.context, lm->grab, c.n_layer));
     }
     const bool tp = lm->tp_world > 1;
@@ -1402,6 +1417,11 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     if (!rc) rc = alloc((void**)&lm->step_sync, (uint64_t)decode_step_sync_words((uint32_t)L, 2u) * 4);
     if (!rc && cudaMallocHost((void**)&lm->host_io, 2 * B * 4) != cudaSuccess)
         rc = set_error(FML_ERR_NOMEM, "cudaMallocHost failed");
+    if (!rc && cudaHostGetDevicePointer((void**)&lm->host_io_dev, lm->host_io, 0) != cudaSuccess)
+    {
+        cudaGetLastError();
+        lm->host_io_dev = nullptr;  // the host-buffer step keeps its copies
+    }
     if (rc)
     {
         free_all(lm);
@@ -1688,8 +1708,7 @@ int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl
     FML_CUDA_TRY(cudaMemset(lm->ar_flags, 0, (uint64_t)world * AR_CTAS * sizeof(uint32_t)));
     FML_CUDA_TRY(cudaMemset(lm->ar_epoch, 0, sizeof(uint32_t)));
     lm->step_batch = 0;
-    if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
-    lm->graph_exec = nullptr;
+    drop_graphs(lm);
     return FML_OK;
 }
 
@@ -1734,8 +1753,7 @@ int fml_lm_tp_connect(fml_lm* lm, const void* all)
     FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_part, recv.data(), world * sizeof(float*), cudaMemcpyHostToDevice));
     FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_flags, flags.data(), world * sizeof(uint32_t*), cudaMemcpyHostToDevice));
     lm->ar_fused = true;
-    if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
-    lm->graph_exec = nullptr;
+    drop_graphs(lm);
     return FML_OK;
 }
 
@@ -1753,8 +1771,7 @@ int fml_lm_set_fused_step(fml_lm* lm, int on)
     FML_REQUIRE(lm, "fml_lm_set_fused_step: null engine");
     lm->fused = on != 0;
     lm->step_batch = 0;
-    if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
-    lm->graph_exec = nullptr;
+    drop_graphs(lm);
     return FML_OK;
 }
 
@@ -1772,14 +1789,93 @@ int fml_lm_set_graph(fml_lm* lm, int use_graph)
     return FML_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// A step may run only while every sequence has room for one more key.
+int check_step_state(fml_lm* lm, const char* fn)
+{
+    if (!lm->bound || lm->batch == 0) return set_error(FML_ERR_STATE, "%s: call fml_lm_prefill first", fn);
+    for (uint32_t b = 0; b < lm->batch; ++b)
+        if (lm->hpos[b] >= lm->cfg.context)
+            return set_error(FML_ERR_STATE, "%s: sequence %u is at the context limit (%u)", fn, b, lm->cfg.context);
+    return FML_OK;
+}
+
+// Record one step into an executable graph.  With host_io the step takes
+// its tokens from host_io[0, B) and leaves the next tokens in
+// host_io[max_batch, max_batch + B) (pinned host memory): the step's first
+// kernel reads them over the host link and its last kernel writes them back
+// (mapped memory; otherwise, and for the fused step, copies bracket it).
+int record_step(fml_lm* lm, uint32_t* next_tokens, float* logits, bool host_io, cudaGraphExec_t* out)
+{
+    *out = nullptr;
+    const uint32_t B = lm->batch;
+    const bool mapped = host_io && lm->host_io_dev && !fused_step_ready(lm);
+    cudaStream_t cap;
+    FML_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+    FML_CUDA_TRY(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
+    int rc = FML_OK;
+    if (mapped) rc = enqueue_step(lm, lm->host_io_dev + lm->cfg.max_batch, logits, cap, lm->host_io_dev);
+    else
+    {
+        if (host_io && cudaMemcpyAsync(lm->pending, lm->host_io, B * 4, cudaMemcpyHostToDevice, cap) != cudaSuccess)
+            rc = set_error(FML_ERR_CUDA, "graph capture: token upload");
+        if (!rc) rc = enqueue_step(lm, next_tokens, logits, cap);
+        if (!rc && host_io &&
+            cudaMemcpyAsync(lm->host_io + lm->cfg.max_batch, next_tokens, B * 4, cudaMemcpyDeviceToHost, cap) !=
+                cudaSuccess)
+            rc = set_error(FML_ERR_CUDA, "graph capture: token download");
+    }
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(cap, &g);
+    cudaStreamDestroy(cap);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    // capture counted the launches once; replays are counted at launch
+    launch_counter().fetch_sub(graph_nodes_per_step(lm), std::memory_order_relaxed);
+    return FML_OK;
+}
+
+// Enqueue one host-buffer step: tokens from host_io[0, B) in, the next
+// tokens to host_io[max_batch, max_batch + B) out (read after a sync).
+int enqueue_step_host(fml_lm* lm, cudaStream_t st)
+{
+    FML_RC(check_step_state(lm, "fml_lm_step_host"));
+    const uint32_t B = lm->batch;
+    uint32_t* dev_next = lm->prompt_dev;  // scratch slot for the step's output tokens
+    if (lm->use_graph && !lm->profiling)
+    {
+        if (!lm->host_graph_exec || lm->host_graph_batch != B)
+        {
+            if (lm->host_graph_exec) cudaGraphExecDestroy(lm->host_graph_exec);
+            lm->host_graph_exec = nullptr;
+            FML_RC(record_step(lm, dev_next, nullptr, true, &lm->host_graph_exec));
+            lm->host_graph_batch = B;
+        }
+        FML_CUDA_TRY(cudaGraphLaunch(lm->host_graph_exec, st));
+        launch_counter().fetch_add(graph_nodes_per_step(lm), std::memory_order_relaxed);
+        for (uint32_t b = 0; b < B; ++b) lm->hpos[b] += 1;
+        return FML_OK;
+    }
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->pending, lm->host_io, B * 4, cudaMemcpyHostToDevice, st));
+    FML_RC(fml_lm_step(lm, dev_next, nullptr, reinterpret_cast<fml_stream_t>(st)));
+    FML_CUDA_TRY(cudaMemcpyAsync(lm->host_io + lm->cfg.max_batch, dev_next, B * 4, cudaMemcpyDeviceToHost, st));
+    return FML_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t stream)
 {
     FML_REQUIRE(lm, "fml_lm_step: null engine");
-    if (!lm->bound || lm->batch == 0) return set_error(FML_ERR_STATE, "fml_lm_step: call fml_lm_prefill first");
-    for (uint32_t b = 0; b < lm->batch; ++b)
-        if (lm->hpos[b] >= lm->cfg.context)
-            return set_error(FML_ERR_STATE, "fml_lm_step: sequence %u is at the context limit (%u)", b,
-                             lm->cfg.context);
+    FML_RC(check_step_state(lm, "fml_lm_step"));
     cudaStream_t st = as_stream(stream);
     if (lm->use_graph && !lm->profiling)
     {
@@ -1788,23 +1884,10 @@ int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t s
         {
             if (lm->graph_exec) cudaGraphExecDestroy(lm->graph_exec);
             lm->graph_exec = nullptr;
-            cudaStream_t cap;
-            FML_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
-            FML_CUDA_TRY(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
-            int rc = enqueue_step(lm, next_tokens, logits, cap);
-            cudaGraph_t g = nullptr;
-            cudaError_t e = cudaStreamEndCapture(cap, &g);
-            cudaStreamDestroy(cap);
-            if (rc) { if (g) cudaGraphDestroy(g); return rc; }
-            if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
-            e = cudaGraphInstantiate(&lm->graph_exec, g, 0);
-            cudaGraphDestroy(g);
-            if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+            FML_RC(record_step(lm, next_tokens, logits, false, &lm->graph_exec));
             lm->graph_next = next_tokens;
             lm->graph_logits = logits;
             lm->graph_batch = lm->batch;
-            // capture counted the launches once; replays are counted below
-            launch_counter().fetch_sub(graph_nodes_per_step(lm), std::memory_order_relaxed);
         }
         FML_CUDA_TRY(cudaGraphLaunch(lm->graph_exec, st));
         launch_counter().fetch_add(graph_nodes_per_step(lm), std::memory_order_relaxed);
@@ -1825,12 +1908,27 @@ int fml_lm_step_host(fml_lm* lm, const uint32_t* tokens_in, uint32_t* tokens_out
     cudaStream_t st = as_stream(stream);
     const uint32_t B = lm->batch;
     std::memcpy(lm->host_io, tokens_in, B * 4);
-    FML_CUDA_TRY(cudaMemcpyAsync(lm->pending, lm->host_io, B * 4, cudaMemcpyHostToDevice, st));
-    uint32_t* dev_next = lm->prompt_dev;  // scratch slot for the step's output tokens
-    FML_RC(fml_lm_step(lm, dev_next, nullptr, stream));
-    FML_CUDA_TRY(cudaMemcpyAsync(lm->host_io + lm->cfg.max_batch, dev_next, B * 4, cudaMemcpyDeviceToHost, st));
+    FML_RC(enqueue_step_host(lm, st));
     FML_CUDA_TRY(cudaStreamSynchronize(st));
     std::memcpy(tokens_out, lm->host_io + lm->cfg.max_batch, B * 4);
+    return FML_OK;
+}
+
+int fml_lm_generate_host(fml_lm* lm, uint32_t steps, const uint32_t* tokens_in, uint32_t* tokens_out,
+                         fml_stream_t stream)
+{
+    FML_REQUIRE(lm && tokens_in && tokens_out, "fml_lm_generate_host: null argument");
+    if (lm->batch == 0) return set_error(FML_ERR_STATE, "fml_lm_generate_host: call fml_lm_prefill first");
+    cudaStream_t st = as_stream(stream);
+    const uint32_t B = lm->batch;
+    for (uint32_t t = 0; t < steps; ++t)
+    {
+        // every step's tokens go up from the host and come back before the next
+        std::memcpy(lm->host_io, t == 0 ? tokens_in : tokens_out + (uint64_t)(t - 1) * B, B * 4);
+        FML_RC(enqueue_step_host(lm, st));
+        FML_CUDA_TRY(cudaStreamSynchronize(st));
+        std::memcpy(tokens_out + (uint64_t)t * B, lm->host_io + lm->cfg.max_batch, B * 4);
+    }
     return FML_OK;
 }
 

@@ -126,6 +126,17 @@ class NanoLM:
         assert tokens_in.dtype == np.uint32 and tokens_out.dtype == np.uint32
         call("fml_lm_step_host", self._h, tokens_in.ctypes.data, tokens_out.ctypes.data, self._stream())
 
+    def generate_host(self, tokens_in: np.ndarray, steps: int) -> np.ndarray:
+        """`steps` host-buffer steps in one call: step 0 consumes tokens_in
+        ([batch] uint32, host), each later step the tokens the previous one
+        brought back to the host; returns the next tokens of every step
+        ([steps, batch] uint32)."""
+        assert tokens_in.dtype == np.uint32 and tokens_in.shape == (self.batch,)
+        tokens_in = np.ascontiguousarray(tokens_in)
+        out = np.empty((steps, self.batch), np.uint32)
+        call("fml_lm_generate_host", self._h, steps, tokens_in.ctypes.data, out.ctypes.data, self._stream())
+        return out
+
     def generate(self, prompts: np.ndarray, n_new: int, want_logits: bool = False, logit_rows=None):
         """Greedy decode: returns tokens [B, P + n_new] (uint32) and, if asked,
         the logits of every generated position [n_new - 1, B, V] (the prefill's

@@ -377,9 +377,20 @@ FML_API int fml_lm_get_fused_step(fml_lm* lm, int* active);
 FML_API int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t stream);
 
 /* The same step through host memory, the way a host caller drives the loop:
- * copies `tokens_in` (host, [batch]) into the pending tokens, runs the step,
- * copies the next tokens into `tokens_out` (host) and waits for them. */
+ * `tokens_in` (host, [batch]) go to the device, the step runs, the next
+ * tokens come back into `tokens_out` (host) and the call waits for them.
+ * With graphs on, the step's first kernel reads the tokens from the engine's
+ * pinned host buffer and its last kernel writes the next tokens there. */
 FML_API int fml_lm_step_host(fml_lm* lm, const uint32_t* tokens_in, uint32_t* tokens_out, fml_stream_t stream);
+
+/* `steps` host-buffer steps in one call (the harness Generate() loop over
+ * Model::Run, NanoLLM.cpp:189-204 for the token decode): step 0 reads
+ * `tokens_in` (host, [batch]); step t > 0 reads the tokens step t - 1 wrote
+ * back to the host; step t writes its next tokens to
+ * tokens_out[t * batch, (t + 1) * batch) (host).  Every step copies its
+ * tokens up and its result down and waits for it, like fml_lm_step_host. */
+FML_API int fml_lm_generate_host(fml_lm* lm, uint32_t steps, const uint32_t* tokens_in, uint32_t* tokens_out,
+                                 fml_stream_t stream);
 
 /* Replay the step as one CUDA graph (captured on first use; the step reads
  * positions and tokens from device memory, so one graph serves every step).

@@ -157,6 +157,35 @@ def test_host_step_matches_device_step(golden):
     lm.close()
 
 
+@pytest.mark.parametrize("graph", [True, False])
+def test_generate_host_matches_device_generate(golden, graph):
+    """The host-buffer loop (every step's tokens up from and back to the
+    host, the copies inside the step's graph) gives the device loop's tokens,
+    and the host-buffer step graph and the device step graph can alternate."""
+    meta, g, _ = golden
+    m = meta["greedy"]["cfg1"]
+    s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
+    w = O.init_weights(s, m["wseed"])
+    prompts = np.stack([g["cfg1_prompt"], g["cfg1_prompt"][::-1].copy(),
+                        (g["cfg1_prompt"] + 7) % m["V"], (g["cfg1_prompt"] * 3) % m["V"]]).astype(np.uint32)
+    lm = _lm(s, 4)
+    lm.bind(w)
+    lm.set_graph(graph)
+    want, _ = lm.generate(prompts, 24)
+    P = prompts.shape[1]
+    lm.prefill(prompts)
+    first = lm.pending_tokens().cpu().numpy().view(np.uint32).copy()
+    got = lm.generate_host(first, 12)
+    np.testing.assert_array_equal(got, want[:, P + 1:P + 13].T)
+    # alternate with the device step, then continue on the host
+    nxt = lm.step()[0].cpu().numpy().view(np.uint32)
+    np.testing.assert_array_equal(nxt, want[:, P + 13])
+    more = lm.generate_host(nxt.copy(), 10)
+    np.testing.assert_array_equal(more, want[:, P + 14:P + 24].T)
+    assert lm.position(0) == P + 23
+    lm.close()
+
+
 def test_rewind_replays_the_same_stream(golden):
     meta, g, _ = golden
     m = meta["greedy"]["cfg1"]
