@@ -1022,12 +1022,21 @@ int launch_gemv_team(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
     return launch_ks(kern, dim3(gx, gy), dim3(128), smem, st, pdl, a);
 }
 
-// K split: one warp per column group up to K = 512 (4 float4 slices per
-// lane), two up to 1024, four above.
+// K split: one warp per column group up to K = 1024 (8 float4 slices per
+// lane), four above (FML_GEMV_KW1_MAX / FML_GEMV_KW2_MAX: the largest K for
+// one and for two warps).  Measured on B200: one warp instead of two at
+// K = 1024 (config 4) 2738 -> 2703 us per step; two instead of four at
+// K = 2048 (config 3's mlp) 245 -> 251 us.
+#ifndef FML_GEMV_KW1_MAX
+#define FML_GEMV_KW1_MAX 1024
+#endif
+#ifndef FML_GEMV_KW2_MAX
+#define FML_GEMV_KW2_MAX 1024
+#endif
 template <int MT, int EPI, bool LN>
 int launch_gemv_team_k(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 {
-    uint32_t kw = a.K <= 512 ? 1u : (a.K <= 1024 ? 2u : 4u);
+    uint32_t kw = a.K <= FML_GEMV_KW1_MAX ? 1u : (a.K <= FML_GEMV_KW2_MAX ? 2u : 4u);
     if (const char* e = getenv("FML_GEMV_KW"))  // tuning override: 1, 2 or 4
     {
         const long v = strtol(e, nullptr, 10);
