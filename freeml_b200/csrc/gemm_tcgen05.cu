@@ -4,14 +4,17 @@
 //
 //   C[M x N] (+ epilogue) = A[M x K] . B[N x K]^T        (both K-contiguous)
 //
-// One CTA per 128 x 128 output tile, K staged 32 fp32 (one 128-byte row) at a
-// time through a 3-stage ring of TMA tensor loads (128-byte swizzle, each
-// load into this CTA only).  The accumulator lives in TMEM (128 lanes x 128 fp32 columns).
-// Warp roles (6 warps):
+// 128 x 128 output tiles, K staged 32 fp32 (one 128-byte row) at a time
+// through a 3-stage ring of TMA tensor loads (128-byte swizzle, each load into
+// this CTA only); a persistent CTA per SM walks the tiles with the
+// accumulator double-buffered in TMEM (2 x 128 lanes x 128 fp32 columns).
+// Warp roles (10 warps):
 //   warp 0      TMEM allocation; one thread issues the TMA loads
 //   warp 1      one thread issues tcgen05.mma and tcgen05.commit
-//   warps 2..5  TF32x3 split of each staged tile, then the epilogue
-//               (tcgen05.ld of the accumulator rows, store to global)
+//   warps 2..5  TF32x3 split of each staged A tile (and of the B tile,
+//               unless B's lo part is given in memory)
+//   warps 6..9  epilogue (tcgen05.ld of a finished accumulator, store to
+//               global with the fused GELU or residual add)
 //
 // Precision: kind::tf32 reads only the top 19 bits of each fp32 operand.
 // TF32x3 (default) splits x = hi + lo with hi = x with the low 13 bits
@@ -27,6 +30,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "fml_common.cuh"
@@ -150,30 +154,47 @@ struct TcArgs
     const float* R;   // TC_RESID: C = R + A.B^T (row stride ldc)
 };
 
+// One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x +
+// gridDim.x, ... (n fastest, so that a wave shares its A rows).  The stage
+// ring runs on across tile boundaries, and the accumulator is double-buffered
+// in TMEM (2 x 128 columns) so that four epilogue warps drain tile j while
+// the MMAs of tile j + 1 run (measured against one CTA per tile, whose
+// tensor pipe idled while it filled its pipeline and drained its epilogue:
+// config 4 prefill 339 -> 320 ms).
 // Shared memory: STAGES x {A, B, A_lo, B_lo} tiles (1024-byte aligned), then
-// barriers and the TMEM base address.
-// BLO (TF32x3 only): B's lo part is given in memory (map_blo, same geometry
-// as map_b) and loaded by TMA into the B_lo tile; the converters split A only.
+// barriers and the TMEM base address.  BLO (TF32x3 only): B's lo part is
+// given in memory (map_blo, same geometry as map_b) and TMA-loaded into the
+// B_lo tile; the converters split A only.
+// Warp roles (10 warps):
+//   warp 0      TMEM allocation; one thread issues the TMA loads
+//   warp 1      one thread issues tcgen05.mma / tcgen05.commit
+//   warps 2..5  TF32x3 split of each staged A tile (relay only without split)
+//   warps 6..9  epilogue: tcgen05.ld of a finished accumulator, store
+// Barriers: full / conv / empty per stage (TMA landed / split done / MMAs have
+// read it), acc_full / acc_empty per accumulator (MMAs done / drained).
 template <bool SPLIT3, int EPI, bool BLO = false>
-__global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a,
-                                                              const __grid_constant__ CUtensorMap map_b,
-                                                              const __grid_constant__ CUtensorMap map_blo, TcArgs args)
+__global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a,
+                                                                         const __grid_constant__ CUtensorMap map_b,
+                                                                         const __grid_constant__ CUtensorMap map_blo,
+                                                                         TcArgs args)
 {
     using namespace tc;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // align the carve-out to 1024 bytes (the swizzle atom)
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int NT = SPLIT3 ? 4 : 2;  // tiles per stage
     unsigned char* tiles = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(tiles + STAGES * NT * TILE_BYTES);
     uint64_t* conv = full + STAGES;
     uint64_t* empty = conv + STAGES;
-    uint64_t* done = empty + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* done = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int kblocks = (args.K + BK - 1) / BK;
+    const int tiles_n = (args.N + BN - 1) / BN;
+    const int ntiles = tiles_n * ((args.M + BM - 1) / BM);
 
     if (threadIdx.x == 0)
     {
@@ -183,13 +204,18 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
             mbar_init(&conv[s], 4);  // one arrival per converter warp
             mbar_init(&empty[s], 1);
         }
+        for (int b = 0; b < 2; ++b)
+        {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+        }
         mbar_init(done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0)
     {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
+                     "r"(2 * TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -205,121 +231,149 @@ __global__ void __launch_bounds__(192, 1) gemm_tcgen05_kernel(const __grid_const
     {
         if (lane == 0)
         {
-            for (int kb = 0; kb < kblocks && ok; ++kb)
+            uint32_t it = 0;  // k-blocks issued over all tiles
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
             {
-                const int s = kb % STAGES;
-                if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1)) { ok = false; break; }
-                mbar_arrive_expect_tx(&full[s], (BLO ? 3 : 2) * TILE_BYTES);
-                tma_load_2d(tile_ptr(s, 0), &map_a, kb * BK, m0, &full[s]);
-                tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
-                if constexpr (BLO) tma_load_2d(tile_ptr(s, 3), &map_blo, kb * BK, n0, &full[s]);
+                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it)
+                {
+                    const int s = it % STAGES;
+                    if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], (BLO ? 3 : 2) * TILE_BYTES);
+                    tma_load_2d(tile_ptr(s, 0), &map_a, kb * BK, m0, &full[s]);
+                    tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
+                    if constexpr (BLO) tma_load_2d(tile_ptr(s, 3), &map_blo, kb * BK, n0, &full[s]);
+                }
             }
+            // the last STAGES loads issued (all earlier ones were consumed):
+            // none may still be landing when the CTA exits
+            for (uint32_t i = it > (uint32_t)STAGES ? it - STAGES : 0u; i < it; ++i)
+                if (!mbar_wait(&full[i % STAGES], (i / STAGES) & 1)) ok = false;
         }
     }
     else if (warp == 1)
     {
         if (lane == 0)
         {
-            for (int kb = 0; kb < kblocks && ok; ++kb)
+            uint32_t it = 0, j = 0;  // k-blocks consumed, tiles accumulated
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++j)
             {
-                const int s = kb % STAGES;
-                if (!mbar_wait(&conv[s], (kb / STAGES) & 1)) { ok = false; break; }
+                const uint32_t buf = j & 1u, use = j >> 1;
+                if (use >= 1 && !mbar_wait(&acc_empty[buf], (use - 1) & 1)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-                for (int k = 0; k < BK / 8; ++k)  // K = 8 tf32 (32 bytes) per MMA
+                const uint32_t acc_tmem = tmem_base + buf * TMEM_COLS;
+                for (int kb = 0; kb < kblocks; ++kb, ++it)
                 {
-                    const uint32_t off = k * 32;
-                    const uint64_t da = smem_desc(tile_ptr(s, 0), off);
-                    const uint64_t db = smem_desc(tile_ptr(s, 1), off);
-                    const bool acc = kb > 0 || k > 0;
-                    mma_tf32(tmem_base, da, db, acc);
-                    if constexpr (SPLIT3)
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&conv[s], (it / STAGES) & 1)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                    for (int k = 0; k < BK / 8; ++k)  // K = 8 tf32 (32 bytes) per MMA
                     {
-                        mma_tf32(tmem_base, da, smem_desc(tile_ptr(s, 3), off), true);   // hi * lo
-                        mma_tf32(tmem_base, smem_desc(tile_ptr(s, 2), off), db, true);   // lo * hi
+                        const uint32_t off = k * 32;
+                        const uint64_t da = smem_desc(tile_ptr(s, 0), off);
+                        const uint64_t db = smem_desc(tile_ptr(s, 1), off);
+                        mma_tf32(acc_tmem, da, db, kb > 0 || k > 0);
+                        if constexpr (SPLIT3)
+                        {
+                            mma_tf32(acc_tmem, da, smem_desc(tile_ptr(s, 3), off), true);  // hi * lo
+                            mma_tf32(acc_tmem, smem_desc(tile_ptr(s, 2), off), db, true);  // lo * hi
+                        }
                     }
+                    mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
                 }
-                mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                if (!ok) break;
+                mma_commit(&acc_full[buf]);  // the accumulator is complete
             }
-            mma_commit(done);
+            mma_commit(done);  // every MMA this thread issued
+        }
+    }
+    else if (warp < 6)
+    {
+        // warps 2..5: split each staged A tile (and B's, without B_lo)
+        const int ct = threadIdx.x - 64;  // 0..127
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
+        {
+            for (int kb = 0; kb < kblocks; ++kb, ++it)
+            {
+                const int s = it % STAGES;
+                if (!__all_sync(FULL_MASK, mbar_wait(&full[s], (it / STAGES) & 1))) { ok = false; break; }
+                if constexpr (SPLIT3)
+                {
+                    for (int which = 0; which < (BLO ? 1 : 2); ++which)
+                    {
+                        const float4* x4 = reinterpret_cast<const float4*>(tile_ptr(s, which));
+                        float4* lo = reinterpret_cast<float4*>(tile_ptr(s, which + 2));
+                        for (int i = ct; i < (int)(TILE_BYTES / 16); i += 128)
+                        {
+                            const float4 x = x4[i];
+                            float4 l;
+                            l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+                            l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+                            l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+                            l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+                            lo[i] = l;
+                        }
+                    }
+                    // make these generic-proxy writes visible to the tensor core
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&conv[s]);
+            }
         }
     }
     else
     {
-        // warps 2..5: split each staged tile, then the epilogue
-        const int ct = threadIdx.x - 64;  // 0..127
-        for (int kb = 0; kb < kblocks; ++kb)
+        // warps 6..9: drain the accumulators; warp w reads TMEM lanes
+        // 32 (w % 4) .. 32 (w % 4) + 31
+        const int lg = warp & 3;
+        uint32_t j = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j)
         {
-            const int s = kb % STAGES;
-            if (!__all_sync(FULL_MASK, mbar_wait(&full[s], (kb / STAGES) & 1))) { ok = false; break; }
-            if constexpr (SPLIT3)
-            {
-                // kind::tf32 reads only the top 19 bits of each staged fp32
-                // value, so the TMA tile itself is the hi operand; the
-                // converters write lo = x - hi, hi = x with its low 13
-                // mantissa bits cleared (measured: writing hi back as well
-                // cost 9 % of the config-4 prefill)
-                for (int which = 0; which < (BLO ? 1 : 2); ++which)
-                {
-                    const float4* x4 = reinterpret_cast<const float4*>(tile_ptr(s, which));
-                    float4* lo = reinterpret_cast<float4*>(tile_ptr(s, which + 2));
-                    for (int i = ct; i < (int)(TILE_BYTES / 16); i += 128)
-                    {
-                        const float4 x = x4[i];
-                        float4 l;
-                        l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
-                        l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
-                        l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
-                        l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
-                        lo[i] = l;
-                    }
-                }
-                // make these generic-proxy writes visible to the tensor core
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&conv[s]);
-        }
-        if (ok && !__all_sync(FULL_MASK, mbar_wait(done, 0))) ok = false;
-        if (ok)
-        {
+            const uint32_t buf = j & 1u, use = j >> 1;
+            if (!__all_sync(FULL_MASK, mbar_wait(&acc_full[buf], use & 1))) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int lg = warp & 3;  // this warp's TMEM lane quarter
+            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
             const int row = m0 + lg * 32 + lane;
             for (int c0 = 0; c0 < BN; c0 += 32)
             {
                 float v[32];
-                tc::tmem_ld32(tmem_base + ((uint32_t)(lg * 32) << 16) + (uint32_t)c0, v);
+                tc::tmem_ld32(tmem_base + ((uint32_t)(lg * 32) << 16) + buf * TMEM_COLS + (uint32_t)c0, v);
                 if (row < args.M)
                 {
                     float* crow = args.C + (uint64_t)row * args.ldc + n0 + c0;
                     const float* rrow = EPI == TC_RESID ? args.R + (uint64_t)row * args.ldc + n0 + c0 : nullptr;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
+                    for (int jj = 0; jj < 32; ++jj)
                     {
-                        if (n0 + c0 + j < args.N)
+                        if (n0 + c0 + jj < args.N)
                         {
-                            float x = v[j];
+                            float x = v[jj];
                             if constexpr (EPI == TC_GELU) x = gelu_exact(x);
-                            if constexpr (EPI == TC_RESID) x += rrow[j];
-                            crow[j] = x;
+                            if constexpr (EPI == TC_RESID) x += rrow[jj];
+                            crow[jj] = x;
                         }
                     }
                 }
             }
+            // this warp's reads of the accumulator are complete
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     }
 
     if (!ok && lane == 0) atomicAdd(&g_gemm_timeouts, 1);
-    // the MMAs must have finished with TMEM before it is freed: on an early
-    // exit give them a last bounded wait
-    if (!ok && warp == 1 && lane == 0) tc::mbar_wait(done, 0);
+    // the MMAs must have finished with TMEM before it is freed (bounded)
+    if (warp == 1 && lane == 0) tc::mbar_wait(done, 0);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0)
     {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * TMEM_COLS)
                      : "memory");
     }
 }
@@ -361,16 +415,19 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
                      cudaStream_t st)
 {
     constexpr int NT = SPLIT3 ? 4 : 2;
-    const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 16 * 8;
-    static bool attr = false;
-    if (!attr)
+    const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 32 * 8;
+    static int sms = 0;
+    if (!sms)
     {
+        int dev = 0, n = 0;
+        FML_CUDA_TRY(cudaGetDevice(&dev));
+        FML_CUDA_TRY(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
         FML_CUDA_TRY(cudaFuncSetAttribute(gemm_tcgen05_kernel<SPLIT3, EPI, BLO>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
+        sms = n;
     }
-    dim3 grid((args.N + tc::BN - 1) / tc::BN, (args.M + tc::BM - 1) / tc::BM);
-    gemm_tcgen05_kernel<SPLIT3, EPI, BLO><<<grid, 192, smem, st>>>(ma, mb, mblo, args);
+    const int ntiles = ((args.N + tc::BN - 1) / tc::BN) * ((args.M + tc::BM - 1) / tc::BM);
+    gemm_tcgen05_kernel<SPLIT3, EPI, BLO><<<std::min(ntiles, sms), 320, smem, st>>>(ma, mb, mblo, args);
     FML_LAUNCH_CHECK();
     return FML_OK;
 }
