@@ -35,6 +35,40 @@ CONFIG = 3
 FALLBACK_HBM_GBS = 6650.0
 
 
+# ---- algorithmic work (the roofline numerators), fp32 throughout ----------
+
+def weight_bytes(d: int, L: int, vocab: int, tpw: int = 1) -> int:
+    """Weight bytes one rank reads per engine step: per layer QKV 3d x d/tpw,
+    projection d/tpw x d, fc d x 4d/tpw, mlp 4d/tpw x d; the tied embedding's
+    vocabulary slice as the logits head; the LayerNorm gammas (2L + 1) x d."""
+    dl, fl, vl = d // tpw, 4 * d // tpw, -(-vocab // tpw)
+    return 4 * (L * (4 * d * dl + 2 * d * fl) + vl * d + (2 * L + 1) * d)
+
+
+def decode_pass_bytes(d: int, L: int, vocab: int, B: int, P: int, steps: int, tpw: int = 1) -> int:
+    """Bytes of one decode pass of B sequences from key length P: every step
+    reads the weights once, each sequence's cached K and V rows (p + 1 keys of
+    d/tpw per layer), writes its new K/V row, and reads and writes its
+    residual row."""
+    dl = d // tpw
+    return sum(weight_bytes(d, L, vocab, tpw) + B * 4 * (2 * dl * L * (p + 1) + 2 * dl * L + 2 * d)
+               for p in range(P, P + steps))
+
+
+def attention_pass_bytes(d: int, L: int, B: int, P: int, steps: int, tpw: int = 1) -> int:
+    """Bytes the decode attention kernels move over one pass: the K and V
+    rows of p + 1 keys per sequence and layer, and the q and output rows."""
+    dl = d // tpw
+    return sum(4 * L * B * (2 * dl * (p + 1) + 2 * dl) for p in range(P, P + steps))
+
+
+def prefill_flops(d: int, L: int, vocab: int, B: int, P: int) -> int:
+    """FLOPs of one prefill of B prompts of P tokens: 2 x 12 d^2 per token
+    and layer for the four contractions, causal attention at half of
+    4 P^2 d per sequence and layer, and the last row's logits."""
+    return L * (24 * B * P * d * d + 2 * B * P * P * d) + 2 * B * vocab * d
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -407,7 +441,7 @@ def main():
     torch.cuda.synchronize()
     prefill_ms = max_over_ranks(pe0.elapsed_time(pe1), pg, "cuda")
     dm, Lm = s.d_model, s.n_layer
-    prefill_flop = dp * (Lm * (24 * B * P * dm * dm + 2 * B * P * P * dm) + 2 * B * s.vocab * dm)
+    prefill_flop = dp * prefill_flops(dm, Lm, s.vocab, B, P)
 
     if args.profile_only and args.profile_phase == "prefill":
         # for ncu (--profile-from-start off): one more prefill of the same
@@ -480,10 +514,7 @@ def main():
     d, L = s.d_model, s.n_layer
     peak, peak_kind = hbm_peak()
     tpw = ws if tp else 1  # this rank's share of the weights and heads
-    dl, fl, vl = d // tpw, 4 * d // tpw, -(-s.vocab // tpw)
-    step_bytes = sum(4 * (L * (4 * d * dl + 2 * d * fl) + vl * d + (2 * L + 1) * d)
-                     + B * 4 * (2 * dl * L * (p + 1) + 2 * dl * L + 2 * d)
-                     for p in range(P, P + steps_per_pass))
+    step_bytes = decode_pass_bytes(d, L, s.vocab, B, P, steps_per_pass, tpw)
     pass_ms = ms_max / args.steps
     total_prof_ms = sum(v[0] for v in prof.values())
     fused = lm.fused_step_active()
@@ -495,7 +526,7 @@ def main():
         traffic = ncu_traffic("decode_step") if CONFIG == 3 else None
     else:
         k_ms, k_n = prof["attention"]
-        k_bytes = sum(4 * L * B * (2 * dl * (p + 1) + 2 * dl) for p in range(P, P + steps_per_pass))
+        k_bytes = attention_pass_bytes(d, L, B, P, steps_per_pass, tpw)
         k_name = "attention_kernel (split-KV decode attention)"
         traffic = ncu_traffic("attention") if CONFIG == 3 else None
     achieved = k_bytes / (k_ms / 1e3) / 1e9 if k_ms > 0 else None

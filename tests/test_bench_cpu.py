@@ -1,0 +1,55 @@
+"""The roofline numerators bench.py reports (algorithmic bytes and FLOPs of
+the decode step, the attention kernel and the prefill), checked on the CPU
+against the figures the path's arithmetic gives by hand, so that a
+roofline fraction always divides the work the path must do."""
+import bench
+
+
+# (d, L, vocab): BASELINE configs 3, 4 and 5
+CFG3, CFG4, CFG5 = (512, 8, 4096), (1024, 12, 32000), (4096, 32, 32000)
+
+
+def test_weight_bytes_per_step():
+    # 12 d^2 per layer (QKV 3, proj 1, fc 4, mlp 4), the tied embedding once,
+    # (2L + 1) LayerNorm gammas, fp32
+    for (d, L, V), mb in ((CFG3, 109.1), (CFG4, 735.2), (CFG5, 26295.2)):
+        want = 4 * (12 * d * d * L + V * d + (2 * L + 1) * d)
+        assert bench.weight_bytes(d, L, V) == want
+        assert abs(want / 1e6 - mb) < 0.1
+
+
+def test_tensor_parallel_weight_share():
+    d, L, V = CFG5
+    full = bench.weight_bytes(d, L, V)
+    half = bench.weight_bytes(d, L, V, tpw=2)
+    # every contraction and the vocabulary split in two; gammas replicated
+    assert half == 4 * (6 * d * d * L + V // 2 * d + (2 * L + 1) * d)
+    assert abs(half / full - 0.5) < 1e-3
+
+
+def test_decode_pass_bytes_config3_average():
+    d, L, V = CFG3
+    B, P, steps = 32, 128, 383
+    total = bench.decode_pass_bytes(d, L, V, B, P, steps)
+    # 0.445 GB per engine step on average: 109 MB of weights and ~10.5 MB of
+    # K/V per sequence at the mean key length
+    assert abs(total / steps / 1e9 - 0.445) < 0.003
+    # the step's bytes = weights + the attention kernel's bytes + each
+    # sequence's residual row read and written
+    attn = bench.attention_pass_bytes(d, L, B, P, steps)
+    assert total == steps * bench.weight_bytes(d, L, V) + attn + steps * B * 4 * 2 * d
+
+
+def test_attention_bytes_per_launch_config3():
+    d, L, _ = CFG3
+    B, P, steps = 32, 128, 383
+    per_launch = bench.attention_pass_bytes(d, L, B, P, steps) / (steps * L)
+    # K and V of 320 keys on average (32 sequences x 512 floats), plus q / out
+    assert abs(per_launch / 1e6 - 42.07) < 0.01
+
+
+def test_prefill_flops():
+    for (d, L, V), B, P, tflop in ((CFG3, 32, 128, 0.21), (CFG4, 64, 1536, 33.4), (CFG5, 8, 1024, 107.8)):
+        f = bench.prefill_flops(d, L, V, B, P)
+        assert f == L * (24 * B * P * d * d + 2 * B * P * P * d) + 2 * B * V * d
+        assert abs(f / 1e12 - tflop) / tflop < 0.01
