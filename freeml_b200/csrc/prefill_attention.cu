@@ -11,7 +11,9 @@
 // columns tx + 16c of its rows.  Strided ownership keeps the float4 reads of
 // the padded Q and K tiles bank-conflict free.  A row's 64 scores live in the
 // 16 lanes of one half-warp: max and sum are 4-step shuffles.  P goes through
-// shared memory for the P . V product.  fp32 throughout; expf.
+// shared memory for the P . V product.  The K / V tiles are double-buffered:
+// tile k + 1 is copied (cp.async) while tile k is used.  fp32 throughout;
+// expf.
 #include <cmath>
 
 #include "fml_common.cuh"
@@ -20,6 +22,20 @@ namespace fml {
 namespace {
 
 constexpr int PQ = 64, PK = 64;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte global -> shared copy that bypasses registers (L2 only); with
+// `fill` false it writes zeros and reads nothing
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool fill)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(fill ? 16 : 0)
+                 : "memory");
+}
 
 template <int HD>
 __global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __restrict__ q, uint32_t ldq,
@@ -32,9 +48,9 @@ __global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __r
     constexpr int OC = HD / 16; // output columns per thread
     extern __shared__ __align__(16) float sm[];
     float* Qs = sm;              // [PQ][HP]
-    float* Ks = Qs + PQ * HP;    // [PK][HP]
-    float* Vs = Ks + PK * HP;    // [PK][HP]
-    float* Ps = Vs + PK * HP;    // [PQ][PK + 4]
+    float* Kb = Qs + PQ * HP;    // 2 x [PK][HP]: K tiles, double-buffered
+    float* Vb = Kb + 2 * PK * HP;  // 2 x [PK][HP]: V tiles
+    float* Ps = Vb + 2 * PK * HP;  // [PQ][PK + 4]
 
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const uint32_t qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -70,22 +86,41 @@ __global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __r
     }
 
     const uint32_t klast = q0 + nq - 1;  // last key any row of this tile sees
-    for (uint32_t k0 = 0; k0 <= klast; k0 += PK)
-    {
-        __syncthreads();  // previous tile's K / V / P readers are done
+    // K / V tile kt into buffer kt & 1 (rows past klast zero-filled), issued
+    // one tile ahead so that its copy overlaps the current tile's arithmetic
+    auto issue_tile = [&](uint32_t kt) {
+        const uint32_t k0 = kt * PK;
+        float* Kd = Kb + (kt & 1u) * PK * HP;
+        float* Vd = Vb + (kt & 1u) * PK * HP;
         for (int i = tid; i < PK * (HD / 4); i += 256)
         {
             const int r = i / (HD / 4), c = i % (HD / 4);
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (k0 + r <= klast)
-            {
-                kv = *reinterpret_cast<const float4*>(kbase + (uint64_t)(k0 + r) * HD + c * 4);
-                vv = *reinterpret_cast<const float4*>(vbase + (uint64_t)(k0 + r) * HD + c * 4);
-            }
-            *reinterpret_cast<float4*>(Ks + r * HP + c * 4) = kv;
-            *reinterpret_cast<float4*>(Vs + r * HP + c * 4) = vv;
+            const bool in = k0 + r <= klast;
+            const uint64_t off = (uint64_t)(in ? k0 + r : 0u) * HD + c * 4;
+            cp_async16_zfill(Kd + r * HP + c * 4, kbase + off, in);
+            cp_async16_zfill(Vd + r * HP + c * 4, vbase + off, in);
         }
-        __syncthreads();
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    const uint32_t ntiles = klast / PK + 1;
+    issue_tile(0);
+    for (uint32_t kt = 0; kt < ntiles; ++kt)
+    {
+        const uint32_t k0 = kt * PK;
+        const float* Ks = Kb + (kt & 1u) * PK * HP;
+        const float* Vs = Vb + (kt & 1u) * PK * HP;
+        // the next tile's buffer was last read in iteration kt - 1, which
+        // ended with a barrier
+        if (kt + 1 < ntiles)
+        {
+            issue_tile(kt + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        }
+        else
+        {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();  // tile kt has landed for every thread
 
         // scores for rows ty + 16i, keys tx + 16j
         float s[4][4];
@@ -164,6 +199,7 @@ __global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __r
 #pragma unroll
                 for (int c = 0; c < OC; ++c) o[i][c] = fmaf(pv[i], vv[c], o[i][c]);
         }
+        __syncthreads();  // this tile's K / V / P readers are done
     }
 
 #pragma unroll
@@ -182,7 +218,7 @@ template <int HD>
 int launch_hd(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride, uint32_t C,
               float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, float scale, cudaStream_t st)
 {
-    const size_t smem = sizeof(float) * (3 * PQ * (HD + 4) + PQ * (PK + 4));
+    const size_t smem = sizeof(float) * (5 * PQ * (HD + 4) + PQ * (PK + 4));
     static bool attr = false;
     if (!attr)
     {
