@@ -61,6 +61,20 @@ inline unsigned grid_for(uint64_t n, unsigned block, unsigned cap = 148u * 32u)
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// A kernel's dynamic shared-memory limit (cudaFuncSetAttribute) holds for the
+// device it was set on: raise it once per device a launcher runs on (bit
+// `device` of `done`; devices past 63 set it on every call).
+inline int smem_limit_once(const void* func, int bytes, uint64_t& done)
+{
+    int dev = 0;
+    FML_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+    if (bit && (done & bit)) return FML_OK;
+    FML_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done |= bit;
+    return FML_OK;
+}
+
 // ---- device helpers --------------------------------------------------------
 
 __device__ __forceinline__ float warp_sum(float v)

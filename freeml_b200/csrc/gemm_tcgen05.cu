@@ -416,16 +416,12 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
 {
     constexpr int NT = SPLIT3 ? 4 : 2;
     const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 32 * 8;
-    static int sms = 0;
-    if (!sms)
-    {
-        int dev = 0, n = 0;
-        FML_CUDA_TRY(cudaGetDevice(&dev));
-        FML_CUDA_TRY(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
-        FML_CUDA_TRY(cudaFuncSetAttribute(gemm_tcgen05_kernel<SPLIT3, EPI, BLO>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        sms = n;
-    }
+    static uint64_t attr_devices = 0;
+    FML_RC(smem_limit_once(reinterpret_cast<const void*>(gemm_tcgen05_kernel<SPLIT3, EPI, BLO>), (int)smem,
+                           attr_devices));
+    int dev = 0, sms = 0;
+    FML_CUDA_TRY(cudaGetDevice(&dev));
+    FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int ntiles = ((args.N + tc::BN - 1) / tc::BN) * ((args.M + tc::BM - 1) / tc::BM);
     gemm_tcgen05_kernel<SPLIT3, EPI, BLO><<<std::min(ntiles, sms), 320, smem, st>>>(ma, mb, mblo, args);
     FML_LAUNCH_CHECK();

@@ -997,14 +997,10 @@ int launch_gemv_team(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 {
     auto kern = gemv_team_kernel<MT, KW, EPI, LN>;
     const size_t smem = (size_t)(MT + (LN ? 1 : 0)) * a.K * sizeof(float);
-    static bool attr = false;
+    static uint64_t attr_devices = 0;
     static size_t occ_smem = 0;
     static int occ = 0;
-    if (!attr)
-    {
-        FML_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_TEAM_MAX_SMEM));
-        attr = true;
-    }
+    FML_RC(smem_limit_once(reinterpret_cast<const void*>(kern), (int)GEMV_TEAM_MAX_SMEM, attr_devices));
     if (occ_smem != smem || occ == 0)
     {
         int b = 0;

@@ -219,13 +219,8 @@ int launch_hd(const float* q, uint32_t ldq, const float* kc, const float* vc, ui
               float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, float scale, cudaStream_t st)
 {
     const size_t smem = sizeof(float) * (5 * PQ * (HD + 4) + PQ * (PK + 4));
-    static bool attr = false;
-    if (!attr)
-    {
-        FML_CUDA_TRY(
-            cudaFuncSetAttribute(prefill_attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
-    }
+    static uint64_t attr_devices = 0;
+    FML_RC(smem_limit_once(reinterpret_cast<const void*>(prefill_attention_kernel<HD>), (int)smem, attr_devices));
     const dim3 grid((P + PQ - 1) / PQ, H, B);
     prefill_attention_kernel<HD><<<grid, 256, smem, st>>>(q, ldq, kc, vc, seq_stride, C, out, ldo, P, scale);
     FML_LAUNCH_CHECK();
