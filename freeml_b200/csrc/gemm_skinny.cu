@@ -112,19 +112,21 @@ int launch_skinny(float* out, const float* A, const float* B, int M, int N, int 
 int skinny_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc,
               cudaStream_t st)
 {
-    static int sms = 0;
-    if (!sms)
+    static uint64_t pool_devices = 0;  // bit d: device d's pool is set up
+    int dev = 0, sms = 0;
+    FML_CUDA_TRY(cudaGetDevice(&dev));
+    FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+    if (!(pool_devices & bit) || !bit)
     {
-        int dev = 0;
-        FML_CUDA_TRY(cudaGetDevice(&dev));
-        FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        // the split partials come from the device's stream-ordered pool; keep
-        // freed blocks cached in this process (default threshold 0 would hand
-        // them back to the driver at every synchronisation)
+        // the split partials come from this device's stream-ordered pool;
+        // keep freed blocks cached in this process (default threshold 0
+        // would hand them back to the driver at every synchronisation)
         cudaMemPool_t pool;
         FML_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, dev));
         uint64_t keep = ~0ull;
         FML_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+        pool_devices |= bit;
     }
     const int MT = M <= 4 ? 4 : (M <= 8 ? 8 : 16);
     const int base = ((N + SKN_COLS - 1) / SKN_COLS) * ((M + MT - 1) / MT);
