@@ -25,8 +25,18 @@
  *  - pointers are device pointers unless the name says host;
  *  - matrices are row-major fp32, FreeML's Dims3D{x = cols, y = rows};
  *  - `stream` is a cudaStream_t (NULL = the legacy default stream);
- *  - operator entry points never allocate; the engine allocates only in
- *    fml_lm_create / fml_lm_bind_weights;
+ *  - allocation (fml_device_alloc aside, the allocator that MatrixCUDA
+ *    uses): operator entry points allocate nothing, except
+ *    fml_matmul with trans_b == 0 at <= 64 rows, whose split-K partials
+ *    come from the device's stream-ordered pool (cudaMallocAsync, freed on
+ *    the same stream), and fml_attention_decode, which takes a caller
+ *    workspace (fml_attention_decode_noalloc needs none); the engine
+ *    allocates in fml_lm_create, fml_lm_bind_weights / fml_lm_bind_packed
+ *    (a transient staging buffer), fml_lm_set_tensor_parallel /
+ *    fml_lm_tp_connect, and at its first TF32x3 prefill after a bind (the
+ *    weights' TF32 lo parts, left out when memory is short);
+ *  - the engine's device must be current for every call on it
+ *    (fml_lm_create leaves it current) and `stream` must belong to it;
  *  - callers are single-threaded per device, like MatrixManager
  *    (MatrixLibrary/MatrixManager.h:131-135).
  */
