@@ -322,7 +322,9 @@ void MatMul_Strided(MatrixCUDA<T>* _out, MatrixCUDA<T>* _L, MatrixCUDA<T>* _R, u
 
 namespace freeml_cuda {
 // Grow-only device scratch for operators that need temporary space (slot:
-// one per operator kind); the C ABI itself never allocates.
+// one per operator kind): the training entry points of the C ABI take their
+// workspace from the caller.  One process-wide set, for the current device
+// (the drop-in, like MatrixManager, drives one device per process).
 inline float* Scratch(size_t floats, int slot)
 {
     static float* ptr[4] = {};
