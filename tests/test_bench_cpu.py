@@ -53,3 +53,25 @@ def test_prefill_flops():
         f = bench.prefill_flops(d, L, V, B, P)
         assert f == L * (24 * B * P * d * d + 2 * B * P * P * d) + 2 * B * V * d
         assert abs(f / 1e12 - tflop) / tflop < 0.01
+
+
+def test_reference_arm_prints_the_contract_line():
+    """`bench.py --impl reference` times the reference's own CPU path on the
+    host (one step here) and prints one JSON line with the same metric, unit
+    and direction as the GPU arm, marked as the reference."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "0"], capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip().startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    assert (d["metric"], d["unit"], d["higher_is_better"]) == (bench.METRIC, bench.UNIT, True)
+    assert d["value"] > 0 and d["steps"] == 1
+    assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
