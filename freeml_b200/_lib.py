@@ -102,6 +102,7 @@ SIGNATURES = {
     "fml_lm_tp_ipc_handles": (_I, [_P, _P]),
     "fml_lm_tp_connect": (_I, [_P, _P]),
     "fml_lm_tp_error_count": (_I, [_P]),
+    "fml_tp_flag_check": (_I, [_U32, _U32, _U32, _U32, ctypes.POINTER(_I)]),
     "fml_lm_get_fused_step": (_I, [_P, _P]),
     "fml_lm_pending": (_I, [_P, _P, _P]),
     "fml_lm_get_position": (_I, [_P, _U32, ctypes.POINTER(_U32)]),

@@ -72,10 +72,17 @@ DROPIN_BIN = os.path.join(BUILD, "nanollm_dropin")
 
 
 def freeml_root() -> str | None:
-    """The FreeML source tree the drop-in example compiles against."""
-    for cand in (os.environ.get("FREEML_ROOT"), "/root/reference"):
+    """The FreeML source tree the drop-in example compiles against: the
+    FREEML_ROOT environment variable, else a checkout named `reference` next
+    to this repository.  None when neither holds FreeML (a machine that only
+    runs the prebuilt binaries)."""
+    env = os.environ.get("FREEML_ROOT")
+    cands = [env] if env else [os.path.join(os.path.dirname(os.path.realpath(ROOT)), "reference")]
+    for cand in cands:
         if cand and os.path.exists(os.path.join(cand, "ModelLibrary", "Model.h")):
             return cand
+    if env:
+        raise RuntimeError(f"FREEML_ROOT={env} does not hold a FreeML tree (ModelLibrary/Model.h is missing)")
     return None
 
 

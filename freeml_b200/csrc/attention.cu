@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include <cooperative_groups.h>
+#include <cuda.h>
 
 #include "attention.cuh"
 #include "decode_step.cuh"
@@ -444,8 +445,11 @@ int fml_attention_decode(float* out, const float* q, const float* kcache, const 
 // Host code may not hand `g_attention_scratch` to a kernel: on the host that
 // name is only a stand-in, not a device address.  The device address is
 // fetched with cudaGetSymbolAddress once per device (with that device
-// current) and cached; the first call on a device does this set-up, so make
-// that first call outside any stream capture.
+// current) and cached together with the CUDA context it belongs to; the first
+// call on a device does this set-up, so make that first call outside any
+// stream capture.  When the device's context changes (after a device reset the
+// runtime loads this library's module into a new context) the address is
+// fetched again.
 // ---------------------------------------------------------------------------
 
 static __device__ __align__(256) unsigned char g_attention_scratch[FML_NOALLOC_SCRATCH_BYTES];
@@ -453,7 +457,32 @@ static __device__ __align__(256) unsigned char g_attention_scratch[FML_NOALLOC_S
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr
+{
+    CUcontext ctx;
+    void* addr;
+};
+ScratchAddr g_scratch_addr[kMaxDevices] = {};
+
+// The calling thread's current context, through the driver entry point the
+// runtime hands out (the library links no driver library directly); null
+// when there is none or the entry point is unavailable.
+CUcontext current_context()
+{
+    using GetCurrent = CUresult (*)(CUcontext*);
+    static GetCurrent fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetCurrent>(p);
+    });
+    CUcontext ctx = nullptr;
+    if (!fn || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+    return ctx;
+}
 
 int noalloc_scratch(void** out)
 {
@@ -462,16 +491,21 @@ int noalloc_scratch(void** out)
     if (dev < 0 || dev >= kMaxDevices)
         return set_error(FML_ERR_UNSUPPORTED, "fml_attention_decode_noalloc: device %d out of range", dev);
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev])
+    CUcontext ctx = current_context();
+    ScratchAddr& slot = g_scratch_addr[dev];
+    if (!slot.addr || !ctx || ctx != slot.ctx)
     {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
         if (e != cudaSuccess || !p)
             return set_error(FML_ERR_CUDA, "fml_attention_decode_noalloc: cudaGetSymbolAddress failed: %s",
                              cudaGetErrorString(e));
-        g_scratch_addr[dev] = p;
+        // the lookup made the device's context current if it was not yet
+        ctx = current_context();
+        slot.ctx = ctx;
+        slot.addr = p;
     }
-    *out = g_scratch_addr[dev];
+    *out = slot.addr;
     return FML_OK;
 }
 }  // namespace

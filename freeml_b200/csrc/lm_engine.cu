@@ -106,6 +106,21 @@ constexpr uint32_t AR_CTAS = 16;  // CTAs of the all-reduce kernel = flags per r
 constexpr uint64_t AR_WAIT_NS = 1000000000ull;
 __device__ unsigned int g_tp_timeouts = 0;
 
+// Flag tags of the one-shot all-reduce.  A step holds `nslot` all-reduces
+// (2 per layer); use `slot` of step `epoch` raises every flag to
+// epoch * nslot + slot + 1, so consecutive uses count up by one, modulo 2^32.
+// A waiter passes once the flag has reached its tag, compared through the
+// signed difference so the test holds across the 2^32 wrap (flags never lag
+// a tag by 2^31 uses: every rank finishes use u before any starts u + 2).
+__host__ __device__ __forceinline__ uint32_t ar_tag(uint32_t epoch, uint32_t slot, uint32_t nslot)
+{
+    return epoch * nslot + slot + 1u;
+}
+__host__ __device__ __forceinline__ bool ar_flag_reached(uint32_t flag, uint32_t tag)
+{
+    return (int32_t)(flag - tag) >= 0;
+}
+
 // Weight stream load: each weight is read once per step, so it bypasses L1
 // and leaves L1 to the activation rows that every column group re-reads
 // (measured: +4 % decode tokens/s on config 5, where the activation rows are
@@ -631,13 +646,13 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
 __global__ void __launch_bounds__(256) ar_oneshot_kernel(float* __restrict__ y, const float* __restrict__ resid,
                                                          const float* const* parts, uint64_t part_off,
                                                          uint32_t* const* peer_flags, const uint32_t* flags,
-                                                         const uint32_t* epoch, uint32_t slot, uint32_t world,
-                                                         uint32_t rank, uint64_t n)
+                                                         const uint32_t* epoch, uint32_t slot, uint32_t nslot,
+                                                         uint32_t world, uint32_t rank, uint64_t n)
 {
     griddep_wait();  // this rank's partial is complete
     griddep_launch_dependents();
     const uint32_t b = blockIdx.x;
-    const uint32_t tag = __ldcg(epoch) * 128u + slot + 1u;
+    const uint32_t tag = ar_tag(__ldcg(epoch), slot, nslot);
     if (threadIdx.x < world)
     {
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer_flags[threadIdx.x] + rank * AR_CTAS + b),
@@ -649,7 +664,7 @@ __global__ void __launch_bounds__(256) ar_oneshot_kernel(float* __restrict__ y, 
         {
             uint32_t v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-            if (v >= tag) break;
+            if (ar_flag_reached(v, tag)) break;
             uint64_t now;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
             if (it == 0) t0 = now;
@@ -1128,7 +1143,8 @@ int gemv_allreduce(fml_lm* lm, GemvArgs a, float* y, const float* resid, uint32_
     FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
     return launch_k(ar_oneshot_kernel, dim3(AR_CTAS), dim3(256), st, pdl, y, resid,
                     (const float* const*)lm->ar_peer_part, off, (uint32_t* const*)lm->ar_peer_flags,
-                    (const uint32_t*)lm->ar_flags, (const uint32_t*)lm->ar_epoch, slot, (uint32_t)lm->tp_world,
+                    (const uint32_t*)lm->ar_flags, (const uint32_t*)lm->ar_epoch, slot, 2u * lm->cfg.n_layer,
+                    (uint32_t)lm->tp_world,
                     (uint32_t)lm->tp_rank, n);
 }
 
@@ -1759,6 +1775,14 @@ int fml_lm_tp_connect(fml_lm* lm, const void* all)
     FML_CUDA_TRY(cudaMemcpy(lm->ar_peer_flags, flags.data(), world * sizeof(uint32_t*), cudaMemcpyHostToDevice));
     lm->ar_fused = true;
     drop_graphs(lm);
+    return FML_OK;
+}
+
+int fml_tp_flag_check(uint32_t epoch, uint32_t slot, uint32_t nslot, uint32_t flag, int* reached)
+{
+    FML_REQUIRE(reached, "fml_tp_flag_check: null argument");
+    FML_REQUIRE(slot < nslot, "fml_tp_flag_check: slot %u outside [0, %u)", slot, nslot);
+    *reached = ar_flag_reached(flag, ar_tag(epoch, slot, nslot)) ? 1 : 0;
     return FML_OK;
 }
 

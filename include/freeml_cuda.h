@@ -244,7 +244,9 @@ FML_API int fml_attention_decode(float* out, const float* q, const float* kcache
  * scratch would exceed it are rejected with FML_ERR_UNSUPPORTED (use
  * fml_attention_decode instead).  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress), so make that first call
- * outside any stream capture.  Every call shares the one array: calls that
+ * outside any stream capture; after a device reset the next call looks it up
+ * again (the address is cached per device and CUDA context).  Every call
+ * shares the one array: calls that
  * overlap on the GPU (different streams, or different host threads on the same
  * device) race and must be serialised by the caller.  Same arguments and
  * results as fml_attention_decode otherwise. */
@@ -367,6 +369,12 @@ FML_API int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const vo
 FML_API int fml_lm_tp_ipc_handles(fml_lm* lm, void* out);
 FML_API int fml_lm_tp_connect(fml_lm* lm, const void* all_handles);
 FML_API int fml_lm_tp_error_count(uint64_t* count);
+
+/* The flag test of that all-reduce, on the host: *reached = 1 when a flag
+ * holding `flag` satisfies a waiter of use `slot` (of `nslot` per step, 2 per
+ * layer) in step `epoch`.  Tags count up by one per use modulo 2^32 and the
+ * test is wrap-safe.  A test hook: no counterpart in the reference. */
+FML_API int fml_tp_flag_check(uint32_t epoch, uint32_t slot, uint32_t nslot, uint32_t flag, int* reached);
 
 /* Precision of the prefill contractions (FML_MATH_*; default
  * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy). */

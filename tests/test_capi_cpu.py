@@ -71,3 +71,30 @@ def test_zero_size_ops_are_noops():
     # n == 0 returns before any launch
     assert _lib.call("fml_add", None, None, None, 0, None) == 0
     assert _lib.call("fml_gelu", None, None, 0, None) == 0
+
+
+def _flag_reached(epoch, slot, nslot, flag):
+    r = ctypes.c_int(-1)
+    _lib.call("fml_tp_flag_check", epoch, slot, nslot, flag, ctypes.byref(r))
+    return bool(r.value)
+
+
+@pytest.mark.parametrize("n_layer", [1, 8, 32, 64, 100])
+def test_tp_flag_tags_are_ordered_across_steps_and_the_wrap(n_layer):
+    """The peer all-reduce's flags: a waiter passes on its own tag or a later
+    one and waits on every earlier one -- also for models of 64 layers and
+    more, and where epoch * slots wraps past 2^32."""
+    nslot = 2 * n_layer
+    M = 1 << 32
+    wrap_epoch = M // nslot  # the first step whose tags wrap
+    for epoch in (0, 1, 5, wrap_epoch - 1, wrap_epoch, wrap_epoch + 1, (M - 1) // nslot):
+        for slot in (0, 1, nslot - 1):
+            tag = (epoch * nslot + slot + 1) % M
+            assert _flag_reached(epoch, slot, nslot, tag)
+            assert _flag_reached(epoch, slot, nslot, (tag + 1) % M)  # a peer one use ahead
+            assert not _flag_reached(epoch, slot, nslot, (tag - 1) % M)  # the previous use
+            prev_step = ((epoch - 1) * nslot + slot + 1) % M  # the same slot one step earlier
+            assert not _flag_reached(epoch, slot, nslot, prev_step)
+            # the last slot of the previous step never satisfies slot 0 of this one
+            if slot == 0:
+                assert not _flag_reached(epoch, 0, nslot, ((epoch - 1) * nslot + nslot) % M)

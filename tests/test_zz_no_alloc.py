@@ -50,11 +50,26 @@ def _no_alloc(q, kc, vc, ln, scale):
     return out
 
 
+# How the key-range splits are merged.  By default up to 8 splits form one
+# thread-block cluster and merge on chip, which touches only the counters in
+# the fixed array; with clusters off, or with 16 splits, every split writes
+# its partials into the array and the last one to finish merges them, so a
+# second call runs over the first call's partials and counters.
+MERGES = {
+    "cluster": {},
+    "global": {"FML_ATTN_CLUSTER": "0"},
+    "global-16-splits": {"FML_ATTN_SPLITS": "16"},
+}
+
+
+@pytest.mark.parametrize("merge", sorted(MERGES))
 @pytest.mark.parametrize("B,H,hd,C,lens", [
     (1, 8, 64, 2048, [2048]),           # a single sequence: many splits of the key range
     (4, 8, 64, 512, [0, 1, 300, 512]),  # ragged lengths, including an empty one
 ])
-def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(B, H, hd, C, lens):
+def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(B, H, hd, C, lens, merge, monkeypatch):
+    for k, v in MERGES[merge].items():
+        monkeypatch.setenv(k, v)  # read by the library at every call
     torch.cuda.set_device(0)
     scale = float(1.0 / np.sqrt(hd))
     first = _case(B, H, hd, C, lens, seed=C + B)
