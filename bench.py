@@ -69,6 +69,24 @@ def prefill_flops(d: int, L: int, vocab: int, B: int, P: int) -> int:
     return L * (24 * B * P * d * d + 2 * B * P * P * d) + 2 * B * vocab * d
 
 
+def kernel_times_from_stamps(stamps, classes):
+    """Per-class time inside the step graph from completion stamps
+    [steps, kernels] (ns): a kernel's time is its completion minus the
+    previous kernel's (the first kernel of step s: minus step s-1's last).
+    Step 0 has no previous step in the pass and is left out."""
+    by, n, total = {}, {}, 0
+    steps, nk = stamps.shape
+    for st in range(1, steps):
+        prev = int(stamps[st - 1, nk - 1])
+        for i in range(nk):
+            t = int(stamps[st, i])
+            by[classes[i]] = by.get(classes[i], 0) + (t - prev)
+            n[classes[i]] = n.get(classes[i], 0) + 1
+            prev = t
+        total += int(stamps[st, nk - 1]) - int(stamps[st - 1, nk - 1])
+    return {"by_class_ns": by, "launches": n, "total_ns": total, "steps": max(steps - 1, 0)}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -503,33 +521,24 @@ def main():
     e2e_s = max_over_ranks(time.perf_counter() - t0, pg, "cuda")
     e2e_value = dp * B * steps_per_pass * e2e_passes / e2e_s
 
-    # ---- roofline of the dominant kernel (attention), from a profiled pass ----
-    lm.set_graph(False)
-    lm.set_profiling(True)
-    one_pass()
-    torch.cuda.synchronize()
-    prof = lm.profile()
-    lm.set_profiling(False)
-    lm.set_graph(True)
+    # ---- per-kernel times inside the replayed step graph (the timed code
+    # path, with programmatic dependent launch): one more pass with
+    # completion stamps, every kernel's CTAs stamping the global timer ----
     d, L = s.d_model, s.n_layer
     peak, peak_kind = hbm_peak()
     tpw = ws if tp else 1  # this rank's share of the weights and heads
+    dl = d // tpw
     step_bytes = decode_pass_bytes(d, L, s.vocab, B, P, steps_per_pass, tpw)
     pass_ms = ms_max / args.steps
-    total_prof_ms = sum(v[0] for v in prof.values())
-    fused = lm.fused_step_active()
-    if fused:
-        # the fused step is the only kernel: its algorithmic bytes are the step's
-        k_ms, k_n = prof["step"]
-        k_bytes = step_bytes
-        k_name = "decode_step_kernel (fused decode step: all layers, attention, lm_head, argmax)"
-        traffic = ncu_traffic("decode_step") if CONFIG == 3 else None
-    else:
-        k_ms, k_n = prof["attention"]
-        k_bytes = attention_pass_bytes(d, L, B, P, steps_per_pass, tpw)
-        k_name = "attention_kernel (split-KV decode attention)"
-        traffic = ncu_traffic("attention") if CONFIG == 3 else None
-    achieved = k_bytes / (k_ms / 1e3) / 1e9 if k_ms > 0 else None
+    stamps, classes = lm.stamped_pass(one_pass, steps_per_pass)
+    kt = kernel_times_from_stamps(stamps, classes)
+    # the attention launches of steps 1.. (step 0 follows the rewind kernel,
+    # not a finished step, so it has no start to measure from)
+    att_bytes = sum(4 * L * B * (2 * dl * (p + 1) + 2 * dl) for p in range(P + 1, P + steps_per_pass))
+    att_s, att_n = kt["by_class_ns"].get("attention", 0) / 1e9, kt["launches"].get("attention", 0)
+    achieved = att_bytes / att_s / 1e9 if att_s > 0 else None
+    k_name = "attention_kernel (split-KV decode attention)"
+    traffic = ncu_traffic("attention") if CONFIG == 3 else None
 
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": pass_ms, "higher_is_better": True, "scaling": "strong",
@@ -538,20 +547,26 @@ def main():
             "config": dict(workload_config(ws, B, tp),
                            allreduce=("NCCL" if args.tp_nccl else "one-shot kernel over NVLink peer memory "
                                       "(decode; prefill: NCCL)") if tp else None,
-                           engine="fused step kernel" if fused else "per-operation kernels (CUDA graph, PDL)"),
+                           engine="per-operation kernels (CUDA graph, programmatic dependent launch); decode "
+                                  "contractions on tcgen05 (TF32x3) where the shape allows"),
             "gpu_launches": int(launches),
             "clocks": clocks,
             "roofline": {"bound": "hbm", "kernel": k_name,
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
                          "traffic": (traffic or {}).get("bytes_per_launch_at_bench_avg"),
-                         "algorithmic_bytes_per_launch": k_bytes / max(k_n, 1),
-                         "avg_launch_us": k_ms / max(k_n, 1) * 1e3,
-                         "share_of_step_time": k_ms / total_prof_ms if total_prof_ms else None},
+                         "algorithmic_bytes_per_launch": att_bytes / max(att_n, 1),
+                         "avg_launch_us": att_s / max(att_n, 1) * 1e6,
+                         "share_of_step_time": kt["by_class_ns"].get("attention", 0) / kt["total_ns"]
+                         if kt["total_ns"] else None,
+                         "timing": "in the replayed step graph: each launch's time = its last CTA's completion "
+                                   "stamp minus the previous kernel's (global timer), over steps 1..382 of one "
+                                   "extra pass"},
             "step_roofline": {"algorithmic_bytes_per_pass": step_bytes,
                               "achieved_GBps": step_bytes / (pass_ms / 1e3) / 1e9,
                               "frac": step_bytes / (pass_ms / 1e3) / 1e9 / peak},
-            "kernel_ms_per_pass": {k: v[0] for k, v in prof.items()},
+            "kernel_us_per_step": {k: v / 1e3 / max(kt["steps"], 1) for k, v in kt["by_class_ns"].items()},
+            "stamped_step_us": kt["total_ns"] / 1e3 / max(kt["steps"], 1),
             "prefill": {"ms": prefill_ms, "tokens_per_s": dp * B * P / (prefill_ms / 1e3),
                         "algorithmic_tflop": prefill_flop / 1e12,
                         "tflops": prefill_flop / (prefill_ms / 1e3) / 1e12,

@@ -18,7 +18,9 @@ STATUS_NAMES = {1: "FML_ERR_INVALID", 2: "FML_ERR_CUDA", 3: "FML_ERR_NOMEM", 4: 
 
 FML_MATH_FP32, FML_MATH_TF32X3, FML_MATH_TF32 = 0, 1, 2
 FML_LM_NCLASS = 10
-PROFILE_CLASSES = ["embed", "layernorm", "qkv", "attention", "proj", "fc", "mlp", "lm_head", "finalize", "step"]
+PROFILE_CLASSES = ["embed", "layernorm", "qkv", "attention", "proj", "fc", "mlp", "lm_head", "finalize",
+                   "allreduce"]
+FML_DECODE_GEMV_CUDA_CORES, FML_DECODE_GEMV_TENSOR_CORES = 0, 1
 
 
 class FmlError(RuntimeError):
@@ -96,14 +98,15 @@ SIGNATURES = {
     "fml_lm_generate_host": (_I, [_P, _U32, _P, _P, _P]),
     "fml_lm_set_graph": (_I, [_P, _I]),
     "fml_lm_set_prefill_math": (_I, [_P, _I]),
-    "fml_lm_set_fused_step": (_I, [_P, _I]),
+    "fml_lm_set_decode_gemv": (_I, [_P, _I]),
+    "fml_lm_set_stamps": (_I, [_P, _P, _U32, ctypes.POINTER(_U32)]),
+    "fml_lm_stamp_classes": (_I, [_P, _P, _U32, ctypes.POINTER(_U32)]),
     "fml_nccl_unique_id": (_I, [_P]),
     "fml_lm_set_tensor_parallel": (_I, [_P, _I, _I, _P]),
     "fml_lm_tp_ipc_handles": (_I, [_P, _P]),
     "fml_lm_tp_connect": (_I, [_P, _P]),
     "fml_lm_tp_error_count": (_I, [_P]),
     "fml_tp_flag_check": (_I, [_U32, _U32, _U32, _U32, ctypes.POINTER(_I)]),
-    "fml_lm_get_fused_step": (_I, [_P, _P]),
     "fml_lm_pending": (_I, [_P, _P, _P]),
     "fml_lm_get_position": (_I, [_P, _U32, ctypes.POINTER(_U32)]),
     "fml_lm_rewind": (_I, [_P, _U32, _P, _I, _P]),

@@ -11,7 +11,7 @@
 #include <cuda.h>
 
 #include "attention.cuh"
-#include "decode_step.cuh"
+#include "gemv_tcgen05.cuh"
 
 namespace fml {
 
@@ -80,6 +80,7 @@ template <int HD, bool CL>
 __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
 {
     FML_TIMELINE_SCOPE(20);
+    const StampAtExit stamp_at_exit(a.stamp);
     constexpr int G = HD / 4;       // lanes per key
     constexpr int KPW = 32 / G;     // keys per warp step
     constexpr int U = 4;            // steps whose loads are in flight together
@@ -382,7 +383,7 @@ int fml_device_error_count(uint64_t* count)
     uint64_t tpw = 0;
     FML_CUDA_TRY(cudaDeviceSynchronize());
     FML_RC(gemm_tc_error_count(&g));
-    FML_RC(decode_step_error_count(&f));
+    FML_RC(gemv_tc_error_count(&f));
     FML_RC(fml_lm_tp_error_count(&tpw));
     *count = (uint64_t)g + (uint64_t)f + tpw;
     return FML_OK;

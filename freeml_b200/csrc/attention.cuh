@@ -26,6 +26,7 @@ struct AttnArgs
     float* part;          // [B][H][S][HD + 2] split partials
     uint32_t* counters;   // [B][H] split-merge counters (zero between launches)
     uint32_t* grab;       // work-unit counter (zero before each launch)
+    StepStamp stamp;      // optional completion stamp (decode engine)
 };
 
 void attention_splits(uint64_t pairs, uint64_t ctx, uint32_t* S_out, uint32_t* chunk_out);

@@ -101,6 +101,40 @@ __device__ __forceinline__ void griddep_launch_dependents()
 
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ---- in-graph completion stamps of the decode step's kernels ------------
+// When `buf` is set, thread 0 of every CTA of a step kernel raises
+// buf[*step * stride + idx] to the global timer (ns) as the CTA exits, so the
+// slot ends up holding the time the kernel's last CTA finished.  `step` is a
+// device counter the step's last kernel advances; the host reads the slots of
+// a replayed pass and takes differences of consecutive kernels' completions
+// (the time each kernel adds to the step's dependent chain).  Off (null) in
+// timed runs.
+struct StepStamp
+{
+    unsigned long long* buf;
+    const uint32_t* step;
+    uint32_t stride, idx, cap;
+};
+
+__device__ __forceinline__ void stamp_write(const StepStamp& s)
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const uint32_t slot = *s.step * s.stride + s.idx;
+    if (slot < s.cap) atomicMax(s.buf + slot, t);
+}
+
+// Writes the CTA's stamp when the kernel returns (any return path).
+struct StampAtExit
+{
+    const StepStamp& s;
+    __device__ explicit StampAtExit(const StepStamp& st) : s(st) {}
+    __device__ ~StampAtExit()
+    {
+        if (s.buf && threadIdx.x == 0) stamp_write(s);
+    }
+};
+
 // ---- optional per-CTA timeline (debug builds with -DFML_TIMELINE only) ----
 // Thread 0 of every CTA appends (kernel id, start, end) global-timer stamps
 // to a device ring that the host reads back; compiled out otherwise.

@@ -37,7 +37,7 @@
 #include <nccl.h>
 
 #include "attention.cuh"
-#include "decode_step.cuh"
+#include "gemv_tcgen05.cuh"
 #include "fml_common.cuh"
 
 #ifdef FML_TIMELINE
@@ -73,9 +73,11 @@ int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, cons
 // t = pos[b].  Prefill: r = b*P + t, id = prompt[r].
 __global__ void embed_kernel(float* __restrict__ x, const float* __restrict__ tok, const float* __restrict__ posemb,
                              const uint32_t* __restrict__ ids, const uint32_t* __restrict__ pos, uint32_t rows,
-                             uint32_t P, uint32_t d, uint32_t V, uint32_t C, uint32_t* zero, uint32_t nzero)
+                             uint32_t P, uint32_t d, uint32_t V, uint32_t C, uint32_t* zero, uint32_t nzero,
+                             StepStamp stamp)
 {
     FML_TIMELINE_SCOPE(1);
+    const StampAtExit stamp_at_exit(stamp);
     griddep_launch_dependents();
     griddep_wait();
     FML_TIMELINE_MARK(1);
@@ -156,6 +158,7 @@ struct GemvArgs
 
     // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
     const float* gamma;
+    StepStamp stamp;  // optional completion stamp
 };
 
 // y[m, n] = sum_k xn[m, k] W[n, k] for the small-M (decode) shapes, where
@@ -175,6 +178,7 @@ template <int MT, int EPI, bool LN>
 __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
 {
     FML_TIMELINE_SCOPE(10 + EPI);
+    const StampAtExit stamp_at_exit(a.stamp);
     constexpr int NW = 4;
     constexpr int CNT = MT * NW;
     constexpr int R = CNT >= 32 ? CNT / 32 : 1;
@@ -425,6 +429,7 @@ template <int MT, int KW, int EPI, bool LN>
 __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
 {
     FML_TIMELINE_SCOPE(10 + EPI);
+    const StampAtExit stamp_at_exit(a.stamp);
     constexpr int NW = 4;              // output columns per group
     constexpr int CNT = MT * NW;       // sums per lane (16 or 32)
     constexpr int TEAMS = 4 / KW;
@@ -647,8 +652,9 @@ __global__ void __launch_bounds__(256) ar_oneshot_kernel(float* __restrict__ y, 
                                                          const float* const* parts, uint64_t part_off,
                                                          uint32_t* const* peer_flags, const uint32_t* flags,
                                                          const uint32_t* epoch, uint32_t slot, uint32_t nslot,
-                                                         uint32_t world, uint32_t rank, uint64_t n)
+                                                         uint32_t world, uint32_t rank, uint64_t n, StepStamp stamp)
 {
+    const StampAtExit stamp_at_exit(stamp);
     griddep_wait();  // this rank's partial is complete
     griddep_launch_dependents();
     const uint32_t b = blockIdx.x;
@@ -714,14 +720,21 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
 }
 
 // After lm_head: pending token = argmax, advance the position, reset keys.
+// With stamps on, thread 0 stamps the step's last slot and then advances the
+// stamp step counter (every other kernel of the step has finished by then).
 __global__ void finalize_kernel(unsigned long long* keys, uint32_t* pending, uint32_t* pos, uint32_t* next_out,
-                                uint32_t B, uint32_t set_pos, uint32_t* epoch)
+                                uint32_t B, uint32_t set_pos, uint32_t* epoch, StepStamp stamp, uint32_t* stamp_ctr)
 {
     FML_TIMELINE_SCOPE(30);
     griddep_wait();
     FML_TIMELINE_MARK(1);
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b == 0 && epoch) *epoch += 1u;
+    if (b == 0 && stamp.buf)
+    {
+        stamp_write(stamp);
+        *stamp_ctr += 1u;
+    }
     if (b >= B) return;
     const uint32_t tok = argmax_key_index(keys[b]);
     pending[b] = tok;
@@ -836,15 +849,16 @@ struct fml_lm
     uint32_t** ar_peer_flags = nullptr;
     std::vector<void*> ar_opened;    // peer mappings to close
 
-    // fused decode step (one persistent kernel per step), opt-in: on config 3
-    // it measures slower than the per-operation kernels (437 vs 337 us/step)
-    bool fused = false;
-    bool step_ok = false;
-    uint32_t step_batch = 0;  // batch the plan was made for (0: none)
-    StepArgs sa{};
-    int step_grid = 0;
-    size_t step_smem = 0;
-    uint32_t* step_sync = nullptr;
+    // decode contractions: tensor cores (TF32x3 on tcgen05) where the shape
+    // allows, else the CUDA-core GEMVs (fml_lm_set_decode_gemv)
+    bool gemv_tc = true;
+    // in-graph completion stamps (fml_lm_set_stamps): one slot per kernel of
+    // a step, `stamp_stride` slots per step; the class of each slot
+    unsigned long long* stamps = nullptr;
+    uint32_t stamp_cap = 0, stamp_stride = 0, stamp_n = 0;
+    uint32_t* stamp_step = nullptr;  // device step counter (advanced by finalize)
+    std::vector<int> stamp_class;
+    uint32_t step_kernels = 0;  // kernels one enqueued step launches
     cudaGraphExec_t graph_exec = nullptr;
     cudaStream_t graph_stream = nullptr;
     uint32_t* graph_next = nullptr;
@@ -896,7 +910,7 @@ void free_all(fml_lm* lm)
     lm->wlo = nullptr;
     void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
                     lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
-                    lm->counters, lm->prompt_dev, lm->grab, lm->step_sync};
+                    lm->counters, lm->prompt_dev, lm->grab, lm->stamp_step};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (lm->host_io) cudaFreeHost(lm->host_io);
@@ -1097,7 +1111,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
 }
 
 int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, const uint32_t* pos, uint32_t P,
-                     uint32_t S, uint32_t chunk, cudaStream_t st, bool pdl = false)
+                     uint32_t S, uint32_t chunk, cudaStream_t st, bool pdl = false, StepStamp stamp = StepStamp{})
 {
     AttnArgs a{};
     a.row0 = row0;
@@ -1118,6 +1132,7 @@ int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, c
     a.part = lm->part;
     a.counters = lm->counters;
     a.grab = lm->grab + layer;
+    a.stamp = stamp;
     FML_REQUIRE(rows <= 65535u, "attention: too many rows in one launch (%u)", rows);
     FML_RC(launch_attention_kernel(a, lm->hd, dim3(lm->hl, rows, S), st, pdl));
     return FML_OK;
@@ -1132,22 +1147,6 @@ int all_reduce_sum(fml_lm* lm, float* buf, uint64_t n, cudaStream_t st)
     return FML_OK;
 }
 
-// Row-parallel projection + all-reduce over peer memory: the GEMV writes this
-// rank's partial into its shared buffer (parity `slot & 1`), the one-shot
-// kernel sums the world's partials and the residual into y.
-int gemv_allreduce(fml_lm* lm, GemvArgs a, float* y, const float* resid, uint32_t slot, cudaStream_t st, bool pdl)
-{
-    const uint64_t n = (uint64_t)a.M * a.N, off = (uint64_t)(slot & 1u) * lm->cfg.max_batch * lm->cfg.d_model;
-    a.y = lm->ar_part + off;
-    a.ldy = a.N;
-    FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
-    return launch_k(ar_oneshot_kernel, dim3(AR_CTAS), dim3(256), st, pdl, y, resid,
-                    (const float* const*)lm->ar_peer_part, off, (uint32_t* const*)lm->ar_peer_flags,
-                    (const uint32_t*)lm->ar_flags, (const uint32_t*)lm->ar_epoch, slot, 2u * lm->cfg.n_layer,
-                    (uint32_t)lm->tp_world,
-                    (uint32_t)lm->tp_rank, n);
-}
-
 // Vocabulary-parallel argmax: every rank's packed (value, ~index) keys hold
 // its local best; the max over ranks is the global first-index argmax.
 int all_reduce_max_keys(fml_lm* lm, uint32_t B, cudaStream_t st)
@@ -1157,38 +1156,57 @@ int all_reduce_max_keys(fml_lm* lm, uint32_t B, cudaStream_t st)
     return FML_OK;
 }
 
-// Plan the fused step for the active batch (once per batch size).
-bool fused_step_ready(fml_lm* lm)
+// The stamp of the next kernel a step enqueues (class `cls`, FML_LM_* profile
+// classes); a null stamp when stamps are off.
+StepStamp next_stamp(fml_lm* lm, int cls)
 {
-    if (!lm->fused || lm->tp_world > 1) return false;
-    if (lm->step_batch == lm->batch) return lm->step_ok;
-    const fml_lm_config& c = lm->cfg;
-    StepArgs& a = lm->sa;
-    a = StepArgs{};
-    a.wbuf = lm->wbuf;
-    a.kc = lm->kc;
-    a.vc = lm->vc;
-    a.layer_stride = lm->layer_stride;
-    a.seq_stride = lm->seq_stride;
-    a.x = lm->x;
-    a.buf = lm->buf;
-    a.q = lm->q;
-    a.att = lm->att;
-    a.hid = lm->hid;
-    a.pending = lm->pending;
-    a.pos = lm->pos;
-    a.keys = lm->keys;
-    a.sync = lm->step_sync;
-    a.B = lm->batch;
-    a.V = c.vocab;
-    a.C = c.context;
-    a.d = c.d_model;
-    a.H = c.n_head;
-    a.hd = lm->hd;
-    a.L = c.n_layer;
-    lm->step_ok = decode_step_plan(a, lm->device, &lm->step_grid, &lm->step_smem) == FML_OK;
-    lm->step_batch = lm->batch;
-    return lm->step_ok;
+    StepStamp s{};
+    if (lm->stamps)
+    {
+        s.buf = lm->stamps;
+        s.step = lm->stamp_step;
+        s.stride = lm->stamp_stride;
+        s.idx = lm->stamp_n;
+        s.cap = lm->stamp_cap;
+    }
+    lm->stamp_class.push_back(cls);
+    ++lm->stamp_n;
+    return s;
+}
+
+// One decode contraction: the tensor-core kernel where the shape allows and
+// the engine has it on, else the CUDA-core GEMV.
+template <int EPI, bool LN>
+int decode_gemv(fml_lm* lm, GemvArgs a, int cls, cudaStream_t st, bool pdl)
+{
+    a.stamp = next_stamp(lm, cls);
+    if (lm->gemv_tc)
+    {
+        GemvTcArgs t{};
+        t.x = a.x; t.ldx = a.ldx; t.w = a.w; t.M = a.M; t.N = a.N; t.K = a.K;
+        t.epi = EPI; t.ln = LN; t.gamma = a.gamma;
+        t.y = a.y; t.ldy = a.ldy; t.r = a.r; t.ldr = a.ldr;
+        t.q = a.q; t.kc = a.kc; t.vc = a.vc; t.pos = a.pos; t.d = a.d; t.hd = a.hd; t.C = a.C;
+        t.seq_stride = a.seq_stride; t.keys = a.keys; t.n_off = a.n_off; t.stamp = a.stamp;
+        if (gemv_tc_supported(t)) return launch_gemv_tc(t, st, pdl);
+    }
+    return launch_gemv<EPI, LN>(a, st, pdl);
+}
+
+// Row-parallel projection + all-reduce over peer memory: the GEMV writes this
+// rank's partial into its shared buffer (parity `slot & 1`), the one-shot
+// kernel sums the world's partials and the residual into y.
+int gemv_allreduce(fml_lm* lm, GemvArgs a, float* y, const float* resid, uint32_t slot, int cls, cudaStream_t st,
+                   bool pdl)
+{
+    const uint64_t n = (uint64_t)a.M * a.N, off = (uint64_t)(slot & 1u) * lm->cfg.max_batch * lm->cfg.d_model;
+    a.y = lm->ar_part + off;
+    a.ldy = a.N;
+    FML_RC((decode_gemv<EPI_STORE, false>(lm, a, cls, st, pdl)));
+    return launch_k(ar_oneshot_kernel, dim3(AR_CTAS), dim3(256), st, pdl, y, resid,
+                    (const float* const*)lm->ar_peer_part, off, (uint32_t* const*)lm->ar_peer_flags,
+                    (const uint32_t*)lm->ar_flags, (const uint32_t*)lm->ar_epoch, slot, 2u * lm->cfg.n_layer,
+                    (uint32_t)lm->tp_world, (uint32_t)lm->tp_rank, n, next_stamp(lm, 9));
 }
 
 // Enqueue one decode step for the active batch: embed, per layer
@@ -1201,20 +1219,14 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
     const fml_lm_config& c = lm->cfg;
     const uint32_t B = lm->batch, d = c.d_model;
     const bool pdl = lm->pdl && !lm->profiling;
-    if (fused_step_ready(lm))
-    {
-        ProfScope ps(lm, 9, st);
-        StepArgs a = lm->sa;
-        a.next_out = next_out;
-        a.logits = logits;
-        return launch_decode_step(a, lm->step_grid, lm->step_smem, st);
-    }
+    const uint64_t launched0 = launch_counter().load(std::memory_order_relaxed);
+    lm->stamp_n = 0;
+    lm->stamp_class.clear();
     {
         ProfScope ps(lm, 0, st);
         FML_RC(launch_k(embed_kernel, dim3(B), dim3(128), st, false, lm->x, (const float*)lm->tok,
                         (const float*)lm->pos_emb, ids ? ids : (const uint32_t*)lm->pending, (const uint32_t*)lm->pos,
-                        B, 1u, d,
-                        c.vocab, c.context, lm->grab, c.n_layer));
+                        B, 1u, d, c.vocab, c.context, lm->grab, c.n_layer, next_stamp(lm, 0)));
     }
     const bool tp = lm->tp_world > 1;
     const bool resid_here = lm->tp_rank == 0;  // row-parallel sums take the residual once
@@ -1226,22 +1238,22 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.x = lm->x; a.ldx = d; a.w = lm->wqkv[l]; a.M = B; a.N = 3 * lm->dl; a.K = d; a.gamma = lm->ln0[l];
             a.q = lm->q; a.kc = lm->kc + (uint64_t)l * lm->layer_stride; a.vc = lm->vc + (uint64_t)l * lm->layer_stride;
             a.pos = lm->pos; a.d = lm->dl; a.H = lm->hl; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
-            FML_RC((launch_gemv<EPI_QKV, true>(a, st, pdl)));
+            FML_RC((decode_gemv<EPI_QKV, true>(lm, a, 2, st, pdl)));
         }
         {
             ProfScope ps(lm, 3, st);
-            FML_RC(launch_attention(lm, l, 0, B, lm->pos, 1, lm->S, 0, st, pdl));
+            FML_RC(launch_attention(lm, l, 0, B, lm->pos, 1, lm->S, 0, st, pdl, next_stamp(lm, 3)));
         }
         {
             ProfScope ps(lm, 4, st);
             GemvArgs a{};
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, st, pdl));
+            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, 4, st, pdl));
             else
             {
-                if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
-                else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
+                if (resid_here) FML_RC((decode_gemv<EPI_RESID, false>(lm, a, 4, st, pdl)));
+                else FML_RC((decode_gemv<EPI_STORE, false>(lm, a, 4, st, pdl)));
                 if (tp) FML_RC(all_reduce_sum(lm, lm->buf, (uint64_t)B * d, st));
             }
         }
@@ -1250,18 +1262,18 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             GemvArgs a{};
             a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = lm->fl; a.K = d; a.gamma = lm->ln1[l];
             a.y = lm->hid; a.ldy = lm->fl;
-            FML_RC((launch_gemv<EPI_GELU, true>(a, st, pdl && (!tp || lm->ar_fused))));
+            FML_RC((decode_gemv<EPI_GELU, true>(lm, a, 5, st, pdl && (!tp || lm->ar_fused))));
         }
         {
             ProfScope ps(lm, 6, st);
             GemvArgs a{};
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, st, pdl));
+            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, 6, st, pdl));
             else
             {
-                if (resid_here) FML_RC((launch_gemv<EPI_RESID, false>(a, st, pdl)));
-                else FML_RC((launch_gemv<EPI_STORE, false>(a, st, pdl)));
+                if (resid_here) FML_RC((decode_gemv<EPI_RESID, false>(lm, a, 6, st, pdl)));
+                else FML_RC((decode_gemv<EPI_STORE, false>(lm, a, 6, st, pdl)));
                 if (tp) FML_RC(all_reduce_sum(lm, lm->x, (uint64_t)B * d, st));
             }
         }
@@ -1271,14 +1283,15 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
         GemvArgs a{};
         a.x = lm->x; a.ldx = d; a.w = lm->tok + (uint64_t)lm->v0 * d; a.M = B; a.N = lm->vl; a.K = d;
         a.gamma = lm->lnf; a.y = logits; a.ldy = lm->vl; a.keys = lm->keys; a.n_off = lm->v0;
-        FML_RC((launch_gemv<EPI_ARGMAX, true>(a, st, pdl && !tp)));
+        FML_RC((decode_gemv<EPI_ARGMAX, true>(lm, a, 7, st, pdl && !tp)));
         if (tp) FML_RC(all_reduce_max_keys(lm, B, st));
     }
     {
         ProfScope ps(lm, 8, st);
         FML_RC(launch_k(finalize_kernel, dim3((B + 127) / 128), dim3(128), st, pdl && !tp, lm->keys, lm->pending,
-                        lm->pos, next_out, B, 0u, lm->ar_epoch));
+                        lm->pos, next_out, B, 0u, lm->ar_epoch, next_stamp(lm, 8), lm->stamp_step));
     }
+    lm->step_kernels = (uint32_t)(launch_counter().load(std::memory_order_relaxed) - launched0);
     return FML_OK;
 }
 
@@ -1344,9 +1357,23 @@ int prefill_gemm(fml_lm* lm, float* C, const float* A, const float* W, int M, in
 }  // namespace
 
 // y[M x N] = x[M x K] . w[N x K]^T for M <= 64 rows (fml_matmul's small-batch
-// Mul<Right>): the decode GEMV without epilogue or programmatic launch.
+// Mul<Right>): the decode contraction without epilogue or programmatic
+// launch -- on the tensor cores in the TF32x3 math mode where the shape
+// allows, else the fp32 CUDA-core GEMV.
+namespace fml {
+int math_mode();
+}
+
 int fml::gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st)
 {
+    if (math_mode() == FML_MATH_TF32X3)
+    {
+        // the tensor-core decode kernel (TF32x3, fp32-level accuracy)
+        GemvTcArgs t{};
+        t.x = x; t.ldx = K; t.w = w; t.M = M; t.N = N; t.K = K;
+        t.epi = GTC_STORE; t.ln = false; t.y = y; t.ldy = N;
+        if (gemv_tc_supported(t)) return launch_gemv_tc(t, st, false);
+    }
     GemvArgs a{};
     a.x = x;
     a.ldx = K;
@@ -1361,10 +1388,8 @@ int fml::gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t 
 
 namespace {
 
-uint32_t graph_nodes_per_step(fml_lm* lm)
-{
-    return fused_step_ready(lm) ? 1u : 1u + lm->cfg.n_layer * 5u + 2u;
-}
+// Kernels one recorded step launches (counted when it was enqueued).
+uint32_t graph_nodes_per_step(fml_lm* lm) { return lm->step_kernels; }
 
 }  // namespace
 
@@ -1435,7 +1460,7 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     if (!rc) rc = alloc((void**)&lm->part, B * H * lm->S * (hd + 2) * f);
     if (!rc) rc = alloc((void**)&lm->counters, B * H * 4);
     if (!rc) rc = alloc((void**)&lm->grab, L * 4);
-    if (!rc) rc = alloc((void**)&lm->step_sync, (uint64_t)decode_step_sync_words((uint32_t)L, 2u) * 4);
+    if (!rc) rc = alloc((void**)&lm->stamp_step, 4);
     if (!rc && cudaMallocHost((void**)&lm->host_io, 2 * B * 4) != cudaSuccess)
         rc = set_error(FML_ERR_NOMEM, "cudaMallocHost failed");
     if (!rc && cudaHostGetDevicePointer((void**)&lm->host_io_dev, lm->host_io, 0) != cudaSuccess)
@@ -1454,7 +1479,7 @@ int fml_lm_create(const fml_lm_config* cfg, int device, fml_lm** out)
     cudaMemset(lm->keys, 0, B * 8);
     cudaMemset(lm->counters, 0, B * H * 4);
     cudaMemset(lm->grab, 0, L * 4);
-    cudaMemset(lm->step_sync, 0, (uint64_t)decode_step_sync_words((uint32_t)L, 2u) * 4);
+    cudaMemset(lm->stamp_step, 0, 4);
 
     // carve the weight buffer
     float* p = lm->wbuf;
@@ -1618,9 +1643,8 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     lm->batch = batch;
     FML_CUDA_TRY(cudaMemcpyAsync(lm->prompt_dev, prompts, (uint64_t)R * 4, cudaMemcpyDeviceToDevice, st));
     FML_CUDA_TRY(cudaMemsetAsync(lm->keys, 0, (uint64_t)c.max_batch * 8, st));
-    FML_CUDA_TRY(cudaMemsetAsync(lm->step_sync, 0, (uint64_t)decode_step_sync_words(c.n_layer, 2u) * 4, st));
     embed_kernel<<<R < 65535u ? R : 65535u, 128, 0, st>>>(lm->x, lm->tok, lm->pos_emb, lm->prompt_dev, nullptr, R, P, d,
-                                                          c.vocab, c.context, nullptr, 0u);
+                                                          c.vocab, c.context, nullptr, 0u, StepStamp{});
     FML_LAUNCH_CHECK();
     const bool tp = lm->tp_world > 1;
     const int resid_epi = lm->tp_rank == 0 ? 2 : 0;  // row-parallel sums take the residual once
@@ -1659,7 +1683,7 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
     FML_RC((launch_gemv<EPI_ARGMAX, false>(a, st, false)));
     if (tp) FML_RC(all_reduce_max_keys(lm, batch, st));
     finalize_kernel<<<(batch + 127) / 128, 128, 0, st>>>(lm->keys, lm->pending, lm->pos, nullptr, batch, P,
-                                                         lm->ar_epoch);
+                                                         lm->ar_epoch, StepStamp{}, nullptr);
     FML_LAUNCH_CHECK();
     for (uint32_t b = 0; b < batch; ++b) lm->hpos[b] = P;
     return FML_OK;
@@ -1728,7 +1752,6 @@ int fml_lm_set_tensor_parallel(fml_lm* lm, int rank, int world, const void* nccl
     FML_CUDA_TRY(cudaMalloc(&lm->ar_epoch, sizeof(uint32_t)));
     FML_CUDA_TRY(cudaMemset(lm->ar_flags, 0, (uint64_t)world * AR_CTAS * sizeof(uint32_t)));
     FML_CUDA_TRY(cudaMemset(lm->ar_epoch, 0, sizeof(uint32_t)));
-    lm->step_batch = 0;
     drop_graphs(lm);
     return FML_OK;
 }
@@ -1795,19 +1818,37 @@ int fml_lm_tp_error_count(uint64_t* out)
     return FML_OK;
 }
 
-int fml_lm_set_fused_step(fml_lm* lm, int on)
+int fml_lm_set_decode_gemv(fml_lm* lm, int mode)
 {
-    FML_REQUIRE(lm, "fml_lm_set_fused_step: null engine");
-    lm->fused = on != 0;
-    lm->step_batch = 0;
+    FML_REQUIRE(lm, "fml_lm_set_decode_gemv: null engine");
+    FML_REQUIRE(mode == FML_DECODE_GEMV_CUDA_CORES || mode == FML_DECODE_GEMV_TENSOR_CORES,
+                "fml_lm_set_decode_gemv: unknown mode %d", mode);
+    lm->gemv_tc = mode == FML_DECODE_GEMV_TENSOR_CORES;
     drop_graphs(lm);
     return FML_OK;
 }
 
-int fml_lm_get_fused_step(fml_lm* lm, int* active)
+int fml_lm_set_stamps(fml_lm* lm, unsigned long long* stamps, uint32_t cap, uint32_t* stride)
 {
-    FML_REQUIRE(lm && active, "fml_lm_get_fused_step: null argument");
-    *active = lm->batch > 0 && fused_step_ready(lm) ? 1 : 0;
+    FML_REQUIRE(lm, "fml_lm_set_stamps: null engine");
+    FML_REQUIRE(!stamps || aligned16(stamps), "fml_lm_set_stamps: the buffer must be 16-byte aligned");
+    lm->stamps = cap ? stamps : nullptr;
+    lm->stamp_cap = lm->stamps ? cap : 0u;
+    // an upper bound of the kernels of one step: embed, per layer the QKV,
+    // attention, proj and mlp GEMVs (with their all-reduce kernels under
+    // tensor parallelism) and fc, lm_head, finalize
+    lm->stamp_stride = 3u + 7u * lm->cfg.n_layer;
+    if (stride) *stride = lm->stamp_stride;
+    FML_CUDA_TRY(cudaMemset(lm->stamp_step, 0, 4));
+    drop_graphs(lm);
+    return FML_OK;
+}
+
+int fml_lm_stamp_classes(fml_lm* lm, int* classes, uint32_t n, uint32_t* kernels)
+{
+    FML_REQUIRE(lm && kernels, "fml_lm_stamp_classes: null argument");
+    *kernels = (uint32_t)lm->stamp_class.size();
+    for (uint32_t i = 0; i < n && i < lm->stamp_class.size(); ++i) classes[i] = lm->stamp_class[i];
     return FML_OK;
 }
 
@@ -1836,12 +1877,12 @@ int check_step_state(fml_lm* lm, const char* fn)
 // its tokens from host_io[0, B) and leaves the next tokens in
 // host_io[max_batch, max_batch + B) (pinned host memory): the step's first
 // kernel reads them over the host link and its last kernel writes them back
-// (mapped memory; otherwise, and for the fused step, copies bracket it).
+// (mapped memory; otherwise copies bracket it).
 int record_step(fml_lm* lm, uint32_t* next_tokens, float* logits, bool host_io, cudaGraphExec_t* out)
 {
     *out = nullptr;
     const uint32_t B = lm->batch;
-    const bool mapped = host_io && lm->host_io_dev && !fused_step_ready(lm);
+    const bool mapped = host_io && lm->host_io_dev;
     cudaStream_t cap;
     FML_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
     FML_CUDA_TRY(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));

@@ -185,14 +185,32 @@ class NanoLM:
         buf = ctypes.create_string_buffer(blob, len(blob))
         call("fml_lm_tp_connect", self._h, buf)
 
-    def set_fused_step(self, on: bool) -> None:
-        """Fused decode step (one persistent kernel per step) on or off."""
-        call("fml_lm_set_fused_step", self._h, int(bool(on)))
+    def set_decode_gemv(self, mode: int) -> None:
+        """Decode contractions on the tensor cores (FML_DECODE_GEMV_TENSOR_CORES,
+        default: TF32x3 where the shape allows) or on the CUDA cores
+        (FML_DECODE_GEMV_CUDA_CORES)."""
+        call("fml_lm_set_decode_gemv", self._h, int(mode))
 
-    def fused_step_active(self) -> bool:
-        v = ctypes.c_int(0)
-        call("fml_lm_get_fused_step", self._h, ctypes.byref(v))
-        return bool(v.value)
+    def stamped_pass(self, run, steps: int):
+        """Run `run()` (which must enqueue `steps` engine steps through the
+        recorded graph) with in-graph completion stamps, and return
+        (stamps [steps, kernels] in ns as int64, classes [kernels]): the time
+        each kernel of the step finished, as the timed graph runs it.  Stamps
+        are turned off again afterwards."""
+        stride = ctypes.c_uint32()
+        buf = torch.zeros(max(1, steps) * (3 + 7 * self.shape.n_layer), dtype=torch.int64,
+                          device=torch.device("cuda", self.device))
+        call("fml_lm_set_stamps", self._h, buf.data_ptr(), buf.numel(), ctypes.byref(stride))
+        try:
+            run()
+            torch.cuda.synchronize(self.device)
+            nk = ctypes.c_uint32()
+            cls = (ctypes.c_int * stride.value)()
+            call("fml_lm_stamp_classes", self._h, ctypes.cast(cls, ctypes.c_void_p), stride.value, ctypes.byref(nk))
+        finally:
+            call("fml_lm_set_stamps", self._h, None, 0, None)
+        st = buf.view(-1, stride.value)[:steps, :nk.value].cpu().numpy()
+        return st, [PROFILE_CLASSES[c] for c in list(cls)[:nk.value]]
 
     def set_prefill_math(self, mode: int) -> None:
         """FML_MATH_TF32X3 (default, tensor cores), FML_MATH_TF32 or FML_MATH_FP32."""

@@ -380,13 +380,18 @@ FML_API int fml_tp_flag_check(uint32_t epoch, uint32_t slot, uint32_t nslot, uin
  * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy). */
 FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
 
-/* Fused decode step (default off): one persistent kernel per step when the
- * shape fits (batch <= 32, d_model a multiple of 32, head dim 32/64/128,
- * 4*d_model <= 8192); otherwise, or when off, the per-operation kernels run.
- * fml_lm_get_fused_step reports whether the fused kernel serves the
- * current batch. */
-FML_API int fml_lm_set_fused_step(fml_lm* lm, int on);
-FML_API int fml_lm_get_fused_step(fml_lm* lm, int* active);
+/* Decode contractions (QKV, projection, fc, mlp, lm_head of every step).
+ * FML_DECODE_GEMV_TENSOR_CORES (default): tcgen05 tensor cores in TF32x3
+ * (fp32-level accuracy, fp32 accumulation) with the LayerNorm, GELU,
+ * residual, K/V-cache and argmax work fused in, wherever the shape allows
+ * (batch <= 64, K a multiple of 32 split into at most 16 slices of <= 128,
+ * N a multiple of 4); the other shapes, and FML_DECODE_GEMV_CUDA_CORES, use
+ * the fp32 CUDA-core GEMVs.  The environment variable FML_GEMV_TC=0 also
+ * turns the tensor-core kernel off.  No counterpart in the reference (its
+ * Dense::Forward is Mul over the whole window, Dense.h:179-223). */
+#define FML_DECODE_GEMV_CUDA_CORES 0
+#define FML_DECODE_GEMV_TENSOR_CORES 1
+FML_API int fml_lm_set_decode_gemv(fml_lm* lm, int mode);
 
 /* One decode step for every active sequence: consume each sequence's pending
  * token, append its K/V, and produce the next token (greedy).  Optional
@@ -435,11 +440,25 @@ FML_API uint64_t fml_lm_step_bytes(fml_lm* lm);
 /* Kernel timing: with profiling on (and graphs off), every step records CUDA
  * events around each kernel class and accumulates milliseconds and launch
  * counts per class: 0 embed, 1 layernorm, 2 qkv, 3 attention, 4 proj,
- * 5 fc, 6 mlp, 7 lm_head, 8 argmax/finalize, 9 the fused step kernel (the
- * only class a fused step records).  Reset when turned on. */
+ * 5 fc, 6 mlp, 7 lm_head, 8 argmax/finalize, 9 the tensor-parallel
+ * all-reduce kernel.  Reset when turned on.  Eager launches without
+ * programmatic dependent launch: not the timed execution (see stamps). */
 enum { FML_LM_NCLASS = 10 };
 FML_API int fml_lm_set_profiling(fml_lm* lm, int on);
 FML_API int fml_lm_get_profile(fml_lm* lm, double* ms_by_class, uint64_t* launches_by_class, int n_classes);
+
+/* In-graph kernel timing of the decode step as it is timed (CUDA graph,
+ * programmatic dependent launch).  With `stamps` set (device memory,
+ * `cap` zeroed uint64 slots), the step is recorded again with every kernel's
+ * CTAs raising slot [s * stride + i] to the global timer (ns) as they
+ * finish, where s counts the steps since this call and i is the kernel's
+ * index within the step; *stride receives the slots per step.  The time a
+ * kernel adds to the step is its slot minus the previous kernel's.
+ * fml_lm_stamp_classes gives the profile class (above) of each index of the
+ * last recorded step and *kernels their number.  Null turns stamps off
+ * (re-records without them).  No counterpart in the reference. */
+FML_API int fml_lm_set_stamps(fml_lm* lm, unsigned long long* stamps, uint32_t cap, uint32_t* stride);
+FML_API int fml_lm_stamp_classes(fml_lm* lm, int* classes, uint32_t n, uint32_t* kernels);
 /* Algorithmic bytes of the attention kernels of one step (K/V rows read,
  * queries read, outputs written), for the attention roofline. */
 FML_API uint64_t fml_lm_attention_bytes(fml_lm* lm);

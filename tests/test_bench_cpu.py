@@ -75,3 +75,20 @@ def test_reference_arm_prints_the_contract_line():
     assert d["value"] > 0 and d["steps"] == 1
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_kernel_times_from_stamps():
+    """In-graph kernel times: each kernel's completion minus the previous
+    kernel's; the first kernel of a step is measured from the previous
+    step's last; step 0 (no previous step in the pass) is left out; the
+    per-class times add up to the stamped step time."""
+    import numpy as np
+    classes = ["embed", "qkv", "attention", "finalize"]
+    # two steps of 4 kernels, completion times in ns
+    stamps = np.array([[100, 110, 150, 160],
+                       [170, 185, 235, 240]], dtype=np.int64)
+    kt = bench.kernel_times_from_stamps(stamps, classes)
+    assert kt["steps"] == 1
+    assert kt["by_class_ns"] == {"embed": 10, "qkv": 15, "attention": 50, "finalize": 5}
+    assert kt["launches"] == {"embed": 1, "qkv": 1, "attention": 1, "finalize": 1}
+    assert kt["total_ns"] == 80 == sum(kt["by_class_ns"].values())

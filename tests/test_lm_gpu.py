@@ -11,6 +11,9 @@ Small shapes are compared with the committed golden vectors (the reference's
 own greedy loop); BASELINE config 3 (32 sequences) is checked teacher-forced:
 one oracle forward over each GPU token stream gives the reference logits of
 every generated row (row t depends on tokens <= t only)."""
+import json
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -22,13 +25,44 @@ pytestmark = pytest.mark.gpu
 ATOL = RTOL = 1e-3
 GAP = 2e-3
 
+# decode contractions: tcgen05 TF32x3 (the default) or fp32 CUDA cores
+GEMV = {"tensor_cores": 1, "cuda_cores": 0}
 
-def _lm(shape, batch, fused=False):
+
+def _lm(shape, batch, gemv="tensor_cores"):
     from freeml_b200.lm import NanoLLMShape, NanoLM
     s = NanoLLMShape(shape.V, shape.C, shape.d, shape.H, shape.L)
     lm = NanoLM(s, batch)
-    lm.set_fused_step(fused)
+    lm.set_decode_gemv(GEMV[gemv])
     return lm
+
+
+def _report(name, rows):
+    """Append per-sequence parity results (first-divergence step: -1 none,
+    <= -2 a near-tie at step -2 - v; max |dlogit|) to the JSON-lines file
+    FML_PARITY_REPORT names, when set."""
+    path = os.environ.get("FML_PARITY_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"test": name, "sequences": rows}) + "\n")
+
+
+def _check_teacher_forced(name, ref_rows_fn, toks, logits, seqs, P, N):
+    """Every generated row of the sequences `seqs` against reference logits
+    (ref_rows_fn(b) -> rows P-1 .. P+N-2): argmax agreement up to the first
+    near-tie, logits within the fp32 bound; reports the divergence steps."""
+    rows = []
+    for k, b in enumerate(seqs):
+        ref = ref_rows_fn(b)
+        div = first_divergence(ref, toks[b, P:])
+        upto = N if div == -1 else (-2 - div if div < -1 else div)
+        err = float(np.abs(logits[: upto - 1, k, :] - ref[1:upto]).max()) if upto > 1 else 0.0
+        rows.append({"seq": int(b), "first_divergence": int(div), "rows_compared": int(upto), "max_abs_dlogit": err})
+        assert div == -1 or div < -1, f"{name} sequence {b}: first divergence at step {div}"
+        np.testing.assert_allclose(logits[: upto - 1, k, :], ref[1:upto], rtol=RTOL, atol=ATOL,
+                                   err_msg=f"{name} sequence {b}")
+    _report(name, rows)
+    return rows
 
 
 def first_divergence(ref_logits, gpu_tokens_next):
@@ -44,20 +78,19 @@ def first_divergence(ref_logits, gpu_tokens_next):
     return -1
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["fused_step", "per_op"])
+@pytest.mark.parametrize("gemv", sorted(GEMV))
 @pytest.mark.parametrize("name", ["cfg1", "odd"])
-def test_greedy_matches_reference_loop(golden, name, fused):
-    """Fused step kernel and per-operation kernels, each against the
-    reference's greedy loop."""
+def test_greedy_matches_reference_loop(golden, name, gemv):
+    """Decode contractions on the tensor cores and on the CUDA cores, each
+    against the reference's greedy loop."""
     meta, g, _ = golden
     m = meta["greedy"][name]
     s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
     w = O.init_weights(s, m["wseed"])
-    lm = _lm(s, 1, fused)
+    lm = _lm(s, 1, gemv)
     lm.bind(w)
     prompt = g[f"{name}_prompt"].reshape(1, -1)
     toks, logits = lm.generate(prompt, m["new"], want_logits=True)
-    assert lm.fused_step_active() == fused
     ref_toks, ref_logits = g[f"{name}_tokens"], g[f"{name}_logits"]
     # logits[k] is generated row plen + k (the rows after the prefill's)
     np.testing.assert_allclose(logits[:, 0, :], ref_logits[1:], rtol=RTOL, atol=ATOL)
@@ -213,12 +246,11 @@ def test_batched_sequences_are_independent(golden):
     lm.bind(w)
     batched, _ = lm.generate(prompts, 24)
     lm.close()
-    fused = _lm(s, 4, fused=True)
-    fused.bind(w)
-    fused_toks, _ = fused.generate(prompts, 24)
-    assert fused.fused_step_active()
-    fused.close()
-    np.testing.assert_array_equal(batched, fused_toks)
+    cores = _lm(s, 4, "cuda_cores")
+    cores.bind(w)
+    cores_toks, _ = cores.generate(prompts, 24)
+    cores.close()
+    np.testing.assert_array_equal(batched, cores_toks)
     for b in range(4):
         lm1 = _lm(s, 1)
         lm1.bind(w)
@@ -227,33 +259,71 @@ def test_batched_sequences_are_independent(golden):
         np.testing.assert_array_equal(batched[b], single[0])
 
 
-@pytest.mark.parametrize("fused,nseq_checked,batch", [(False, 4, 32), (True, 2, 32), (False, 2, 8)],
-                         ids=["per_op", "fused_step", "per_op_8seq"])
-def test_config3_teacher_forced(fused, nseq_checked, batch):
+@pytest.mark.parametrize("gemv,nseq_checked,batch", [("tensor_cores", 4, 32), ("cuda_cores", 2, 32),
+                                                   ("tensor_cores", 2, 8), ("tensor_cores", 2, 4)],
+                         ids=["tc_32seq", "cuda_cores_32seq", "tc_8seq", "tc_4seq"])
+def test_config3_teacher_forced(gemv, nseq_checked, batch):
     """V4096 C512 d512 H8 L8, 32 sequences, 128-token
-    prompts (seed 4), 384 greedy tokens.  The engine decodes all 32 (or the
-    first 8: the 8-row GEMV variants, as on each of 4 GPUs); the oracle checks
-    `nseq_checked` of them (every generated row) teacher-forced."""
+    prompts (seed 4), 384 greedy tokens, on the reference's own weights.  The
+    engine decodes all 32 (or the first 8 or 4: the batches of one GPU at 4
+    and 8 GPUs); the C oracle (bit-exact with the reference) checks
+    `nseq_checked` of them, every generated row, teacher-forced."""
     from freeml_b200.lm import CONFIGS, prompt_tokens
     c = CONFIGS[3]
     sh = c["shape"]
     s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
     w = O.init_weights(s, c["wseed"])
     prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])[:batch]
-    lm = _lm(s, batch, fused)
+    lm = _lm(s, batch, gemv)
     lm.bind(w)
-    toks, logits = lm.generate(prompts, c["new"], want_logits=True)
-    assert lm.fused_step_active() == fused
+    seqs = [int(b) for b in np.linspace(0, batch - 1, nseq_checked).astype(int)]
+    toks, logits = lm.generate(prompts, c["new"], want_logits=True, logit_rows=seqs)
     lm.close()
     P, N = c["prompt"], c["new"]
     assert toks.shape == (batch, P + N)
-    for b in np.linspace(0, batch - 1, nseq_checked).astype(int):
-        ref = O.forward(s, w, toks[b, : P + N - 1], row0=P - 1, nrows=N)  # rows P-1 .. P+N-2
-        div = first_divergence(ref, toks[b, P:])
-        assert div == -1 or div < -1, f"sequence {b}: first divergence at step {div}"
-        upto = N if div == -1 else (-2 - div)
-        got = logits[: upto - 1, b, :]
-        np.testing.assert_allclose(got, ref[1:upto], rtol=RTOL, atol=ATOL)
+    _check_teacher_forced(f"config3_{gemv}_{batch}seq_oracle",
+                          lambda b: O.forward(s, w, toks[b, : P + N - 1], row0=P - 1, nrows=N),
+                          toks, logits, seqs, P, N)
+
+
+def _torch_rows(params, sh, toks, P, N):
+    """rows P-1 .. P+N-2 of the PyTorch fp32 restatement (TF32 off) on the GPU"""
+    from tests import torch_ref
+
+    def rows(b):
+        with torch.no_grad():
+            return torch_ref.forward(params, sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer,
+                                     toks[b, : P + N - 1].astype(np.int64), P - 1, N).cpu().numpy()
+    return rows
+
+
+@pytest.fixture
+def fp32_matmul():
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def test_config3_all_sequences_teacher_forced(fp32_matmul):
+    """Config 3, every one of the 32 sequences and all 383 generated rows,
+    on the reference's weights, teacher-forced against the PyTorch fp32
+    restatement on the GPU (pinned to the reference compiled from FreeML at
+    this very shape by tests/test_torch_ref_cpu.py)."""
+    from freeml_b200.lm import CONFIGS, prompt_tokens
+    c = CONFIGS[3]
+    sh = c["shape"]
+    s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
+    w = O.init_weights(s, c["wseed"])
+    prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])
+    lm = _lm(s, c["batch"])
+    lm.bind(w)
+    toks, logits = lm.generate(prompts, c["new"], want_logits=True)
+    lm.close()
+    P, N = c["prompt"], c["new"]
+    params = torch.from_numpy(w).cuda()
+    _check_teacher_forced("config3_all_torch", _torch_rows(params, sh, toks, P, N), toks, logits,
+                          list(range(c["batch"])), P, N)
 
 
 # TF32 (one pass, 10-bit mantissa operands) prefill: a looser stated bound.
@@ -315,37 +385,42 @@ def test_config4_prefill_heavy_teacher_forced():
         np.testing.assert_allclose(logits[: upto - 1, k, :], ref[1:upto], rtol=RTOL, atol=ATOL)
 
 
-def test_config5_teacher_forced_vs_torch_fp32():
+def test_config4_all_sequences_teacher_forced(fp32_matmul):
+    """Config 4, all 64 sequences x 63 generated rows after the 1536-token
+    tensor-core prefill, teacher-forced against the PyTorch fp32
+    restatement on the GPU, on the reference's weights."""
+    from freeml_b200.lm import CONFIGS, prompt_tokens
+    c = CONFIGS[4]
+    sh = c["shape"]
+    s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
+    w = O.init_weights(s, c["wseed"])
+    prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])
+    lm = _lm(s, c["batch"])
+    lm.bind(w)
+    toks, logits = lm.generate(prompts, c["new"], want_logits=True)
+    lm.close()
+    P, N = c["prompt"], c["new"]
+    params = torch.from_numpy(w).cuda()
+    _check_teacher_forced("config4_all_torch", _torch_rows(params, sh, toks, P, N), toks, logits,
+                          list(range(c["batch"])), P, N)
+
+
+def test_config5_teacher_forced_vs_torch_fp32(fp32_matmul):
     """BASELINE config 5 on one GPU: V32000 C4096 d4096 H32 L32 (6.6e9 fp32
     parameters, seeded N(0, 0.02) on the device), 8 sequences of 1024 prompt
-    tokens (seed 8), 8 greedy tokens.  The C oracle cannot run this size, so
-    two sequences are checked teacher-forced against the PyTorch fp32
-    restatement (pinned to the reference's golden logits on CPU), with TF32
-    off in the check."""
-    import torch
-
+    tokens (seed 8), the full 256 greedy tokens.  The C oracle cannot run this
+    size, so all 8 sequences are checked, every generated row,
+    teacher-forced against the PyTorch fp32 restatement (pinned to the
+    reference on CPU), with TF32 off in the check."""
     from freeml_b200.lm import CONFIGS, NanoLM, prompt_tokens, random_params
-    from tests import torch_ref
     c = CONFIGS[5]
     sh = c["shape"]
     params = random_params(sh, c["wseed"], 0)
-    P, N, B = c["prompt"], 8, c["batch"]
+    P, N, B = c["prompt"], c["new"], c["batch"]
     prompts = prompt_tokens(c["pseed"], sh.vocab, B, P)
-    checked = [0, B - 1]
     lm = NanoLM(sh, B)
     lm.bind(params)
-    toks, logits = lm.generate(prompts, N, want_logits=True, logit_rows=checked)
+    toks, logits = lm.generate(prompts, N, want_logits=True)
     lm.close()
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = False
-    try:
-        for k, b in enumerate(checked):
-            with torch.no_grad():
-                ref = torch_ref.forward(params, sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer,
-                                        toks[b, : P + N - 1].astype(np.int64), P - 1, N).cpu().numpy()
-            div = first_divergence(ref, toks[b, P:])
-            assert div == -1 or div < -1, f"sequence {b}: first divergence at step {div}"
-            upto = N if div == -1 else (-2 - div)
-            np.testing.assert_allclose(logits[: upto - 1, k, :], ref[1:upto], rtol=RTOL, atol=ATOL)
-    finally:
-        torch.backends.cuda.matmul.allow_tf32 = prev
+    _check_teacher_forced("config5_all_torch", _torch_rows(params, sh, toks, P, N), toks, logits,
+                          list(range(B)), P, N)
