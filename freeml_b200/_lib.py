@@ -20,7 +20,6 @@ FML_MATH_FP32, FML_MATH_TF32X3, FML_MATH_TF32 = 0, 1, 2
 FML_LM_NCLASS = 10
 PROFILE_CLASSES = ["embed", "layernorm", "qkv", "attention", "proj", "fc", "mlp", "lm_head", "finalize",
                    "allreduce"]
-FML_DECODE_GEMV_CUDA_CORES, FML_DECODE_GEMV_TENSOR_CORES = 0, 1
 
 
 class FmlError(RuntimeError):
@@ -98,7 +97,6 @@ SIGNATURES = {
     "fml_lm_generate_host": (_I, [_P, _U32, _P, _P, _P]),
     "fml_lm_set_graph": (_I, [_P, _I]),
     "fml_lm_set_prefill_math": (_I, [_P, _I]),
-    "fml_lm_set_decode_gemv": (_I, [_P, _I]),
     "fml_lm_set_stamps": (_I, [_P, _P, _U32, ctypes.POINTER(_U32)]),
     "fml_lm_stamp_classes": (_I, [_P, _P, _U32, ctypes.POINTER(_U32)]),
     "fml_nccl_unique_id": (_I, [_P]),

@@ -11,9 +11,13 @@
 #include <cuda.h>
 
 #include "attention.cuh"
-#include "gemv_tcgen05.cuh"
 
 namespace fml {
+
+#ifdef FML_TIMELINE
+// debug builds: this unit's timeline ring (fml_debug_timeline binds it)
+int timeline_bind_attention(TimelineRec* p, uint32_t cap) { return timeline_bind_unit(p, cap); }
+#endif
 
 // Causal attention for one query row over the cached keys 0..len-1
 // (CausalSelfAttentionLayer.h:424-499: Q_h K_h^T, * 1/sqrt(hd) + causal
@@ -379,13 +383,12 @@ extern "C" {
 int fml_device_error_count(uint64_t* count)
 {
     FML_REQUIRE(count, "fml_device_error_count: null argument");
-    int g = 0, f = 0;
+    int g = 0;
     uint64_t tpw = 0;
     FML_CUDA_TRY(cudaDeviceSynchronize());
     FML_RC(gemm_tc_error_count(&g));
-    FML_RC(gemv_tc_error_count(&f));
     FML_RC(fml_lm_tp_error_count(&tpw));
-    *count = (uint64_t)g + (uint64_t)f + tpw;
+    *count = (uint64_t)g + tpw;
     return FML_OK;
 }
 

@@ -37,7 +37,6 @@
 #include <nccl.h>
 
 #include "attention.cuh"
-#include "gemv_tcgen05.cuh"
 #include "fml_common.cuh"
 
 #ifdef FML_TIMELINE
@@ -849,9 +848,6 @@ struct fml_lm
     uint32_t** ar_peer_flags = nullptr;
     std::vector<void*> ar_opened;    // peer mappings to close
 
-    // decode contractions: tensor cores (TF32x3 on tcgen05) where the shape
-    // allows, else the CUDA-core GEMVs (fml_lm_set_decode_gemv)
-    bool gemv_tc = true;
     // in-graph completion stamps (fml_lm_set_stamps): one slot per kernel of
     // a step, `stamp_stride` slots per step; the class of each slot
     unsigned long long* stamps = nullptr;
@@ -1174,22 +1170,12 @@ StepStamp next_stamp(fml_lm* lm, int cls)
     return s;
 }
 
-// One decode contraction: the tensor-core kernel where the shape allows and
-// the engine has it on, else the CUDA-core GEMV.
+// One decode contraction (the CUDA-core GEMV with its fused prologue and
+// epilogue) with the step's next completion stamp.
 template <int EPI, bool LN>
 int decode_gemv(fml_lm* lm, GemvArgs a, int cls, cudaStream_t st, bool pdl)
 {
     a.stamp = next_stamp(lm, cls);
-    if (lm->gemv_tc)
-    {
-        GemvTcArgs t{};
-        t.x = a.x; t.ldx = a.ldx; t.w = a.w; t.M = a.M; t.N = a.N; t.K = a.K;
-        t.epi = EPI; t.ln = LN; t.gamma = a.gamma;
-        t.y = a.y; t.ldy = a.ldy; t.r = a.r; t.ldr = a.ldr;
-        t.q = a.q; t.kc = a.kc; t.vc = a.vc; t.pos = a.pos; t.d = a.d; t.hd = a.hd; t.C = a.C;
-        t.seq_stride = a.seq_stride; t.keys = a.keys; t.n_off = a.n_off; t.stamp = a.stamp;
-        if (gemv_tc_supported(t)) return launch_gemv_tc(t, st, pdl);
-    }
     return launch_gemv<EPI, LN>(a, st, pdl);
 }
 
@@ -1357,23 +1343,9 @@ int prefill_gemm(fml_lm* lm, float* C, const float* A, const float* W, int M, in
 }  // namespace
 
 // y[M x N] = x[M x K] . w[N x K]^T for M <= 64 rows (fml_matmul's small-batch
-// Mul<Right>): the decode contraction without epilogue or programmatic
-// launch -- on the tensor cores in the TF32x3 math mode where the shape
-// allows, else the fp32 CUDA-core GEMV.
-namespace fml {
-int math_mode();
-}
-
+// Mul<Right>): the decode GEMV without epilogue or programmatic launch.
 int fml::gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st)
 {
-    if (math_mode() == FML_MATH_TF32X3)
-    {
-        // the tensor-core decode kernel (TF32x3, fp32-level accuracy)
-        GemvTcArgs t{};
-        t.x = x; t.ldx = K; t.w = w; t.M = M; t.N = N; t.K = K;
-        t.epi = GTC_STORE; t.ln = false; t.y = y; t.ldy = N;
-        if (gemv_tc_supported(t)) return launch_gemv_tc(t, st, false);
-    }
     GemvArgs a{};
     a.x = x;
     a.ldx = K;
@@ -1815,16 +1787,6 @@ int fml_lm_tp_error_count(uint64_t* out)
     unsigned int v = 0;
     FML_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_tp_timeouts, sizeof(v)));
     *out = v;
-    return FML_OK;
-}
-
-int fml_lm_set_decode_gemv(fml_lm* lm, int mode)
-{
-    FML_REQUIRE(lm, "fml_lm_set_decode_gemv: null engine");
-    FML_REQUIRE(mode == FML_DECODE_GEMV_CUDA_CORES || mode == FML_DECODE_GEMV_TENSOR_CORES,
-                "fml_lm_set_decode_gemv: unknown mode %d", mode);
-    lm->gemv_tc = mode == FML_DECODE_GEMV_TENSOR_CORES;
-    drop_graphs(lm);
     return FML_OK;
 }
 

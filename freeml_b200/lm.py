@@ -185,12 +185,6 @@ class NanoLM:
         buf = ctypes.create_string_buffer(blob, len(blob))
         call("fml_lm_tp_connect", self._h, buf)
 
-    def set_decode_gemv(self, mode: int) -> None:
-        """Decode contractions on the tensor cores (FML_DECODE_GEMV_TENSOR_CORES,
-        default: TF32x3 where the shape allows) or on the CUDA cores
-        (FML_DECODE_GEMV_CUDA_CORES)."""
-        call("fml_lm_set_decode_gemv", self._h, int(mode))
-
     def stamped_pass(self, run, steps: int):
         """Run `run()` (which must enqueue `steps` engine steps through the
         recorded graph) with in-graph completion stamps, and return

@@ -380,18 +380,6 @@ FML_API int fml_tp_flag_check(uint32_t epoch, uint32_t slot, uint32_t nslot, uin
  * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy). */
 FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
 
-/* Decode contractions (QKV, projection, fc, mlp, lm_head of every step).
- * FML_DECODE_GEMV_TENSOR_CORES (default): tcgen05 tensor cores in TF32x3
- * (fp32-level accuracy, fp32 accumulation) with the LayerNorm, GELU,
- * residual, K/V-cache and argmax work fused in, wherever the shape allows
- * (batch <= 64, K a multiple of 32 split into at most 16 slices of <= 128,
- * N a multiple of 4); the other shapes, and FML_DECODE_GEMV_CUDA_CORES, use
- * the fp32 CUDA-core GEMVs.  The environment variable FML_GEMV_TC=0 also
- * turns the tensor-core kernel off.  No counterpart in the reference (its
- * Dense::Forward is Mul over the whole window, Dense.h:179-223). */
-#define FML_DECODE_GEMV_CUDA_CORES 0
-#define FML_DECODE_GEMV_TENSOR_CORES 1
-FML_API int fml_lm_set_decode_gemv(fml_lm* lm, int mode);
 
 /* One decode step for every active sequence: consume each sequence's pending
  * token, append its K/V, and produce the next token (greedy).  Optional

@@ -25,16 +25,10 @@ pytestmark = pytest.mark.gpu
 ATOL = RTOL = 1e-3
 GAP = 2e-3
 
-# decode contractions: tcgen05 TF32x3 (the default) or fp32 CUDA cores
-GEMV = {"tensor_cores": 1, "cuda_cores": 0}
-
-
-def _lm(shape, batch, gemv="tensor_cores"):
+def _lm(shape, batch):
     from freeml_b200.lm import NanoLLMShape, NanoLM
     s = NanoLLMShape(shape.V, shape.C, shape.d, shape.H, shape.L)
-    lm = NanoLM(s, batch)
-    lm.set_decode_gemv(GEMV[gemv])
-    return lm
+    return NanoLM(s, batch)
 
 
 def _report(name, rows):
@@ -78,16 +72,15 @@ def first_divergence(ref_logits, gpu_tokens_next):
     return -1
 
 
-@pytest.mark.parametrize("gemv", sorted(GEMV))
 @pytest.mark.parametrize("name", ["cfg1", "odd"])
-def test_greedy_matches_reference_loop(golden, name, gemv):
-    """Decode contractions on the tensor cores and on the CUDA cores, each
-    against the reference's greedy loop."""
+def test_greedy_matches_reference_loop(golden, name):
+    """The engine against the reference's greedy loop: identical tokens,
+    logits within the fp32 bound."""
     meta, g, _ = golden
     m = meta["greedy"][name]
     s = O.LMShape(m["V"], m["C"], m["d"], m["H"], m["L"])
     w = O.init_weights(s, m["wseed"])
-    lm = _lm(s, 1, gemv)
+    lm = _lm(s, 1)
     lm.bind(w)
     prompt = g[f"{name}_prompt"].reshape(1, -1)
     toks, logits = lm.generate(prompt, m["new"], want_logits=True)
@@ -246,11 +239,6 @@ def test_batched_sequences_are_independent(golden):
     lm.bind(w)
     batched, _ = lm.generate(prompts, 24)
     lm.close()
-    cores = _lm(s, 4, "cuda_cores")
-    cores.bind(w)
-    cores_toks, _ = cores.generate(prompts, 24)
-    cores.close()
-    np.testing.assert_array_equal(batched, cores_toks)
     for b in range(4):
         lm1 = _lm(s, 1)
         lm1.bind(w)
@@ -259,10 +247,8 @@ def test_batched_sequences_are_independent(golden):
         np.testing.assert_array_equal(batched[b], single[0])
 
 
-@pytest.mark.parametrize("gemv,nseq_checked,batch", [("tensor_cores", 4, 32), ("cuda_cores", 2, 32),
-                                                   ("tensor_cores", 2, 8), ("tensor_cores", 2, 4)],
-                         ids=["tc_32seq", "cuda_cores_32seq", "tc_8seq", "tc_4seq"])
-def test_config3_teacher_forced(gemv, nseq_checked, batch):
+@pytest.mark.parametrize("nseq_checked,batch", [(4, 32), (2, 8), (2, 4)], ids=["32seq", "8seq", "4seq"])
+def test_config3_teacher_forced(nseq_checked, batch):
     """V4096 C512 d512 H8 L8, 32 sequences, 128-token
     prompts (seed 4), 384 greedy tokens, on the reference's own weights.  The
     engine decodes all 32 (or the first 8 or 4: the batches of one GPU at 4
@@ -274,14 +260,14 @@ def test_config3_teacher_forced(gemv, nseq_checked, batch):
     s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
     w = O.init_weights(s, c["wseed"])
     prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])[:batch]
-    lm = _lm(s, batch, gemv)
+    lm = _lm(s, batch)
     lm.bind(w)
     seqs = [int(b) for b in np.linspace(0, batch - 1, nseq_checked).astype(int)]
     toks, logits = lm.generate(prompts, c["new"], want_logits=True, logit_rows=seqs)
     lm.close()
     P, N = c["prompt"], c["new"]
     assert toks.shape == (batch, P + N)
-    _check_teacher_forced(f"config3_{gemv}_{batch}seq_oracle",
+    _check_teacher_forced(f"config3_{batch}seq_oracle",
                           lambda b: O.forward(s, w, toks[b, : P + N - 1], row0=P - 1, nrows=N),
                           toks, logits, seqs, P, N)
 
