@@ -19,6 +19,7 @@ constexpr unsigned FULL_MASK = 0xffffffffu;
 int set_error(int status, const char* fmt, ...);
 std::atomic<uint64_t>& launch_counter();
 int gemm_tc_error_count(int* out);  // tensor-core GEMM wait limits hit
+int skinny_error_count(int* out);   // skinny GEMM wait limits hit
 
 #define FML_CUDA_TRY(expr)                                                                     \
     do {                                                                                       \

@@ -170,10 +170,14 @@ int gemm_f32_ta(float* C, const float* A, const float* B, int M, int N, int K, i
     return FML_OK;
 }
 
-static int g_math_mode = FML_MATH_FP32;
+// Batched / prefill contractions on the tensor cores by default: TF32x3 is
+// fp32-level accuracy (fml_set_math_mode selects the fp32 CUDA-core kernels).
+static int g_math_mode = FML_MATH_TF32X3;
 
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
             int epi, const float* R, cudaStream_t st, const float* B_lo = nullptr);
+int gemm_tc_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
+               cudaStream_t st);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 bool skinny_nn_ok(const float* C, const float* A, const float* B, int M, int N, int K, int ldb, int ldc);
 int skinny_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc,
@@ -192,6 +196,16 @@ int gemm_nt(float* C, const float* A, const float* B, int M, int N, int K, int l
     FML_RC(gemm_f32(C, A, B, M, N, K, lda, ldb, ldc, true, 1, 0, 0, 0, st));
     if (epi == 0 || M <= 0 || N <= 0) return FML_OK;
     return set_error(FML_ERR_UNSUPPORTED, "gemm_nt: epilogue %d needs the tensor-core path", epi);
+}
+
+// C = A . B (B [K x N] row-major): tensor cores in the TF32 modes when the
+// operands meet TMA's alignment rules, else the fp32 CUDA-core kernel.
+int gemm_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, cudaStream_t st)
+{
+    const bool tc_ok = g_math_mode != FML_MATH_FP32 && K > 0 && aligned16(A) && aligned16(B) && lda % 4 == 0 &&
+                       ldb % 4 == 0;
+    if (tc_ok) return gemm_tc_nn(C, A, B, M, N, K, lda, ldb, ldc, g_math_mode == FML_MATH_TF32X3, st);
+    return gemm_f32(C, A, B, M, N, K, lda, ldb, ldc, false, 1, 0, 0, 0, st);
 }
 
 }  // namespace fml
@@ -225,7 +239,7 @@ int fml_matmul(float* out, const float* a, const float* b, uint32_t M, uint32_t 
     }
     if (skinny_nn_ok(out, a, b, (int)M, (int)N, (int)K, (int)N, (int)N))
         return skinny_nn(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, st);
-    return gemm_f32(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, false, 1, 0, 0, 0, st);
+    return gemm_nn(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, st);
 }
 
 int fml_matmul_strided(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K, uint32_t lda,
@@ -234,8 +248,24 @@ int fml_matmul_strided(float* out, const float* a, const float* b, uint32_t M, u
 {
     FML_REQUIRE(M == 0 || N == 0 || (out && a && b), "fml_matmul_strided: null pointer");
     FML_REQUIRE(batch >= 1, "fml_matmul_strided: batch must be >= 1");
+    cudaStream_t st = as_stream(stream);
+    // the per-head contractions of CausalSelfAttentionLayer.h:445-497 (scores
+    // Q_h K_h^T and P V_h over row-strided head views): tensor cores in the
+    // TF32 modes above 64 rows, one launch per plane
+    if (g_math_mode != FML_MATH_FP32 && M > 64 && K > 0)
+    {
+        for (uint32_t z = 0; z < batch; ++z)
+        {
+            float* c = out + z * plane_c;
+            const float* pa = a + z * plane_a;
+            const float* pb = b + z * plane_b;
+            if (trans_b) FML_RC(gemm_nt(c, pa, pb, (int)M, (int)N, (int)K, (int)lda, (int)ldb, (int)ldc, 0, nullptr, st));
+            else FML_RC(gemm_nn(c, pa, pb, (int)M, (int)N, (int)K, (int)lda, (int)ldb, (int)ldc, st));
+        }
+        return FML_OK;
+    }
     return gemm_f32(out, a, b, (int)M, (int)N, (int)K, (int)lda, (int)ldb, (int)ldc, trans_b != 0, (int)batch, plane_a,
-                    plane_b, plane_c, as_stream(stream));
+                    plane_b, plane_c, st);
 }
 
 }  // extern "C"

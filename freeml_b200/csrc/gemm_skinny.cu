@@ -1,165 +1,255 @@
 // Skinny contractions (M <= 64 rows): Mul<None> (MatrixBase_Mul.h:591-615)
 // with B [K x N] row-major, the Dense forward of a batch of at most 64 rows
-// (the drop-in's decode-time Dense and BASELINE config 2's Dense sweep).
+// (the drop-in's small-batch Dense and BASELINE config 2's Dense sweep).
 //
-// The 128 x 128-tile GEMM leaves most of the GPU idle at such shapes (N/128
-// CTAs), so this kernel splits K over grid.z instead: a CTA of 64 threads owns
-// 256 consecutive columns (one float4 of B per thread per k: a warp reads
-// 512 contiguous bytes of a B row, 8 rows in flight per thread) and MT rows,
-// stages its rows of A in shared memory 128 k at a time (every lane reads the
-// same A element: a broadcast), and accumulates in fp32 over its k range in
-// ascending order.  With more than one split the partial results go to a
-// stream-ordered scratch buffer and a second kernel sums them in split order,
-// so the result is deterministic.  Every B element is read from DRAM once per
-// row tile.  (A cluster-of-splits variant reducing through distributed shared
-// memory was measured slower: at most 8-16 splits per column block leave too
-// few bytes in flight for narrow outputs.)
+// One launch, no scratch memory.  The 128-column blocks of the output are
+// too few to fill the GPU at these shapes, so K is split over S CTAs (S = 1,
+// 2, 4, 8 or 16) that form one thread-block cluster per column block:
+//   * each CTA streams its K slice in chunks of KC rows through two
+//     shared-memory buffers: the chunk's B rows (128 columns, 512 bytes each)
+//     and A rows (KC floats each) arrive by bulk asynchronous copies
+//     (cp.async.bulk, completing on an mbarrier), the next chunk's copies in
+//     flight while the current chunk is multiplied;
+//   * warp w accumulates rows m = w, w + 4, ... (at most 16) of the block in
+//     fp32, lane l four consecutive columns (one float4 of each B row);
+//   * the CTA's partial [M x 128] is split by columns over the cluster: CTA
+//     o owns columns [o 128/S, (o+1) 128/S); every CTA stores its part of
+//     each owner's columns into the owner's receive buffer (distributed
+//     shared memory, slot = its rank), one cluster barrier, and each owner
+//     sums the S partials in rank order from its own shared memory
+//     (deterministic) and writes C.
+// Every B element is read from DRAM once.  Every mbarrier wait is bounded
+// (an expiry is counted in the device error count and the CTA winds down);
+// the cluster barriers are reached by every thread on every path.
 #include <algorithm>
 
-#include "fml_common.cuh"
+#include <cooperative_groups.h>
+
+#include "tcgen05.cuh"
 
 namespace fml {
 
-constexpr int SKN_THREADS = 64, SKN_COLS = SKN_THREADS * 4, SKN_K = 128;
+__device__ int g_skinny_timeouts;
 
-template <int MT>
-__global__ void __launch_bounds__(SKN_THREADS) skinny_nn_kernel(const float* __restrict__ A,
-                                                                 const float* __restrict__ B, float* __restrict__ out,
-                                                                 int M, int N, int K, int lda, int ldb, int ldo,
-                                                                 int kper, uint64_t plane)
+namespace {
+
+constexpr int SK_THREADS = 128, SK_COLS = 128, SK_KC = 64;
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 {
-    __shared__ float xs[MT][SKN_K];
-    const int tid = threadIdx.x;
-    const int n = (blockIdx.x * SKN_THREADS + tid) * 4;
-    const int m0 = blockIdx.y * MT;
-    const int k0 = blockIdx.z * kper;
-    const int k1 = min(K, k0 + kper);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+                 : "memory");
+}
+
+struct SkinnyArgs
+{
+    const float* A;  // [M x K], row stride lda
+    const float* B;  // [K x N], row stride ldb
+    float* C;        // [M x N], row stride ldc
+    int M, N, K, lda, ldb, ldc;
+    int kper;        // K rows per split (a multiple of 4)
+};
+
+// MT: rows per warp (M <= 4 MT)
+template <int MT>
+__global__ void __launch_bounds__(SK_THREADS, 1) skinny_nn_kernel(SkinnyArgs a)
+{
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int M = a.M;
+    const uint32_t S = gridDim.y;      // K splits = CTAs of the cluster
+    const uint32_t s = blockIdx.y;     // this CTA's split = its cluster rank
+    const int n0 = blockIdx.x * SK_COLS;
+    const int ncols = min(SK_COLS, a.N - n0);  // a multiple of 4
+    const int k0 = (int)s * a.kper;
+    const int kend = min(a.K, k0 + a.kper);
+    const int nchunks = kend > k0 ? (kend - k0 + SK_KC - 1) / SK_KC : 0;
+
+    // shared memory: 2 x {B chunk [KC x 128], A chunk [M x KC]}, receive
+    // buffer [S][M][128/S], two mbarriers
+    float* bbuf = reinterpret_cast<float*>(smem_raw);                 // 2 x KC x 128
+    float* abuf = bbuf + 2 * SK_KC * SK_COLS;                         // 2 x M x KC
+    float* recv = abuf + 2 * M * SK_KC;                               // M x 128
+    uint64_t* full = reinterpret_cast<uint64_t*>(recv + M * SK_COLS);  // [2]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    cg::cluster_group cluster = cg::this_cluster();
+    cg::cluster_group::arrival_token started = cluster.barrier_arrive();
+    if (tid == 0)
+    {
+        tc::mbar_init(&full[0], 1);
+        tc::mbar_init(&full[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    // warp 0 issues chunk c into buffer b: its B rows (ncols floats each) and
+    // A rows (the chunk's kc floats of each of the M rows)
+    auto issue = [&](int c, int b) {
+        const int kb = k0 + c * SK_KC, kc = min(SK_KC, kend - kb);
+        if (lane == 0)
+            tc::mbar_arrive_expect_tx(&full[b], (uint32_t)(kc * ncols + M * kc) * 4u);
+        __syncwarp();
+        for (int r = lane; r < kc; r += 32)
+            bulk_g2s(bbuf + (b * SK_KC + r) * SK_COLS, a.B + (uint64_t)(kb + r) * a.ldb + n0, ncols * 4u, &full[b]);
+        for (int m = lane; m < M; m += 32)
+            bulk_g2s(abuf + (b * M + m) * SK_KC, a.A + (uint64_t)m * a.lda + kb, kc * 4u, &full[b]);
+    };
+    if (warp == 0)
+    {
+        if (nchunks > 0) issue(0, 0);
+        if (nchunks > 1) issue(1, 1);
+    }
+
     float4 acc[MT];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int kc = k0; kc < k1; kc += SKN_K)
+    for (int i = 0; i < MT; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int c4 = 4 * lane;  // this lane's columns within the block
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c)
     {
-        const int kn = min(SKN_K, k1 - kc);
-        __syncthreads();
-        for (int i = tid; i < MT * SKN_K; i += SKN_THREADS)
+        const int b = c & 1;
+        ok = tc::mbar_wait(&full[b], (uint32_t)(c >> 1) & 1u) && ok;
+        const int kc = min(SK_KC, kend - (k0 + c * SK_KC));
+        if (ok && c4 < ncols)
         {
-            const int m = i / SKN_K, kk = i - m * SKN_K;
-            xs[m][kk] = (m0 + m < M && kk < kn) ? A[(uint64_t)(m0 + m) * lda + kc + kk] : 0.f;
-        }
-        __syncthreads();
-        if (n < N)
-        {
-            const float* bp = B + (uint64_t)kc * ldb + n;
-#pragma unroll 8
-            for (int kk = 0; kk < kn; ++kk)
+            const float* bb = bbuf + b * SK_KC * SK_COLS + c4;
+            const float* ab = abuf + b * M * SK_KC;
+            for (int k = 0; k < kc; ++k)
             {
-                const float4 w = __ldg(reinterpret_cast<const float4*>(bp + (uint64_t)kk * ldb));
+                const float4 w = *reinterpret_cast<const float4*>(bb + k * SK_COLS);
 #pragma unroll
-                for (int m = 0; m < MT; ++m)
+                for (int i = 0; i < MT; ++i)
                 {
-                    const float x = xs[m][kk];
-                    acc[m].x = fmaf(x, w.x, acc[m].x);
-                    acc[m].y = fmaf(x, w.y, acc[m].y);
-                    acc[m].z = fmaf(x, w.z, acc[m].z);
-                    acc[m].w = fmaf(x, w.w, acc[m].w);
+                    const int m = warp + 4 * i;
+                    if (m < M)
+                    {
+                        const float x = ab[m * SK_KC + k];
+                        acc[i].x = fmaf(x, w.x, acc[i].x);
+                        acc[i].y = fmaf(x, w.y, acc[i].y);
+                        acc[i].z = fmaf(x, w.z, acc[i].z);
+                        acc[i].w = fmaf(x, w.w, acc[i].w);
+                    }
                 }
             }
         }
+        // every thread is done with buffer b; `ok` made uniform so that a
+        // warp never splits around the issue's warp-synchronous steps
+        ok = __syncthreads_and(ok) != 0;
+        if (warp == 0 && c + 2 < nchunks && ok) issue(c + 2, b);
     }
-    if (n >= N) return;
-    float* o = out + blockIdx.z * plane;
+    ok = __syncthreads_and(ok) != 0;
+
+    // columns [o W, (o+1) W) of the block belong to CTA o
+    const int W = SK_COLS / (int)S;
+    cluster.barrier_wait(std::move(started));  // every CTA of the cluster is running
+    if (ok)
+    {
+        const int o = c4 / W, j = c4 % W;
+        float* dst = cluster.map_shared_rank(recv, o);
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-        if (m0 + m < M) *reinterpret_cast<float4*>(o + (uint64_t)(m0 + m) * ldo + n) = acc[m];
+        for (int i = 0; i < MT; ++i)
+        {
+            const int m = warp + 4 * i;
+            if (m < M) *reinterpret_cast<float4*>(dst + ((int)s * M + m) * W + j) = acc[i];
+        }
+    }
+    cluster.sync();  // every partial is in its owner's receive buffer
+    if (ok)
+    {
+        const int q = W / 4;  // float4 columns per row of this CTA's share
+        for (int t = tid; t < M * q; t += SK_THREADS)
+        {
+            const int m = t / q, j = 4 * (t % q), n = n0 + (int)s * W + j;
+            if (n >= a.N) continue;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (uint32_t r = 0; r < S; ++r)
+            {
+                const float4 u = *reinterpret_cast<const float4*>(recv + (r * M + m) * W + j);
+                v.x += u.x;
+                v.y += u.y;
+                v.z += u.z;
+                v.w += u.w;
+            }
+            *reinterpret_cast<float4*>(a.C + (uint64_t)m * a.ldc + n) = v;
+        }
+    }
+    if (!ok && tid == 0) atomicAdd(&g_skinny_timeouts, 1);
 }
 
-// C[m, n] = sum over splits s (in order) of part[s][m][n]
-__global__ void split_sum_kernel(float* __restrict__ C, const float* __restrict__ part, int M, int N, int ldc, int S)
+size_t skinny_smem(int M) { return (size_t)(2 * SK_KC * SK_COLS + 2 * M * SK_KC + M * SK_COLS) * 4 + 64; }
+
+template <int MT>
+int launch_skinny(const SkinnyArgs& a, int S, cudaStream_t st)
 {
-    const uint64_t n4 = (uint64_t)N / 4, total = (uint64_t)M * n4;
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x)
+    auto kern = skinny_nn_kernel<MT>;
+    static uint64_t attr_devices = 0;
+    int dev = 0;
+    FML_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
+    if (!bit || !(attr_devices & bit))
     {
-        const uint64_t m = i / n4, c = (i - m * n4) * 4;
-        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int z = 0; z < S; ++z)
-        {
-            const float4 v = *reinterpret_cast<const float4*>(part + ((uint64_t)z * M + m) * N + c);
-            s.x += v.x;
-            s.y += v.y;
-            s.z += v.z;
-            s.w += v.w;
-        }
-        *reinterpret_cast<float4*>(C + m * ldc + c) = s;
+        FML_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)skinny_smem(64)));
+        FML_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                          cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        attr_devices |= bit;
     }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.N + SK_COLS - 1) / SK_COLS, S);
+    cfg.blockDim = dim3(SK_THREADS);
+    cfg.dynamicSmemBytes = skinny_smem(a.M);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "skinny_nn launch: %s", cudaGetErrorString(e));
+    FML_LAUNCH_CHECK();
+    return FML_OK;
 }
+
+}  // namespace
 
 bool skinny_nn_ok(const float* C, const float* A, const float* B, int M, int N, int K, int ldb, int ldc)
 {
-    return M > 0 && M <= 64 && N > 0 && K > 0 && N % 4 == 0 && ldb % 4 == 0 && ldc % 4 == 0 &&
-           (reinterpret_cast<uintptr_t>(B) & 15) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
-}
-
-template <int MT>
-int launch_skinny(float* out, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldo,
-                  int S, int kper, uint64_t plane, cudaStream_t st)
-{
-    dim3 grid((N + SKN_COLS - 1) / SKN_COLS, (M + MT - 1) / MT, S);
-    skinny_nn_kernel<MT><<<grid, SKN_THREADS, 0, st>>>(A, B, out, M, N, K, lda, ldb, ldo, kper, plane);
-    FML_LAUNCH_CHECK();
-    return FML_OK;
+    // bulk copies need 16-byte aligned rows: A, B, C and their row strides
+    return M > 0 && M <= 64 && N > 0 && K > 0 && N % 4 == 0 && K % 4 == 0 && ldb % 4 == 0 && ldc % 4 == 0 &&
+           aligned16(A) && aligned16(B) && aligned16(C);
 }
 
 int skinny_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc,
               cudaStream_t st)
 {
-    static uint64_t pool_devices = 0;  // bit d: device d's pool is set up
+    FML_REQUIRE(lda % 4 == 0, "skinny_nn: lda must be a multiple of 4");
     int dev = 0, sms = 0;
     FML_CUDA_TRY(cudaGetDevice(&dev));
     FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const uint64_t bit = dev >= 0 && dev < 64 ? 1ull << dev : 0ull;
-    if (!(pool_devices & bit) || !bit)
-    {
-        // the split partials come from this device's stream-ordered pool;
-        // keep freed blocks cached in this process (default threshold 0
-        // would hand them back to the driver at every synchronisation)
-        cudaMemPool_t pool;
-        FML_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, dev));
-        uint64_t keep = ~0ull;
-        FML_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
-        pool_devices |= bit;
-    }
-    const int MT = M <= 4 ? 4 : (M <= 8 ? 8 : 16);
-    const int base = ((N + SKN_COLS - 1) / SKN_COLS) * ((M + MT - 1) / MT);
-    // about eight CTAs per SM, at least 32 k per split, partials <= 64 MB
-    int S = (8 * sms + base - 1) / base;
-    S = std::min(S, (K + 31) / 32);
-    S = std::min(S, std::max(1, (int)((64ull << 20) / (4ull * M * N))));
-    S = std::max(S, 1);
-    const int kper = (K + S - 1) / S;
-    S = (K + kper - 1) / kper;
-    float* part = nullptr;
-    float* out = C;
-    int ldo = ldc;
-    if (S > 1)
-    {
-        FML_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&part), (size_t)S * M * N * sizeof(float), st));
-        out = part;
-        ldo = N;
-    }
-    const uint64_t plane = (uint64_t)M * N;
-    int rc;
-    if (MT == 4) rc = launch_skinny<4>(out, A, B, M, N, K, lda, ldb, ldo, S, kper, plane, st);
-    else if (MT == 8) rc = launch_skinny<8>(out, A, B, M, N, K, lda, ldb, ldo, S, kper, plane, st);
-    else rc = launch_skinny<16>(out, A, B, M, N, K, lda, ldb, ldo, S, kper, plane, st);
-    if (rc == FML_OK && S > 1)
-    {
-        const uint64_t total = (uint64_t)M * N / 4;
-        split_sum_kernel<<<(unsigned)std::min<uint64_t>((total + 255) / 256, 4096), 256, 0, st>>>(C, part, M, N, ldc,
-                                                                                                  S);
-        FML_LAUNCH_CHECK();
-    }
-    if (part) FML_CUDA_TRY(cudaFreeAsync(part, st));
-    return rc;
+    const int blocks = (N + SK_COLS - 1) / SK_COLS;
+    // splits: about two CTAs per SM, at least one 64-row chunk each, a power
+    // of two up to 16 (the owners' column shares stay float4 multiples)
+    int S = 1;
+    while (S < 16 && blocks * S * 2 <= 2 * sms && (K + 2 * S - 1) / (2 * S) >= SK_KC) S *= 2;
+    int kper = (K + S - 1) / S;
+    kper = (kper + 3) & ~3;  // chunk starts stay 16-byte aligned
+    SkinnyArgs a{A, B, C, M, N, K, lda, ldb, ldc, kper};
+    if (M <= 4) return launch_skinny<1>(a, S, st);
+    if (M <= 8) return launch_skinny<2>(a, S, st);
+    if (M <= 16) return launch_skinny<4>(a, S, st);
+    if (M <= 32) return launch_skinny<8>(a, S, st);
+    return launch_skinny<16>(a, S, st);
+}
+
+int skinny_error_count(int* out)
+{
+    FML_CUDA_TRY(cudaMemcpyFromSymbol(out, g_skinny_timeouts, sizeof(int)));
+    return FML_OK;
 }
 
 }  // namespace fml

@@ -3,6 +3,7 @@
 // large-M shapes.
 //
 //   C[M x N] (+ epilogue) = A[M x K] . B[N x K]^T        (both K-contiguous)
+//   C[M x N]                = A[M x K] . B[K x N]          (BMN: B row-major)
 //
 // 128 x 128 output tiles, K staged 32 fp32 (one 128-byte row) at a time
 // through a 3-stage ring of TMA tensor loads (128-byte swizzle, each load into
@@ -42,10 +43,26 @@ constexpr int STAGES = 3;
 constexpr uint32_t TILE_BYTES = BM * BK * 4;  // 16 KB (A or B tile)
 constexpr uint32_t TMEM_COLS = 128;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+constexpr uint32_t IDESC_BMN = IDESC | (1u << 16);  // B read MN-major (bit 16: "transpose B")
+constexpr uint32_t MN_BOX = 32;                      // n per 128-byte swizzle row of an MN-major B tile
 
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, bool accumulate)
 {
     mma_tf32(tmem_d, da, db, IDESC, accumulate);
+}
+
+// MN-major, 128-byte-swizzled B operand of one K = 8 step: the tile holds
+// BN / 32 boxes of [32 k rows x 32 n] (4 KB each, n contiguous in 128-byte
+// rows, the rows swizzled in 8-row / 1 KB atoms, as a 32 x 32 TMA box with
+// 128-byte swizzle lands them).  The canonical MN-major layout: 32 elements
+// of n per swizzle row, the next 32 n one box (LBO = 4 KB) on, the next 8
+// k one atom (SBO = 1 KB) on; k step kk starts at atom kk.
+__device__ __forceinline__ uint64_t smem_desc_mn(const void* tile, uint32_t kk)
+{
+    const uint64_t start = (uint64_t)((smem_u32(tile) + kk * 1024u) >> 4) & 0x3FFFull;
+    const uint64_t lbo = (MN_BOX * BK * 4u) >> 4;  // next 32 n: the next box
+    const uint64_t sbo = 1024ull >> 4;             // next 8 k: the next atom
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | (2ull << 61);
 }
 
 }  // namespace tc
@@ -78,7 +95,9 @@ struct TcArgs
 //   warps 6..9  epilogue: tcgen05.ld of a finished accumulator, store
 // Barriers: full / conv / empty per stage (TMA landed / split done / MMAs have
 // read it), acc_full / acc_empty per accumulator (MMAs done / drained).
-template <bool SPLIT3, int EPI, bool BLO = false>
+// BMN: B is [K x N] row-major (Mul<None>, MatMul_Strided<None>): each stage
+// loads it as BN / 32 boxes of 32 k x 32 n and the MMA reads it MN-major.
+template <bool SPLIT3, int EPI, bool BLO = false, bool BMN = false>
 __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a,
                                                                          const __grid_constant__ CUtensorMap map_b,
                                                                          const __grid_constant__ CUtensorMap map_blo,
@@ -147,7 +166,15 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
                     if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], (BLO ? 3 : 2) * TILE_BYTES);
                     tma_load_2d(tile_ptr(s, 0), &map_a, kb * BK, m0, &full[s]);
-                    tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
+                    if constexpr (BMN)
+                    {
+#pragma unroll
+                        for (int j = 0; j < BN / (int)MN_BOX; ++j)
+                            tma_load_2d(tile_ptr(s, 1) + j * (MN_BOX * BK * 4), &map_b, n0 + j * (int)MN_BOX,
+                                        kb * BK, &full[s]);
+                    }
+                    else
+                        tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
                     if constexpr (BLO) tma_load_2d(tile_ptr(s, 3), &map_blo, kb * BK, n0, &full[s]);
                 }
             }
@@ -178,12 +205,25 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
                     {
                         const uint32_t off = k * 32;
                         const uint64_t da = smem_desc(tile_ptr(s, 0), off);
-                        const uint64_t db = smem_desc(tile_ptr(s, 1), off);
-                        mma_tf32(acc_tmem, da, db, kb > 0 || k > 0);
-                        if constexpr (SPLIT3)
+                        if constexpr (BMN)
                         {
-                            mma_tf32(acc_tmem, da, smem_desc(tile_ptr(s, 3), off), true);  // hi * lo
-                            mma_tf32(acc_tmem, smem_desc(tile_ptr(s, 2), off), db, true);  // lo * hi
+                            const uint64_t db = smem_desc_mn(tile_ptr(s, 1), k);
+                            tc::mma_tf32(acc_tmem, da, db, IDESC_BMN, kb > 0 || k > 0);
+                            if constexpr (SPLIT3)
+                            {
+                                tc::mma_tf32(acc_tmem, da, smem_desc_mn(tile_ptr(s, 3), k), IDESC_BMN, true);
+                                tc::mma_tf32(acc_tmem, smem_desc(tile_ptr(s, 2), off), db, IDESC_BMN, true);
+                            }
+                        }
+                        else
+                        {
+                            const uint64_t db = smem_desc(tile_ptr(s, 1), off);
+                            mma_tf32(acc_tmem, da, db, kb > 0 || k > 0);
+                            if constexpr (SPLIT3)
+                            {
+                                mma_tf32(acc_tmem, da, smem_desc(tile_ptr(s, 3), off), true);  // hi * lo
+                                mma_tf32(acc_tmem, smem_desc(tile_ptr(s, 2), off), db, true);  // lo * hi
+                            }
                         }
                     }
                     mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
@@ -286,20 +326,20 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
 
 // ---- host side ---------------------------------------------------------------
 
-template <bool SPLIT3, int EPI, bool BLO = false>
+template <bool SPLIT3, int EPI, bool BLO = false, bool BMN = false>
 static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo, const TcArgs& args,
                      cudaStream_t st)
 {
     constexpr int NT = SPLIT3 ? 4 : 2;
     const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 32 * 8;
     static uint64_t attr_devices = 0;
-    FML_RC(smem_limit_once(reinterpret_cast<const void*>(gemm_tcgen05_kernel<SPLIT3, EPI, BLO>), (int)smem,
+    FML_RC(smem_limit_once(reinterpret_cast<const void*>(gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN>), (int)smem,
                            attr_devices));
     int dev = 0, sms = 0;
     FML_CUDA_TRY(cudaGetDevice(&dev));
     FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int ntiles = ((args.N + tc::BN - 1) / tc::BN) * ((args.M + tc::BM - 1) / tc::BM);
-    gemm_tcgen05_kernel<SPLIT3, EPI, BLO><<<std::min(ntiles, sms), 320, smem, st>>>(ma, mb, mblo, args);
+    gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN><<<std::min(ntiles, sms), 320, smem, st>>>(ma, mb, mblo, args);
     FML_LAUNCH_CHECK();
     return FML_OK;
 }
@@ -337,6 +377,26 @@ int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int l
     if (epi == TC_GELU) return launch_tc<false, TC_GELU>(ma, mb, mblo, args, st);
     if (epi == TC_RESID) return launch_tc<false, TC_RESID>(ma, mb, mblo, args, st);
     return launch_tc<false, TC_STORE>(ma, mb, mblo, args, st);
+}
+
+// C = A . B on the tensor cores with B [K x N] row-major (row stride ldb):
+// Mul<None> and MatMul_Strided<None>.  B is staged MN-major (no transpose);
+// the same alignment rules as gemm_tc (ldb a multiple of 4, B 16-byte
+// aligned).
+int gemm_tc_nn(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
+               cudaStream_t st)
+{
+    if (M <= 0 || N <= 0) return FML_OK;
+    FML_REQUIRE(K > 0, "gemm_tc_nn: K must be positive");
+    FML_REQUIRE(aligned16(A) && aligned16(B) && lda % 4 == 0 && ldb % 4 == 0,
+                "gemm_tc_nn: operands must be 16-byte aligned with row strides that are multiples of 4");
+    CUtensorMap ma, mb;
+    FML_RC(tc::make_map(&ma, A, M, K, lda, tc::BM));
+    // B [K x N]: n is the contiguous (inner) dimension, 32 x 32 boxes
+    FML_RC(tc::make_map(&mb, B, K, N, ldb, (int)tc::MN_BOX));
+    TcArgs args{M, N, K, C, ldc, nullptr};
+    if (split3) return launch_tc<true, TC_STORE, false, true>(ma, mb, mb, args, st);
+    return launch_tc<false, TC_STORE, false, true>(ma, mb, mb, args, st);
 }
 
 // lo = x - hi(x) (hi = x with the low 13 mantissa bits cleared), for B_lo.

@@ -376,6 +376,14 @@ int main(int argc, char** argv)
         if (std::string(argv[i]).rfind("--", 0) == 0) a.kv[std::string(argv[i]).substr(2)] = argv[i + 1];
     Shape s{a.u("vocab", 256), a.u("ctx", 128), a.u("d", 128), a.u("heads", 4), a.u("layers", 4), a.u("wseed", 0)};
     const std::string mode = argv[1];
+    // --math fp32|tf32x3|tf32: precision of the batched contractions (Mul,
+    // MatMul_Strided above 64 rows); the library's default is tf32x3
+    if (a.has("math"))
+    {
+        const std::string m = a.get("math");
+        const int mm = m == "fp32" ? FML_MATH_FP32 : m == "tf32" ? FML_MATH_TF32 : FML_MATH_TF32X3;
+        if (fml_set_math_mode(mm) != FML_OK) { std::fprintf(stderr, "%s\n", fml_last_error()); return 2; }
+    }
     if (mode == "greedy") return Greedy(s, a);
     if (mode == "engine") return Engine(s, a);
     if (mode == "weights") return DumpWeights(s, a);

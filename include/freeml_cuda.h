@@ -26,11 +26,9 @@
  *  - matrices are row-major fp32, FreeML's Dims3D{x = cols, y = rows};
  *  - `stream` is a cudaStream_t (NULL = the legacy default stream);
  *  - allocation (fml_device_alloc aside, the allocator that MatrixCUDA
- *    uses): operator entry points allocate nothing, except
- *    fml_matmul with trans_b == 0 at <= 64 rows, whose split-K partials
- *    come from the device's stream-ordered pool (cudaMallocAsync, freed on
- *    the same stream), and fml_attention_decode, which takes a caller
- *    workspace (fml_attention_decode_noalloc needs none); the engine
+ *    uses): operator entry points allocate nothing (fml_attention_decode
+ *    takes a caller workspace; fml_attention_decode_noalloc needs none);
+ *    the engine
  *    allocates in fml_lm_create, fml_lm_bind_weights / fml_lm_bind_packed
  *    (a transient staging buffer), fml_lm_set_tensor_parallel /
  *    fml_lm_tp_connect, and at its first TF32x3 prefill after a bind (the
@@ -159,13 +157,19 @@ FML_API int fml_split_qkv(float* q, float* k, float* v, const float* packed, uin
 /* Mul<Mode>(out, L, R)  MatrixBase_Mul.h:591-615 for Mode in {None, Right}:
  *   trans_b == 0: out[M x N] = L[M x K] . R[K x N]
  *   trans_b == 1: out[M x N] = L[M x K] . R[N x K]^T
- * Precision follows fml_set_math_mode(). */
+ * Above 64 rows: tcgen05 tensor cores in the TF32 math modes (R read in its
+ * stored layout, K-major for Right, N-major for None), the fp32 CUDA-core
+ * kernel in FML_MATH_FP32.  At most 64 rows: memory-bound fp32 CUDA-core
+ * kernels in every mode.  Precision follows fml_set_math_mode(). */
 FML_API int fml_matmul(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K,
                int trans_b, fml_stream_t stream);
 
 /* MatMul_Strided<Mode>(out, L, R, Lrs, 1, Rrs, 1, Ors, 1)  MatrixBase_Mul.h:617-722
  * (column strides of 1, the form CausalSelfAttentionLayer.h:445-497 uses),
- * for `batch` planes spaced by the plane strides (elements). */
+ * for `batch` planes spaced by the plane strides (elements).  Above 64 rows
+ * in the TF32 math modes: tcgen05 tensor cores, one launch per plane (the
+ * row strides and plane offsets must keep every row 16-byte aligned, else
+ * the CUDA-core kernel runs). */
 FML_API int fml_matmul_strided(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K,
                        uint32_t lda, uint32_t ldb, uint32_t ldc, int trans_b, uint32_t batch,
                        uint64_t plane_a, uint64_t plane_b, uint64_t plane_c, fml_stream_t stream);
@@ -255,11 +259,13 @@ FML_API int fml_attention_decode_noalloc(float* out, const float* q, const float
                                          const uint32_t* lens, uint32_t batch, uint32_t heads, uint32_t head_dim,
                                          uint32_t context, float scale, fml_stream_t stream);
 
-/* Precision of fml_matmul / the engine's prefill contractions:
- *   FML_MATH_FP32  -- fp32 FFMA on the CUDA cores (default; the logits bound
- *                     of 1e-3 abs/rel against the reference holds);
+/* Precision of fml_matmul / fml_matmul_strided (the drop-in's Mul and
+ * MatMul_Strided) above 64 rows:
+ *   FML_MATH_FP32  -- fp32 FFMA on the CUDA cores;
  *   FML_MATH_TF32X3 -- tcgen05 tensor cores, each fp32 operand split into a
- *                     TF32 pair and three products accumulated in fp32;
+ *                     TF32 pair and three products accumulated in fp32
+ *                     (default: fp32-level accuracy, the logits bound of
+ *                     1e-3 abs/rel against the reference holds);
  *   FML_MATH_TF32  -- tcgen05 tensor cores, one TF32 product (looser bound). */
 enum fml_math_mode { FML_MATH_FP32 = 0, FML_MATH_TF32X3 = 1, FML_MATH_TF32 = 2 };
 FML_API int fml_set_math_mode(int mode);

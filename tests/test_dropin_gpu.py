@@ -54,25 +54,30 @@ def test_dropin_weights_are_the_reference_weights(golden, dropin, name):
     assert hashlib.sha256(w.tobytes()).hexdigest() == m["weights_sha256"]
 
 
-def _greedy(dropin, g, m, name, graph):
+def _greedy(dropin, g, m, name, graph, math="tf32x3"):
     with tempfile.TemporaryDirectory() as td:
         pf, tf, lf = (os.path.join(td, n) for n in ("p.bin", "t.bin", "l.bin"))
         g[f"{name}_prompt"].astype(np.uint32).tofile(pf)
         p = subprocess.run([dropin, "greedy", *_args(m), "--prompt", pf, "--plen", str(m["plen"]),
-                            "--new", str(m["new"]), "--out-tokens", tf, "--out-logits", lf, "--graph", str(graph)],
+                            "--new", str(m["new"]), "--out-tokens", tf, "--out-logits", lf, "--graph", str(graph),
+                            "--math", math],
                            check=True, capture_output=True, text=True, timeout=600)
         stats = json.loads(p.stdout.strip().splitlines()[-1])
         return np.fromfile(tf, np.uint32), np.fromfile(lf, np.float32).reshape(m["new"], m["V"]), stats
 
 
+@pytest.mark.parametrize("math", ["tf32x3", "fp32"])
 @pytest.mark.parametrize("graph", [0, 1], ids=["eager", "launch_plan"])
 @pytest.mark.parametrize("name", ["cfg1", "odd"])
-def test_dropin_model_run_greedy_matches_reference(golden, dropin, name, graph):
+def test_dropin_model_run_greedy_matches_reference(golden, dropin, name, graph, math):
     """Model::Run per token, either dispatching every operator (eager) or
-    replaying the Run recorded once as a CUDA graph (launch plan)."""
+    replaying the Run recorded once as a CUDA graph (launch plan); the Dense
+    and attention contractions (Mul<None>, Mul<Right>, MatMul_Strided over
+    the 128-row window) on the tcgen05 tensor cores in TF32x3 (the default)
+    and on the CUDA cores in fp32."""
     meta, g, _ = golden
     m = meta["greedy"][name]
-    toks, logits, stats = _greedy(dropin, g, m, name, graph)
+    toks, logits, stats = _greedy(dropin, g, m, name, graph, math)
     np.testing.assert_array_equal(toks, g[f"{name}_tokens"])
     np.testing.assert_allclose(logits, g[f"{name}_logits"], rtol=1e-3, atol=1e-3)
     assert stats["host_transfers_in_run"] == 0, stats

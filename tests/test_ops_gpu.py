@@ -243,12 +243,13 @@ def test_matmul_tensor_core_tf32x3_vs_oracle(M, N, K):
     A = rs.randn(M, K).astype(np.float32)
     B = (0.02 * rs.randn(N, K)).astype(np.float32)
     out = torch.empty(M, N, device="cuda")
+    prev = _lib.load().fml_get_math_mode()
     _lib.call("fml_set_math_mode", _lib.FML_MATH_TF32X3)
     try:
         F.Mul(out, cu(A), cu(B), F.RIGHT)
         got = host(out)
     finally:
-        _lib.call("fml_set_math_mode", _lib.FML_MATH_FP32)
+        _lib.call("fml_set_math_mode", prev)
     ref = O.op_mul(A, B, 1)
     gemm_close(got, ref, A, B.T)
     n = ctypes_u64()
@@ -266,12 +267,13 @@ def test_matmul_tensor_core_tf32_vs_oracle(M, N, K):
     A = rs.randn(M, K).astype(np.float32)
     B = (0.02 * rs.randn(N, K)).astype(np.float32)
     out = torch.empty(M, N, device="cuda")
+    prev = _lib.load().fml_get_math_mode()
     _lib.call("fml_set_math_mode", _lib.FML_MATH_TF32)
     try:
         F.Mul(out, cu(A), cu(B), F.RIGHT)
         got = host(out)
     finally:
-        _lib.call("fml_set_math_mode", _lib.FML_MATH_FP32)
+        _lib.call("fml_set_math_mode", prev)
     ref = O.op_mul(A, B, 1)
     scale = np.abs(A).astype(np.float64) @ np.abs(B.T).astype(np.float64)
     assert np.all(np.abs(got - ref) <= 2e-3 * scale + 1e-6)
@@ -281,3 +283,61 @@ def test_matmul_tensor_core_tf32_vs_oracle(M, N, K):
 def ctypes_u64():
     import ctypes
     return ctypes.c_uint64()
+
+
+@pytest.fixture(params=["tf32x3", "fp32"])
+def math_mode(request):
+    """Run a contraction test in the TF32x3 tensor-core mode (the default)
+    and in the fp32 CUDA-core mode, restoring the previous mode after."""
+    from freeml_b200 import _lib
+    prev = _lib.load().fml_get_math_mode()
+    _lib.call("fml_set_math_mode", {"tf32x3": _lib.FML_MATH_TF32X3, "fp32": _lib.FML_MATH_FP32}[request.param])
+    yield request.param
+    _lib.call("fml_set_math_mode", prev)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (128, 384, 128), (130, 96, 260), (512, 2048, 512),
+                                   (512, 512, 2048), (200, 36, 64), (65, 1000, 96)])
+def test_mul_none_vs_oracle(M, N, K, math_mode):
+    """Mul<None> (Dense.h:207: x [M x K] . W [K x N], W in its stored
+    row-major layout) above 64 rows: on tcgen05 in TF32x3 the weight tile is
+    read N-major straight from that layout; partial 128-column tiles and a K
+    that is not a multiple of the 32-wide stage included."""
+    from freeml_b200 import _lib
+    from freeml_b200 import matrix_ops as F
+    rs = np.random.RandomState(M * 5 + N + K)
+    A = rs.randn(M, K).astype(np.float32)
+    B = (0.02 * rs.randn(K, N)).astype(np.float32)
+    out = torch.empty(M, N, device="cuda")
+    before = _lib.launch_count()
+    F.Mul(out, cu(A), cu(B), F.NONE)
+    assert _lib.launch_count() > before
+    gemm_close(host(out), O.op_mul(A, B, 0), A, B)
+    n = ctypes_u64()
+    _lib.call("fml_device_error_count", ctypes.byref(n))
+    assert n.value == 0
+
+
+@pytest.mark.parametrize("T,d,H", [(128, 128, 4), (512, 512, 8), (96, 64, 2)])
+def test_attention_strided_pieces_vs_oracle(T, d, H, math_mode):
+    """The per-head contractions of CausalSelfAttentionLayer.h:445-497 as the
+    drop-in issues them (MatMul_Strided over head views with row stride d):
+    scores S = Q_h K_h^T and Y_h = P V_h written into column block h of Y;
+    tcgen05 above 64 rows in TF32x3."""
+    from freeml_b200 import matrix_ops as F
+    rs = np.random.RandomState(T + d + H)
+    hd = d // H
+    Q, Kc, V = (rs.randn(T, d).astype(np.float32) for _ in range(3))
+    P = np.abs(rs.randn(T, T)).astype(np.float32)
+    P /= P.sum(axis=1, keepdims=True)
+    Y = torch.zeros(T, d, device="cuda")
+    for h in (0, H - 1):
+        S = torch.zeros(T, T, device="cuda")
+        F.MatMul_Strided(S, cu(Q), cu(Kc), T, T, hd, d, d, T, F.RIGHT, off_a=h * hd, off_b=h * hd)
+        qh, kh, vh = Q[:, h * hd:(h + 1) * hd], Kc[:, h * hd:(h + 1) * hd], V[:, h * hd:(h + 1) * hd]
+        gemm_close(host(S), qh.astype(np.float64) @ kh.T.astype(np.float64), qh, kh.T)
+        F.MatMul_Strided(Y, cu(P), cu(V), T, hd, T, T, d, d, F.NONE, off_b=h * hd, off_c=h * hd)
+        got = host(Y)[:, h * hd:(h + 1) * hd]
+        gemm_close(got, P.astype(np.float64) @ vh.astype(np.float64), P, vh)
+    if H > 2:
+        np.testing.assert_array_equal(host(Y)[:, hd:(H - 1) * hd], 0)  # other heads' columns untouched
