@@ -51,18 +51,22 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t 
     mma_tf32(tmem_d, da, db, IDESC, accumulate);
 }
 
-// MN-major, 128-byte-swizzled B operand of one K = 8 step: the tile holds
-// BN / 32 boxes of [32 k rows x 32 n] (4 KB each, n contiguous in 128-byte
-// rows, the rows swizzled in 8-row / 1 KB atoms, as a 32 x 32 TMA box with
-// 128-byte swizzle lands them).  The canonical MN-major layout: 32 elements
-// of n per swizzle row, the next 32 n one box (LBO = 4 KB) on, the next 8
-// k one atom (SBO = 1 KB) on; k step kk starts at atom kk.
+// MN-major B operand of one K = 8 step.  tf32 accepts only one MN-major
+// shared-memory layout, the 128-byte swizzle with 32-byte atoms (descriptor
+// layout type 1, "128B_BASE32B"): rows of 32 n (128 bytes) whose four 32-byte
+// chunks are permuted by the row index mod 4, in 4-row / 512-byte atoms --
+// what a 32 n x 32 k TMA box with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B lands.
+// (The 16-byte-atom 128-byte swizzle of the K-major operands, with the
+// transpose bit set, made every tf32 MMA produce zeros on B200.)  The tile
+// holds BN / 32 such boxes of [32 k x 32 n] (4 KB each): the next 32 n one box
+// on (LBO = 4 KB), the next 4 k one atom on (SBO = 512 B), so K step kk (8 k)
+// starts 1 KB further.
 __device__ __forceinline__ uint64_t smem_desc_mn(const void* tile, uint32_t kk)
 {
     const uint64_t start = (uint64_t)((smem_u32(tile) + kk * 1024u) >> 4) & 0x3FFFull;
     const uint64_t lbo = (MN_BOX * BK * 4u) >> 4;  // next 32 n: the next box
-    const uint64_t sbo = 1024ull >> 4;             // next 8 k: the next atom
-    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | (2ull << 61);
+    const uint64_t sbo = 512ull >> 4;              // next 4 k: the next atom
+    return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | (1ull << 61);
 }
 
 }  // namespace tc
@@ -392,8 +396,9 @@ int gemm_tc_nn(float* C, const float* A, const float* B, int M, int N, int K, in
                 "gemm_tc_nn: operands must be 16-byte aligned with row strides that are multiples of 4");
     CUtensorMap ma, mb;
     FML_RC(tc::make_map(&ma, A, M, K, lda, tc::BM));
-    // B [K x N]: n is the contiguous (inner) dimension, 32 x 32 boxes
-    FML_RC(tc::make_map(&mb, B, K, N, ldb, (int)tc::MN_BOX));
+    // B [K x N]: n is the contiguous (inner) dimension, 32 x 32 boxes in the
+    // 32-byte-atom swizzle of an MN-major tf32 operand
+    FML_RC(tc::make_map(&mb, B, K, N, ldb, (int)tc::MN_BOX, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
     TcArgs args{M, N, K, C, ldc, nullptr};
     if (split3) return launch_tc<true, TC_STORE, false, true>(ma, mb, mb, args, st);
     return launch_tc<false, TC_STORE, false, true>(ma, mb, mb, args, st);

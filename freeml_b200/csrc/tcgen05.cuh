@@ -162,8 +162,12 @@ inline PFN_cuTensorMapEncodeTiled_v12000 get_encode()
 }
 
 // Row-major [rows x K] fp32 matrix (row stride ld floats) as BK x box_rows
-// boxes with 128-byte swizzle; rows past `rows` and k past K read as zero.
-inline int make_map(CUtensorMap* map, const float* base, int rows, int K, int ld, int box_rows)
+// boxes with 128-byte swizzle (16-byte chunks permuted over 8-row atoms, the
+// K-major operand layout; CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B permutes 32-byte
+// chunks over 4-row atoms, the layout an N-major tf32 operand needs); rows
+// past `rows` and k past K read as zero.
+inline int make_map(CUtensorMap* map, const float* base, int rows, int K, int ld, int box_rows,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B)
 {
     auto enc = get_encode();
     if (!enc) return set_error(FML_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
@@ -172,8 +176,8 @@ inline int make_map(CUtensorMap* map, const float* base, int rows, int K, int ld
     const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(FML_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return FML_OK;
 }
