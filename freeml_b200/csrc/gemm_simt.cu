@@ -230,14 +230,19 @@ int fml_matmul(float* out, const float* a, const float* b, uint32_t M, uint32_t 
     FML_REQUIRE(M == 0 || N == 0 || (out && a && b), "fml_matmul: null pointer");
     FML_REQUIRE(M < (1u << 31) && N < (1u << 31) && K < (1u << 31), "fml_matmul: dimension too large");
     cudaStream_t st = as_stream(stream);
-    // at most 64 rows: the memory-bound kernels (exact fp32 in every math mode)
+    // Few rows: the memory-bound fp32 CUDA-core kernels (every weight byte
+    // read once, no tensor-core tile padding) -- up to 64 rows in the fp32
+    // mode, up to 16 in the TF32 modes, where the tensor cores take over
+    // (measured on B200, Mul<None> 4096 x 4096: 301 us on CUDA cores at 64
+    // rows, CUDA-core FMA throughput bound)
+    const uint32_t small = g_math_mode == FML_MATH_FP32 ? 64u : 16u;
     if (trans_b)
     {
-        if (M >= 1 && M <= 64 && K > 0 && K % 4 == 0 && aligned16(a) && aligned16(b))
+        if (M >= 1 && M <= small && K > 0 && K % 4 == 0 && aligned16(a) && aligned16(b))
             return gemv_nt(out, a, b, M, N, K, st);
         return gemm_nt(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)K, (int)N, 0, nullptr, st);
     }
-    if (skinny_nn_ok(out, a, b, (int)M, (int)N, (int)K, (int)N, (int)N))
+    if (M <= small && skinny_nn_ok(out, a, b, (int)M, (int)N, (int)K, (int)N, (int)N))
         return skinny_nn(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, st);
     return gemm_nn(out, a, b, (int)M, (int)N, (int)K, (int)K, (int)N, (int)N, st);
 }

@@ -157,10 +157,11 @@ FML_API int fml_split_qkv(float* q, float* k, float* v, const float* packed, uin
 /* Mul<Mode>(out, L, R)  MatrixBase_Mul.h:591-615 for Mode in {None, Right}:
  *   trans_b == 0: out[M x N] = L[M x K] . R[K x N]
  *   trans_b == 1: out[M x N] = L[M x K] . R[N x K]^T
- * Above 64 rows: tcgen05 tensor cores in the TF32 math modes (R read in its
- * stored layout, K-major for Right, N-major for None), the fp32 CUDA-core
- * kernel in FML_MATH_FP32.  At most 64 rows: memory-bound fp32 CUDA-core
- * kernels in every mode.  Precision follows fml_set_math_mode(). */
+ * Above 16 rows in the TF32 math modes: tcgen05 tensor cores (R read in its
+ * stored layout, K-major for Right, N-major for None).  At most 16 rows (64
+ * in FML_MATH_FP32): memory-bound fp32 CUDA-core kernels, the small-batch
+ * Mul<None> one launch with no scratch memory.  Otherwise the fp32 CUDA-core
+ * GEMM.  Precision follows fml_set_math_mode(). */
 FML_API int fml_matmul(float* out, const float* a, const float* b, uint32_t M, uint32_t N, uint32_t K,
                int trans_b, fml_stream_t stream);
 
