@@ -485,11 +485,27 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
         const float4* src = reinterpret_cast<const float4*>(a.x + (uint64_t)(in ? m0 + m : 0) * a.ldx);
         float4* row = reinterpret_cast<float4*>(xs + (uint64_t)m * K);
         float sum = 0.f;
-        for (uint32_t c = lane; c < K / 4; c += 32)
+        // the row's loads are all requested before the first is used (at
+        // most 16 float4 per lane, K <= 2048): one L2 round trip, not one per
+        // iteration
         {
-            const float4 v = in ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-            row[c] = v;
-            sum += (v.x + v.y) + (v.z + v.w);
+            float4 v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+            {
+                const uint32_t c = lane + 32u * i;
+                v[i] = in && c < K / 4 ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+            {
+                const uint32_t c = lane + 32u * i;
+                if (c < K / 4)
+                {
+                    row[c] = v[i];
+                    sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+                }
+            }
         }
         if constexpr (LN)
         {
@@ -526,6 +542,16 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
     // the loop runs per team; its trip count is the same for the team's warps
     for (; g < ngroups; g += gstride, parity ^= 1u)
     {
+        // the residual this lane's output adds (EPI_RESID), requested now so
+        // that it arrives during the group's FMAs (the previous kernels that
+        // wrote it finished before griddepcontrol.wait)
+        [[maybe_unused]] float rres = 0.f;
+        if constexpr (EPI == EPI_RESID)
+        {
+            const int ridx = reduce_base<CNT>(lane);
+            const uint32_t rm = m0 + ridx / NW, rn = g * NW + ridx % NW;
+            if (reduce_owner<CNT>(lane) && rm < a.M && rn < a.N) rres = __ldcg(a.r + (uint64_t)rm * a.ldr + rn);
+        }
 #if FML_GEMV_F2
         float2 acc2[CNT];  // even / odd k partial sums, packed fp32 FMA
 #pragma unroll
@@ -604,7 +630,7 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
         }
         else if constexpr (EPI == EPI_RESID)
         {
-            if (valid) a.y[(uint64_t)m * a.ldy + n] = a.r[(uint64_t)m * a.ldr + n] + v;
+            if (valid) a.y[(uint64_t)m * a.ldy + n] = rres + v;
         }
         else if constexpr (EPI == EPI_QKV)
         {
