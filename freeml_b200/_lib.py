@@ -68,6 +68,7 @@ SIGNATURES = {
     "fml_attention_workspace_bytes": (ctypes.c_size_t, [_U32, _U32, _U32, _U32]),
     "fml_attention_decode": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _F, _P, ctypes.c_size_t, _P]),
     "fml_attention_decode_noalloc": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _F, _P]),
+    "fml_attention_prefill": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _I, _P]),
     "fml_set_math_mode": (_I, [_I]),
     "fml_get_math_mode": (_I, []),
     "fml_lm_create": (_I, [ctypes.POINTER(LMConfig), _I, ctypes.POINTER(_P)]),

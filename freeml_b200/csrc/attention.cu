@@ -383,13 +383,14 @@ extern "C" {
 int fml_device_error_count(uint64_t* count)
 {
     FML_REQUIRE(count, "fml_device_error_count: null argument");
-    int g = 0, k = 0;
+    int g = 0, k = 0, pf = 0;
     uint64_t tpw = 0;
     FML_CUDA_TRY(cudaDeviceSynchronize());
     FML_RC(gemm_tc_error_count(&g));
     FML_RC(skinny_error_count(&k));
+    FML_RC(prefill_tc_error_count(&pf));
     FML_RC(fml_lm_tp_error_count(&tpw));
-    *count = (uint64_t)g + (uint64_t)k + tpw;
+    *count = (uint64_t)g + (uint64_t)k + (uint64_t)pf + tpw;
     return FML_OK;
 }
 

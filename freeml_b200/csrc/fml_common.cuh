@@ -20,6 +20,7 @@ int set_error(int status, const char* fmt, ...);
 std::atomic<uint64_t>& launch_counter();
 int gemm_tc_error_count(int* out);  // tensor-core GEMM wait limits hit
 int skinny_error_count(int* out);   // skinny GEMM wait limits hit
+int prefill_tc_error_count(int* out);  // tensor-core prefill attention wait limits hit
 
 #define FML_CUDA_TRY(expr)                                                                     \
     do {                                                                                       \

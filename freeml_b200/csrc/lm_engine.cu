@@ -64,6 +64,9 @@ int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, ui
 int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
                              uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
                              float scale, cudaStream_t st);
+int launch_prefill_attention_tc(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
+                                uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
+                                float scale, bool split3, cudaStream_t st);
 
 // ---------------------------------------------------------------- kernels --
 
@@ -1658,9 +1661,19 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
         qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * dl, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, dl, lm->hd,
                                                                                c.context, lm->seq_stride);
         FML_LAUNCH_CHECK();
-        // prefill attention: 64-query tiles sharing each K/V tile
-        FML_RC(launch_prefill_attention(lm->q, dl, kc, vc, lm->seq_stride, c.context, lm->att, dl, batch, lm->hl, P,
-                                        lm->hd, 1.0f / sqrtf((float)lm->hd), st));
+        // prefill attention: tensor cores in the TF32 modes (128-query tiles),
+        // else (or for a layout that kernel does not take) the CUDA-core kernel
+        {
+            const float scale = 1.0f / sqrtf((float)lm->hd);
+            int rc = FML_ERR_UNSUPPORTED;
+            if (lm->prefill_math != FML_MATH_FP32)
+                rc = launch_prefill_attention_tc(lm->q, dl, kc, vc, lm->seq_stride, c.context, lm->att, dl, batch,
+                                                 lm->hl, P, lm->hd, scale, lm->prefill_math == FML_MATH_TF32X3, st);
+            if (rc == FML_ERR_UNSUPPORTED)
+                rc = launch_prefill_attention(lm->q, dl, kc, vc, lm->seq_stride, c.context, lm->att, dl, batch, lm->hl,
+                                              P, lm->hd, scale, st);
+            FML_RC(rc);
+        }
         // buf = x + att . Wproj^T ; hid = gelu(LN1(buf) . Wfc^T) ; x = buf + hid . Wmlp^T
         FML_RC(prefill_gemm(lm, lm->buf, lm->att, lm->wproj[l], (int)R, (int)d, (int)dl, resid_epi, lm->x, st,
                             lm->wlo_valid ? lm->wproj_lo[l] : nullptr));

@@ -122,6 +122,21 @@ def attention_decode_workspace_bytes(batch: int, heads: int, head_dim: int, cont
     return int(load().fml_attention_workspace_bytes(batch, heads, head_dim, context))
 
 
+def attention_prefill(out, q, kcache, vcache, prompt_len, scale, mode=None):
+    """Causal attention over whole prompts (fml_attention_prefill).
+    q/out: [B*P, H*hd] (row b*P + t); kcache/vcache: [B, H, C, hd] with rows
+    0..P-1 filled.  mode: FML_MATH_* (default: the library's math mode)."""
+    from ._lib import load
+    B, H, C, hd = kcache.shape
+    P = int(prompt_len)
+    _check(q.shape == (B * P, H * hd) and out.shape == q.shape and vcache.shape == kcache.shape,
+           "attention_prefill shapes")
+    if mode is None:
+        mode = int(load().fml_get_math_mode())
+    call("fml_attention_prefill", _p(out), _p(q), _p(kcache), _p(vcache), B, H, hd, C, P, float(scale), int(mode),
+         _s())
+
+
 def attention_decode(out, q, kcache, vcache, lens, scale, workspace=None):
     """Causal attention of the newest row per sequence over a KV cache
     (fml_attention_decode).  q/out: [B, H*hd]; kcache/vcache: [B, H, C, hd];

@@ -272,6 +272,20 @@ enum fml_math_mode { FML_MATH_FP32 = 0, FML_MATH_TF32X3 = 1, FML_MATH_TF32 = 2 }
 FML_API int fml_set_math_mode(int mode);
 FML_API int fml_get_math_mode(void);
 
+/* Causal attention over whole prompts -- the attention core of
+ * CausalSelfAttentionLayer::Forward (LayerLibrary/CausalSelfAttentionLayer.h:
+ * 424-499) for every row of a prompt, as the engine's prefill runs it:
+ *   q, out [batch*prompt_len x heads*head_dim] (row b*prompt_len + t)
+ *   kcache, vcache [batch][heads][context][head_dim], rows 0..prompt_len-1
+ *          of each (sequence, head) filled; rows past them may hold anything
+ *   row t attends keys 0..t; scale 1/sqrt(head_dim) in the reference
+ * mode: FML_MATH_FP32 (CUDA cores), FML_MATH_TF32X3 (tcgen05 tensor cores,
+ * fp32-level accuracy) or FML_MATH_TF32.  head_dim 32, 64 or 128;
+ * prompt_len <= context.  Allocates nothing. */
+FML_API int fml_attention_prefill(float* out, const float* q, const float* kcache, const float* vcache,
+                                  uint32_t batch, uint32_t heads, uint32_t head_dim, uint32_t context,
+                                  uint32_t prompt_len, float scale, int mode, fml_stream_t stream);
+
 /* ---------------------------------------------------------------------
  * 2. Decode engine
  * ------------------------------------------------------------------- */

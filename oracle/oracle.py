@@ -212,6 +212,20 @@ def attention_decode_ref(q, k, v, scale):
     return out
 
 
+def attention_prefill_ref(q, k, v, scale):
+    """Whole-prompt causal attention restated from the reference ops
+    (CausalSelfAttentionLayer.h:445-497: Q K^T via MatMul_Strided<Right>,
+    ScaleAdd with the 0/-inf lower-triangular mask, Softmax, P V via
+    MatMul_Strided<None>), per head.  q, k, v: [H, P, hd] -> [H, P, hd]."""
+    H, P, hd = q.shape
+    mask = np.where(np.tril(np.ones((P, P), bool)), 0.0, -np.inf).astype(np.float32)
+    out = np.empty((H, P, hd), np.float32)
+    for h in range(H):
+        s = op_scale_add(op_mul(q[h], k[h], 1), scale, mask)
+        out[h] = op_mul(op_softmax(s), v[h], 0)
+    return out
+
+
 # ---- the reference harness (FreeML's own MatrixCPU path) --------------------
 
 def ref_available() -> bool:

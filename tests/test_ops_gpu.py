@@ -232,6 +232,103 @@ def test_attention_decode_rejects_small_workspace():
                            workspace=torch.empty(16, dtype=torch.uint8, device="cuda"))
 
 
+def _prefill_case(B, H, hd, C, P, seed, poison=False):
+    rs = np.random.RandomState(seed)
+    q = rs.randn(B * P, H * hd).astype(np.float32)
+    kc = rs.randn(B, H, C, hd).astype(np.float32)
+    vc = rs.randn(B, H, C, hd).astype(np.float32)
+    if poison:  # cache rows past the prompt are never read into a result
+        kc[:, :, P:] = np.nan
+        vc[:, :, P:] = np.nan
+    return q, kc, vc
+
+
+def _prefill_oracle(q, kc, vc, P, scale):
+    B, H, C, hd = kc.shape
+    out = np.empty((B * P, H * hd), np.float32)
+    for b in range(B):
+        qb = q[b * P:(b + 1) * P].reshape(P, H, hd).transpose(1, 0, 2)
+        ob = O.attention_prefill_ref(np.ascontiguousarray(qb), kc[b, :, :P], vc[b, :, :P], scale)
+        out[b * P:(b + 1) * P] = ob.transpose(1, 0, 2).reshape(P, H * hd)
+    return out
+
+
+# tolerances against the fp32 oracle: outputs are convex combinations of
+# unit-variance values, scores are sums of hd unit-variance products
+PREFILL_TOL = {"fp32": 2e-5, "tf32x3": 1e-4, "tf32": 3e-2}
+
+
+@pytest.mark.parametrize("B,H,hd,C,P", [
+    (1, 2, 64, 300, 300),     # one partial 128-query tile after two full ones
+    (2, 3, 32, 200, 130),
+    (1, 2, 128, 260, 257),    # hd 128: 32-key tiles
+    (3, 1, 64, 64, 1),        # one-row prompts
+    (1, 4, 64, 512, 512),     # config 2's head shape
+    (2, 2, 64, 1024, 777),
+    (2, 2, 64, 256, 200),     # second query tile of a CTA ends past the prompt
+    (1, 1, 64, 2048, 1536),   # config 4's prompt length
+])
+@pytest.mark.parametrize("mode", ["tf32x3", "fp32", "tf32"])
+def test_attention_prefill_vs_oracle(B, H, hd, C, P, mode):
+    """Prefill attention (fml_attention_prefill) in each math mode against the
+    oracle's op-by-op restatement; in the TF32 modes the tcgen05 kernel,
+    128-query tiles with prompts that end mid-tile.  Cache rows past the
+    prompt hold NaN: they must not reach any output."""
+    from freeml_b200 import _lib
+    from freeml_b200 import matrix_ops as F
+    q, kc, vc = _prefill_case(B, H, hd, C, P, B * 1000 + P + hd, poison=True)
+    scale = float(1.0 / np.sqrt(np.float32(hd)))
+    out = torch.full((B * P, H * hd), 7.0, device="cuda")
+    m = {"fp32": _lib.FML_MATH_FP32, "tf32x3": _lib.FML_MATH_TF32X3, "tf32": _lib.FML_MATH_TF32}[mode]
+    F.attention_prefill(out, cu(q), cu(kc), cu(vc), P, scale, m)
+    got = host(out)
+    ref = _prefill_oracle(q, kc, vc, P, np.float32(scale))
+    assert np.isfinite(got).all()
+    tol = PREFILL_TOL[mode]
+    np.testing.assert_allclose(got, ref, rtol=tol, atol=tol)
+    if mode == "tf32":
+        assert np.abs(got - ref).max() > 1e-6  # it really is the reduced-precision path
+    n = ctypes_u64()
+    _lib.call("fml_device_error_count", ctypes.byref(n))
+    assert n.value == 0
+
+
+@pytest.mark.parametrize("mode", ["tf32x3", "tf32"])
+def test_attention_prefill_one_tile_kernel_at_hd64(monkeypatch, mode):
+    """At head dim 64 the TF32 modes run the two-tile warp-specialised
+    kernel; FML_PREFILL_ATTN_SIMPLE=1 selects the one-tile kernel (the one
+    head dims 32 and 128 use).  Both match the oracle."""
+    from freeml_b200 import _lib
+    from freeml_b200 import matrix_ops as F
+    B, H, hd, C, P = 2, 2, 64, 640, 600
+    q, kc, vc = _prefill_case(B, H, hd, C, P, 11, poison=True)
+    scale = float(1.0 / np.sqrt(np.float32(hd)))
+    m = {"tf32x3": _lib.FML_MATH_TF32X3, "tf32": _lib.FML_MATH_TF32}[mode]
+    ref = _prefill_oracle(q, kc, vc, P, np.float32(scale))
+    for simple in ("1", "0"):
+        monkeypatch.setenv("FML_PREFILL_ATTN_SIMPLE", simple)
+        out = torch.full((B * P, H * hd), 7.0, device="cuda")
+        F.attention_prefill(out, cu(q), cu(kc), cu(vc), P, scale, m)
+        np.testing.assert_allclose(host(out), ref, rtol=PREFILL_TOL[mode], atol=PREFILL_TOL[mode])
+
+
+def test_attention_prefill_modes_agree_on_engine_shape():
+    """Config 3's attention shape (12 heads x hd 64, 256-row prompts, 4
+    sequences): the TF32x3 tensor-core kernel and the fp32 CUDA-core kernel
+    agree to fp32 level."""
+    from freeml_b200 import _lib
+    from freeml_b200 import matrix_ops as F
+    B, H, hd, C, P = 4, 12, 64, 1024, 256
+    q, kc, vc = _prefill_case(B, H, hd, C, P, 5)
+    scale = float(1.0 / np.sqrt(np.float32(hd)))
+    outs = []
+    for m in (_lib.FML_MATH_TF32X3, _lib.FML_MATH_FP32):
+        out = torch.empty(B * P, H * hd, device="cuda")
+        F.attention_prefill(out, cu(q), cu(kc), cu(vc), P, scale, m)
+        outs.append(host(out))
+    np.testing.assert_allclose(outs[0], outs[1], rtol=1e-4, atol=1e-4)
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 128, 32), (130, 96, 260), (512, 1536, 512), (4096, 512, 2048), (7, 300, 64),
                                    # decode sizes (<= 64 rows; the GEMV serves them in every math mode)
                                    (1, 1536, 512), (32, 2048, 512), (17, 132, 128)])
