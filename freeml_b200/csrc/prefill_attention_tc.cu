@@ -357,29 +357,31 @@ __global__ void __launch_bounds__(128, 1) prefill_attention_tc_kernel(const __gr
 // CUDA cores work on the other:
 //   warps 0-3   softmax of tile A (thread = TMEM lane = query row)
 //   warps 4-7   softmax of tile B
-//   warps 8-9   converters: the TF32 lo parts of Q, K and V (TF32x3) and the
+//   warp 8      converter: the TF32 lo parts of K and V (TF32x3) and the
 //               zeroing of V rows past the last key any row sees
-//   warp 10     one thread issues every tcgen05.mma
+//   warps 9-10  one thread each issues tile A's / tile B's tcgen05.mma
 //   warp 11     one thread issues every TMA copy
-// TF32x3 products issue the hi.hi and hi.lo terms as ONE MMA of twice the
-// width (N = 128: a tf32 MMA of N = 64 costs 3/4 of one of N = 128 on this
-// part, so the 64-wide products run the tensor pipe at 2/3 of its rate): the
-// lo tiles of K and V sit next to the hi tiles along N, the two halves land
-// in separate TMEM columns and are summed when read; the lo.hi term is one
-// MMA of N = 64 into the first half.
-// TMEM per tile (2 x 256 columns): S = Q K^T [64 keys | the hi.lo half],
-// overwritten in place by P = exp(S - m) and P's lo part (the A operands of
-// O += P V, read from TMEM), and the O accumulator [64 | the hi.lo half],
-// which stays in TMEM over all key tiles.  A row
-// rescales O (tcgen05.ld / st) only when its running maximum rises by more
-// than 2^8 over the one its P values were taken against, so P stays below
-// 256 and fp32 keeps its precision; the result O / l does not depend on the
-// reference maximum.
-// Per key tile t, for each active tile x (t below x's key-tile count):
-//   S_x(t) after K(t) is converted and O_x(t-1) completed (P_x(t-1) lives in
-//   S_x's columns); P_x(t) after the softmax read S_x(t); O_x(t) after P_x(t)
-//   and V(t) are ready.  K(t+1) is copied once S(t) of both tiles completed,
-//   V(t+1) once O(t) did.
+// K and V operand tiles are double-buffered: the copy and the conversion of
+// key tile t + 1 run while tile t's products do.
+// TMEM per query tile (2 x 256 columns): S = Q K^T [64 keys | the hi.lo
+// half], overwritten in place by P = exp(S - m) and P's lo part (the A
+// operands of O += P V, read from TMEM); the O accumulator [64], which stays
+// in TMEM over all key tiles; and Q's lo part [64] (the A operand of the
+// lo.hi term of S).  A tf32 MMA of N = 64 costs 3/4 of one of N = 128 on
+// this part (it runs the tensor pipe at 2/3 of its rate), so S's hi.hi and
+// hi.lo terms are ONE MMA of N = 128 against [K hi | K lo] (the lo rows sit
+// next to the hi rows of each K box); O's three terms stay 64 wide for the
+// TMEM that Q lo needs.
+// A row rescales O (tcgen05.ld / st) only when its running maximum rises by
+// more than 2^8 over the one its P values were taken against, so P stays
+// below 256 and fp32 keeps its precision; the result O / l does not depend
+// on the reference maximum.
+// The tensor pipe's instruction queue is short: while the thread that issues
+// MMAs waits on an mbarrier (even one already complete, ~170 cycles), the
+// pipe drains and idles.  So each query tile has its own issuing thread, in
+// its own warp, and the pipe runs one tile's products while the other's
+// thread waits (for its softmax, or for the completion of O_x(t-1): S_x(t)
+// overwrites the columns P_x(t-1) is read from).
 // Every wait is bounded and also returns early once any role has recorded an
 // expiry in the CTA's abort flag; the MMA thread then waits for its MMAs and
 // the copy thread for its copies (bounded) before TMEM is freed.
@@ -389,21 +391,21 @@ constexpr int PP_HD = 64, PP_KT = 64;
 constexpr uint32_t PP_QTILE = 128 * PP_HD * 4;  // one 128-row Q tile, 32 KB
 constexpr uint32_t PP_KVT = PP_KT * PP_HD * 4;  // one K or V tile, 16 KB
 constexpr int PP_THREADS = 12 * 32;
-constexpr uint32_t PP_CONV = 64;  // converter threads
-// Q tiles (hi, lo), K and V (hi, lo), and one staging tile each for the
-// copies of the next K and V
-constexpr uint32_t PP_SMEM = 4 * PP_QTILE + 6 * PP_KVT + 1024 + 256;
-// F: copy landed in the staging tile; S: staging tile read out; R: converted
-// operand ready; E: operand consumed by its MMAs
-enum PpBar { PB_QF, PB_QR, PB_KF, PB_KS, PB_KR, PB_KE, PB_VF, PB_VS, PB_VR, PB_VE, PB_S0, PB_S1, PB_P0, PB_P1, PB_O0,
-             PB_O1, PB_FIN, PB_N };
+constexpr uint32_t PP_CONV = 32;  // converter threads
+// operand tiles: K box j (head columns 32j..) = [64 hi rows | 64 lo rows] of
+// 128 bytes (16 KB); V key block kb = four 4 KB boxes [hi columns 0-31, hi
+// 32-63, lo 0-31, lo 32-63] of 32 keys (16 KB)
+constexpr uint32_t PP_KBOX = 2 * PP_KT * 128, PP_VBLK = 4 * 4096, PP_KVOP = 2 * PP_KVT;
+// Q hi tiles, then two K and two V operand tiles (hi and lo each)
+constexpr uint32_t PP_SMEM = 2 * PP_QTILE + 4 * PP_KVOP + 1024 + 256;
+// per operand buffer b: F copy landed, R converted, E[x] consumed by tile
+// x's MMAs (index 2x + b); per query tile x: S, P, O and the final drain
+enum PpBar { PB_QF, PB_QR, PB_KF, PB_KR = PB_KF + 2, PB_KE = PB_KR + 2, PB_VF = PB_KE + 4, PB_VR = PB_VF + 2,
+             PB_VE = PB_VR + 2, PB_S0 = PB_VE + 4, PB_P0 = PB_S0 + 2, PB_O0 = PB_P0 + 2, PB_FIN = PB_O0 + 2,
+             PB_N = PB_FIN + 2 };
 // TMEM columns of tile x: S / P [0, 64), S's hi.lo half / P lo [64, 128), O
-// [128, 192), O's hi.lo half [192, 256)
-constexpr uint32_t PP_TX = 256, PP_PLO = 64, PP_O = 128, PP_HALF = 64;
-// shared-memory operand tiles: K box j (head columns 32j..) = [64 hi rows |
-// 64 lo rows] of 128 bytes (16 KB); V key block kb = four 4 KB boxes [hi
-// columns 0-31, hi 32-63, lo 0-31, lo 32-63] of 32 keys (16 KB)
-constexpr uint32_t PP_KBOX = 2 * PP_KT * 128, PP_VBLK = 4 * 4096;
+// [128, 192), Q lo [192, 256)
+constexpr uint32_t PP_TX = 256, PP_PLO = 64, PP_O = 128, PP_QLO = 192;
 
 __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity)
 {
@@ -432,6 +434,15 @@ __device__ __forceinline__ bool pp_wait(uint64_t* bar, uint32_t ph, volatile int
     return false;
 }
 
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22; 2^-inf = +0)
+__device__ __forceinline__ float ex2_approx(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -446,18 +457,15 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
 {
     using namespace tc;
     constexpr uint32_t IDESC_S = idesc_tf32(128, PP_KT);
-    constexpr uint32_t IDESC_S2 = idesc_tf32(128, 2 * PP_KT);               // [K hi | K lo]
-    constexpr uint32_t IDESC_O = idesc_tf32(128, PP_HD) | (1u << 16);       // B (V) read MN-major
-    constexpr uint32_t IDESC_O2 = idesc_tf32(128, 2 * PP_HD) | (1u << 16);  // [V hi | V lo]
+    constexpr uint32_t IDESC_S2 = idesc_tf32(128, 2 * PP_KT);          // [K hi | K lo]
+    constexpr uint32_t IDESC_O = idesc_tf32(128, PP_HD) | (1u << 16);  // B (V) read MN-major
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* q_s = smem;                    // tile x hi at x * QTILE, lo at (2 + x) * QTILE
-    unsigned char* k_s = smem + 4 * PP_QTILE;     // K hi and lo (PP_KBOX layout)
-    unsigned char* v_s = k_s + 2 * PP_KVT;        // V hi and lo (PP_VBLK layout)
-    unsigned char* kst = v_s + 2 * PP_KVT;        // staging: the next K tile
-    unsigned char* vst = kst + PP_KVT;            // staging: the next V tile
-    uint64_t* bars = reinterpret_cast<uint64_t*>(vst + PP_KVT);
+    unsigned char* q_s = smem;                     // Q hi of tile x at x * QTILE
+    unsigned char* k_op = smem + 2 * PP_QTILE;     // K operand buffer b at b * KVOP (PP_KBOX layout)
+    unsigned char* v_op = k_op + 2 * PP_KVOP;      // V operand buffer b at b * KVOP (PP_VBLK layout)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(v_op + 2 * PP_KVOP);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + PB_N);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -477,9 +485,13 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
     if (tid == 0)
     {
         for (int i = 0; i < PB_N; ++i)
-            mbar_init(&bars[i], (i == PB_QR || i == PB_KS || i == PB_KR || i == PB_VS || i == PB_VR) ? PP_CONV
-                                : (i == PB_P0 || i == PB_P1)                                         ? 128u
-                                                                                                     : 1u);
+        {
+            uint32_t count = 1;
+            if (i == PB_QR) count = 256;  // every softmax thread writes its Q lo row
+            if (i == PB_KR || i == PB_KR + 1 || i == PB_VR || i == PB_VR + 1) count = PP_CONV;
+            if (i == PB_P0 || i == PB_P0 + 1) count = 128;
+            mbar_init(&bars[i], count);
+        }
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -500,12 +512,38 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
         // ---------------- softmax of tile x ----------------
         const int x = warp >> 2;
         const uint32_t nt = x ? nt1 : nt0;
-        const uint32_t row = q0 + 128u * x + 32u * (warp & 3) + lane;  // this thread's query row
+        const int r = 32 * (warp & 3) + lane;                 // row within the tile
+        const uint32_t row = q0 + 128u * x + (uint32_t)r;     // this thread's query row
         const uint32_t tx = tmem + PP_TX * x + ((uint32_t)(32 * (warp & 3)) << 16);
         const float sl2 = a.scale * 1.4426950408889634f;  // scores in log2 units
         float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (uint32_t t = 0; t < nt; ++t)
+        bool ok = __all_sync(FULL_MASK, pp_wait(&bars[PB_QF], 0, abort));
+        if (ok && SPLIT3)
+        {
+            // Q lo of this row into TMEM: row r of box j holds head columns
+            // 32j + 4c.. in 16-byte chunk c ^ (r % 8)
+            const unsigned char* qrow = q_s + x * PP_QTILE + r * 128;
+#pragma unroll
+            for (int j = 0; j < PP_HD / 32; ++j)
+            {
+                uint32_t u[32];
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                {
+                    const float4 v = *reinterpret_cast<const float4*>(qrow + j * (128 * 128) + ((c ^ (r & 7)) * 16));
+                    const float4 lo = tf32_lo4(v);
+                    u[4 * c] = __float_as_uint(lo.x);
+                    u[4 * c + 1] = __float_as_uint(lo.y);
+                    u[4 * c + 2] = __float_as_uint(lo.z);
+                    u[4 * c + 3] = __float_as_uint(lo.w);
+                }
+                tmem_st32(tx + PP_QLO + 32 * j, u);
+            }
+            tmem_wait_st();
+        }
+        tc_fence_before();
+        mbar_arrive(&bars[PB_QR]);
+        for (uint32_t t = 0; ok && t < nt; ++t)
         {
             ok = __all_sync(FULL_MASK, pp_wait(&bars[PB_S0 + x], t, abort));
             if (!ok) break;
@@ -514,45 +552,68 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
 #pragma unroll
             for (int c = 0; c < PP_KT; c += 32)
             {
-                float v[32];
-                tmem_ld32(tx + c, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) s[c + i] = v[i];
+                uint32_t u[32];
+                tmem_ld32_async(tx + c, u);
                 if constexpr (SPLIT3)
                 {
-                    tmem_ld32(tx + PP_HALF + c, v);
+                    uint32_t w[32];
+                    tmem_ld32_async(tx + PP_PLO + c, w);
+                    tmem_wait_ld(u);
+                    tmem_wait_ld(w);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) s[c + i] += v[i];
+                    for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(u[i]) + __uint_as_float(w[i]);
+                }
+                else
+                {
+                    tmem_wait_ld(u);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) s[c + i] = __uint_as_float(u[i]);
                 }
             }
             const uint32_t k0 = t * PP_KT;
-            float mt = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < PP_KT; ++i)
+            // the mask only bites in tiles that reach past the warp's first
+            // row or past the prompt (a warp-uniform test)
+            const uint32_t row0 = row - lane;
+            float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (k0 + PP_KT - 1 <= row0 && k0 + PP_KT <= P)
             {
-                const uint32_t key = k0 + i;
-                s[i] = (key <= row && key < P) ? s[i] * sl2 : -INFINITY;  // a select: masked slots may hold NaN
-                mt = fmaxf(mt, s[i]);
+#pragma unroll
+                for (int i = 0; i < PP_KT; ++i)
+                {
+                    s[i] *= sl2;
+                    mx4[i & 3] = fmaxf(mx4[i & 3], s[i]);
+                }
             }
+            else
+            {
+#pragma unroll
+                for (int i = 0; i < PP_KT; ++i)
+                {
+                    const uint32_t key = k0 + i;
+                    s[i] = (key <= row && key < P) ? s[i] * sl2 : -INFINITY;  // a select: masked slots may hold NaN
+                    mx4[i & 3] = fmaxf(mx4[i & 3], s[i]);
+                }
+            }
+            const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
             const bool need = mt > m + 8.0f;
             if (__any_sync(FULL_MASK, need))
             {
                 const float mn = need ? mt : m;
-                const float corr = exp2f(m - mn);  // 0 on the first tile (m = -inf)
+                const float corr = ex2_approx(m - mn);  // 0 on the first tile (m = -inf)
                 l *= corr;
                 m = mn;
                 if (t > 0)
                 {
                     // O_x(t-1) has completed: S_x(t) was issued after it
 #pragma unroll
-                    for (int c = 0; c < (SPLIT3 ? 2 : 1) * PP_HD; c += 32)
+                    for (int c = 0; c < PP_HD; c += 32)
                     {
                         float v[32];
-                        uint32_t r[32];
+                        uint32_t u[32];
                         tmem_ld32(tx + PP_O + c, v);
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i] * corr);
-                        tmem_st32(tx + PP_O + c, r);
+                        for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i] * corr);
+                        tmem_st32(tx + PP_O + c, u);
                     }
                 }
             }
@@ -560,21 +621,21 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
 #pragma unroll
             for (int c = 0; c < PP_KT; c += 32)
             {
-                uint32_t r[32];
+                uint32_t u[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
                 {
-                    const float p = exp2f(s[c + i] - m);  // 0 for masked keys
+                    const float p = ex2_approx(s[c + i] - m);  // 0 for masked keys
                     ls[i & 3] += p;
                     s[c + i] = p;
-                    r[i] = __float_as_uint(p);
+                    u[i] = __float_as_uint(p);
                 }
-                tmem_st32(tx + c, r);  // P over S's columns (the MMA reads its TF32 part)
+                tmem_st32(tx + c, u);  // P over S's columns (the MMA reads its TF32 part)
                 if constexpr (SPLIT3)
                 {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(s[c + i] - tf32_hi(s[c + i]));
-                    tmem_st32(tx + PP_PLO + c, r);
+                    for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(s[c + i] - tf32_hi(s[c + i]));
+                    tmem_st32(tx + PP_PLO + c, u);
                 }
             }
             l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
@@ -595,13 +656,6 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
                 {
                     float v[32];
                     tmem_ld32(tx + PP_O + c, v);
-                    if constexpr (SPLIT3)
-                    {
-                        float w[32];
-                        tmem_ld32(tx + PP_O + PP_HALF + c, w);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] += w[i];
-                    }
                     if (row < P)
 #pragma unroll
                         for (int i = 0; i < 32; i += 4)
@@ -611,143 +665,121 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
             }
         }
     }
-    else if (warp < 10)
+    else if (warp == 8)
     {
-        // ---------------- converters ----------------
+        // ---------------- converter ----------------
         const int ct = tid - 256;
-        if (pp_wait(&bars[PB_QF], 0, abort))
+        for (uint32_t t = 0; t < ntiles; ++t)
         {
+            const uint32_t bf = t & 1u, ph = t >> 1;
+            // K(t): lo rows from the hi rows the copy wrote (box j = 512
+            // float4 hi, then 512 lo)
+            if (!pp_wait(&bars[PB_KF + bf], ph, abort)) break;
             if constexpr (SPLIT3)
             {
-                const uint32_t n4 = (has_b ? 2u : 1u) * PP_QTILE / 16;
-                const float4* src = reinterpret_cast<const float4*>(q_s);
-                float4* dst = reinterpret_cast<float4*>(q_s + 2 * PP_QTILE);
-                for (uint32_t i = ct; i < n4; i += PP_CONV) dst[i] = tf32_lo4(src[i]);
+                float4* kb4 = reinterpret_cast<float4*>(k_op + bf * PP_KVOP);
+#pragma unroll 4
+                for (uint32_t i = ct; i < PP_KVT / 16; i += PP_CONV)
+                {
+                    float4* hi = kb4 + (i / 512) * 1024 + (i % 512);
+                    hi[512] = tf32_lo4(hi[0]);
+                }
             }
             fence_async_smem();
-            mbar_arrive(&bars[PB_QR]);
-            for (uint32_t t = 0; t < ntiles; ++t)
+            mbar_arrive(&bars[PB_KR + bf]);
+            // V(t): key block kb = hi boxes (256 float4 each) then lo boxes;
+            // rows at or past `nkeys` are zeroed (the cache there may hold
+            // anything, and 0 * NaN is NaN)
+            if (!pp_wait(&bars[PB_VF + bf], ph, abort)) break;
             {
-                // K(t): staging -> operand tiles once S(t-1) released them
-                if (!pp_wait(&bars[PB_KF], t, abort)) break;
-                if (t > 0 && !pp_wait(&bars[PB_KE], t - 1, abort)) break;
+                const uint32_t k0 = t * PP_KT;
+                const uint32_t valid = nkeys - k0 < (uint32_t)PP_KT ? nkeys - k0 : (uint32_t)PP_KT;
+                if (SPLIT3 || valid < (uint32_t)PP_KT)
                 {
-                    // staging box j (8 KB, 512 float4) -> operand box j
-                    const float4* src = reinterpret_cast<const float4*>(kst);
+                    float4* vb4 = reinterpret_cast<float4*>(v_op + bf * PP_KVOP);
 #pragma unroll 4
                     for (uint32_t i = ct; i < PP_KVT / 16; i += PP_CONV)
                     {
-                        const float4 v = src[i];
-                        float4* hi = reinterpret_cast<float4*>(k_s + (i / 512) * PP_KBOX) + (i % 512);
-                        hi[0] = v;
-                        if constexpr (SPLIT3) hi[512] = tf32_lo4(v);
+                        const uint32_t kb = i / 512, key = kb * 32 + (i % 256) / 8;
+                        float4* hi = vb4 + kb * 1024 + (i % 512);
+                        if (key >= valid)
+                        {
+                            hi[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if constexpr (SPLIT3) hi[512] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                        else if constexpr (SPLIT3)
+                            hi[512] = tf32_lo4(hi[0]);
                     }
                 }
-                mbar_arrive(&bars[PB_KS]);  // the staging tile may be refilled
-                fence_async_smem();
-                mbar_arrive(&bars[PB_KR]);
-                // V(t): the same once O(t-1) released them.  V box (kb, j) =
-                // keys kb*32.., head columns 32j.., 4 KB of 32 rows; rows at
-                // or past `nkeys` are zeroed (the cache there may hold
-                // anything, and 0 * NaN is NaN)
-                if (!pp_wait(&bars[PB_VF], t, abort)) break;
-                if (t > 0 && !pp_wait(&bars[PB_VE], t - 1, abort)) break;
-                {
-                    const uint32_t k0 = t * PP_KT;
-                    const uint32_t valid = nkeys - k0 < (uint32_t)PP_KT ? nkeys - k0 : (uint32_t)PP_KT;
-                    // staging box (kb, j) (4 KB, 256 float4) -> hi box j and
-                    // lo box 2 + j of key block kb
-                    const float4* src = reinterpret_cast<const float4*>(vst);
-#pragma unroll 4
-                    for (uint32_t i = ct; i < PP_KVT / 16; i += PP_CONV)
-                    {
-                        const uint32_t box = i / 256, kb = box / (PP_HD / 32), j = box % (PP_HD / 32);
-                        const uint32_t key = kb * 32 + (i % 256) / 8;
-                        float4 v = src[i];
-                        if (key >= valid) v = make_float4(0.f, 0.f, 0.f, 0.f);
-                        float4* hi = reinterpret_cast<float4*>(v_s + kb * PP_VBLK + j * 4096) + (i % 256);
-                        hi[0] = v;
-                        if constexpr (SPLIT3) hi[512] = tf32_lo4(v);
-                    }
-                }
-                mbar_arrive(&bars[PB_VS]);
-                fence_async_smem();
-                mbar_arrive(&bars[PB_VR]);
             }
+            fence_async_smem();
+            mbar_arrive(&bars[PB_VR + bf]);
         }
     }
-    else if (warp == 10)
+    else if (warp < 11)
     {
-        // ---------------- MMA issue ----------------
-        if (lane == 0)
+        // ---------------- MMA issue for tile x ----------------
+        const int x = warp - 9;
+        const uint32_t nt = x ? nt1 : nt0;
+        if (lane == 0 && nt > 0)
         {
             // descriptors: one base each, advanced by (byte offset >> 4) in
             // the start-address field (shared addresses stay below 2^18)
-            const uint64_t dq[2] = {smem_desc(q_s, 0), smem_desc(q_s + PP_QTILE, 0)};
-            const uint64_t dk = smem_desc(k_s, 0), dv = desc_mn(v_s);
-            constexpr uint64_t QLO = (2 * PP_QTILE) >> 4;
+            const uint64_t dq = smem_desc(q_s + x * PP_QTILE, 0);
+            const uint64_t dk = smem_desc(k_op, 0), dv = desc_mn(v_op);
+            const uint32_t ts = tmem + PP_TX * x, to = ts + PP_O;
             bool ok = pp_wait(&bars[PB_QR], 0, abort);
-            for (uint32_t t = 0; ok && t < ntiles; ++t)
+            for (uint32_t t = 0; ok && t < nt; ++t)
             {
-                ok = pp_wait(&bars[PB_KR], t, abort);
-                for (int x = 0; ok && x < 2; ++x)
-                {
-                    if (t >= (x ? nt1 : nt0)) continue;
-                    if (t > 0 && !(ok = pp_wait(&bars[PB_O0 + x], t - 1, abort))) break;
-                    tc_fence_after();
-                    const uint32_t d = tmem + PP_TX * x;
+                const uint32_t bf = t & 1u, ph = t >> 1;
+                // S_x(t) = Q_x K(t)^T, after O_x(t-1) has read P_x(t-1)
+                if (!(ok = pp_wait(&bars[PB_KR + bf], ph, abort))) break;
+                if (t > 0 && !(ok = pp_wait(&bars[PB_O0 + x], t - 1, abort))) break;
+                tc_fence_after();
+                const uint64_t kbase = dk + ((bf * PP_KVOP) >> 4);
 #pragma unroll
-                    for (int j = 0; j < PP_HD / 32; ++j)
+                for (int j = 0; j < PP_HD / 32; ++j)
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
+                    for (int kk = 0; kk < 4; ++kk)
+                    {
+                        const uint64_t da = dq + ((j * (128 * 128) + kk * 32) >> 4);
+                        const uint64_t db = kbase + ((j * PP_KBOX + kk * 32) >> 4);
+                        if constexpr (SPLIT3)
                         {
-                            const uint64_t da = dq[x] + ((j * (128 * 128) + kk * 32) >> 4);
-                            const uint64_t db = dk + ((j * PP_KBOX + kk * 32) >> 4);
-                            if constexpr (SPLIT3)
-                            {
-                                // [hi.hi | hi.lo] in one MMA, then lo.hi into the first half
-                                mma_tf32(d, da, db, IDESC_S2, j > 0 || kk > 0);
-                                mma_tf32(d, da + QLO, db, IDESC_S, true);
-                            }
-                            else
-                                mma_tf32(d, da, db, IDESC_S, j > 0 || kk > 0);
+                            // [hi.hi | hi.lo] in one MMA, then lo.hi (Q lo from TMEM) into the first half
+                            mma_tf32(ts, da, db, IDESC_S2, j > 0 || kk > 0);
+                            mma_tf32_tmem_a(ts, ts + PP_QLO + 32 * j + 8 * kk, db, IDESC_S, true);
                         }
-                    mma_commit(&bars[PB_S0 + x]);
-                }
-                if (!ok) break;
-                mma_commit(&bars[PB_KE]);  // the K tile is free once these MMAs completed
-                ok = pp_wait(&bars[PB_VR], t, abort);
-                for (int x = 0; ok && x < 2; ++x)
-                {
-                    if (t >= (x ? nt1 : nt0)) continue;
-                    if (!(ok = pp_wait(&bars[PB_P0 + x], t, abort))) break;
-                    tc_fence_after();
-                    const uint32_t d = tmem + PP_TX * x + PP_O;
-                    const uint32_t pa = tmem + PP_TX * x;
+                        else
+                            mma_tf32(ts, da, db, IDESC_S, j > 0 || kk > 0);
+                    }
+                mma_commit(&bars[PB_S0 + x]);
+                mma_commit(&bars[PB_KE + 2 * x + bf]);
+                // O_x += P_x(t) V(t)
+                if (!(ok = pp_wait(&bars[PB_VR + bf], ph, abort))) break;
+                if (!(ok = pp_wait(&bars[PB_P0 + x], t, abort))) break;
+                tc_fence_after();
+                const uint64_t vbase = dv + ((bf * PP_KVOP) >> 4);
 #pragma unroll
-                    for (int kb = 0; kb < PP_KT / 32; ++kb)
+                for (int kb = 0; kb < PP_KT / 32; ++kb)
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
+                    for (int kk = 0; kk < 4; ++kk)
+                    {
+                        const uint64_t db = vbase + ((kb * PP_VBLK + kk * 1024) >> 4);
+                        const uint32_t col = kb * 32 + kk * 8;
+                        mma_tf32_tmem_a(to, ts + col, db, IDESC_O, t > 0 || kb > 0 || kk > 0);
+                        if constexpr (SPLIT3)
                         {
-                            const uint64_t db = dv + ((kb * PP_VBLK + kk * 1024) >> 4);
-                            const uint32_t col = kb * 32 + kk * 8;
-                            const bool acc = t > 0 || kb > 0 || kk > 0;
-                            if constexpr (SPLIT3)
-                            {
-                                mma_tf32_tmem_a(d, pa + col, db, IDESC_O2, acc);
-                                mma_tf32_tmem_a(d, pa + PP_PLO + col, db, IDESC_O, true);
-                            }
-                            else
-                                mma_tf32_tmem_a(d, pa + col, db, IDESC_O, acc);
+                            mma_tf32_tmem_a(to, ts + col, db + (8192 >> 4), IDESC_O, true);  // P hi . V lo
+                            mma_tf32_tmem_a(to, ts + PP_PLO + col, db, IDESC_O, true);      // P lo . V hi
                         }
-                    mma_commit(&bars[PB_O0 + x]);
-                }
-                if (!ok) break;
-                mma_commit(&bars[PB_VE]);
+                    }
+                mma_commit(&bars[PB_O0 + x]);
+                mma_commit(&bars[PB_VE + 2 * x + bf]);
             }
             // every MMA this thread issued completes before TMEM is freed
-            mma_commit(&bars[PB_FIN]);
-            mbar_wait(&bars[PB_FIN], 0);
+            mma_commit(&bars[PB_FIN + x]);
+            mbar_wait(&bars[PB_FIN + x], 0);
         }
     }
     else
@@ -755,41 +787,46 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
         // ---------------- TMA copies ----------------
         if (lane == 0)
         {
-            uint32_t nk = 0, nv = 0;
-            auto issue_k = [&](uint32_t t) {
-                mbar_arrive_expect_tx(&bars[PB_KF], PP_KVT);
-                for (int j = 0; j < PP_HD / 32; ++j)
-                    tma_load_2d(kst + j * (PP_KT * 128), &map_k, 32 * j, kv_row0 + (int)(t * PP_KT), &bars[PB_KF]);
-                ++nk;
-            };
-            auto issue_v = [&](uint32_t t) {
-                mbar_arrive_expect_tx(&bars[PB_VF], PP_KVT);
-                for (int kb = 0; kb < PP_KT / 32; ++kb)
-                    for (int j = 0; j < PP_HD / 32; ++j)
-                        tma_load_2d(vst + (kb * (PP_HD / 32) + j) * 4096, &map_v, 32 * j,
-                                    kv_row0 + (int)(t * PP_KT) + 32 * kb, &bars[PB_VF]);
-                ++nv;
-            };
             const int nq = has_b ? 2 : 1;
             mbar_arrive_expect_tx(&bars[PB_QF], nq * PP_QTILE);
             for (int x = 0; x < nq; ++x)
                 for (int j = 0; j < PP_HD / 32; ++j)
                     tma_load_2d(q_s + x * PP_QTILE + j * (128 * 128), &map_q, (int)(h * PP_HD) + 32 * j,
                                 (int)(b * P + q0 + 128 * x), &bars[PB_QF]);
-            issue_k(0);
-            issue_v(0);
-            for (uint32_t t = 1; t < ntiles; ++t)
+            uint32_t issued = 0;
+            for (uint32_t t = 0; t < ntiles; ++t)
             {
-                if (!pp_wait(&bars[PB_KS], t - 1, abort)) break;
-                issue_k(t);
-                if (!pp_wait(&bars[PB_VS], t - 1, abort)) break;
-                issue_v(t);
+                const uint32_t bf = t & 1u;
+                // K(t) into buffer t % 2 once S_A(t-2) and S_B(t-2) have read it
+                if (t >= 2 && t - 2 < nt0 && !pp_wait(&bars[PB_KE + bf], (t >> 1) - 1, abort)) break;
+                if (t >= 2 && t - 2 < nt1 && !pp_wait(&bars[PB_KE + 2 + bf], (t >> 1) - 1, abort)) break;
+                mbar_arrive_expect_tx(&bars[PB_KF + bf], PP_KVT);
+                for (int j = 0; j < PP_HD / 32; ++j)
+                    tma_load_2d(k_op + bf * PP_KVOP + j * PP_KBOX, &map_k, 32 * j, kv_row0 + (int)(t * PP_KT),
+                                &bars[PB_KF + bf]);
+                // V(t) once O_A(t-2) and O_B(t-2) have
+                if ((t >= 2 && t - 2 < nt0 && !pp_wait(&bars[PB_VE + bf], (t >> 1) - 1, abort)) ||
+                    (t >= 2 && t - 2 < nt1 && !pp_wait(&bars[PB_VE + 2 + bf], (t >> 1) - 1, abort)))
+                {
+                    issued = 2 * t + 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&bars[PB_VF + bf], PP_KVT);
+                for (int kb = 0; kb < PP_KT / 32; ++kb)
+                    for (int j = 0; j < PP_HD / 32; ++j)
+                        tma_load_2d(v_op + bf * PP_KVOP + kb * PP_VBLK + j * 4096, &map_v, 32 * j,
+                                    kv_row0 + (int)(t * PP_KT) + 32 * kb, &bars[PB_VF + bf]);
+                issued = 2 * t + 2;
             }
             // the copies this thread started land before the CTA exits
-            // (bounded; immediate on the normal path)
+            // (bounded; immediate on the normal path).  Copy n < issued is
+            // K(n / 2) for even n, V(n / 2) for odd n.
             mbar_wait(&bars[PB_QF], 0);
-            mbar_wait(&bars[PB_KF], (nk - 1) & 1u);
-            mbar_wait(&bars[PB_VF], (nv - 1) & 1u);
+            for (uint32_t n = issued >= 4 ? issued - 4 : 0; n < issued; ++n)
+            {
+                const uint32_t t = n >> 1;
+                mbar_wait(&bars[(n & 1u ? PB_VF : PB_KF) + (t & 1u)], t >> 1);
+            }
         }
     }
 
