@@ -79,6 +79,7 @@ struct TcArgs
     float* C;         // [M x N], row stride ldc
     int ldc;
     const float* R;   // TC_RESID: C = R + A.B^T (row stride ldc)
+    bool vec4;        // C (and R) 16-byte aligned with ldc a multiple of 4
 };
 
 // One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x +
@@ -295,15 +296,40 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
                 {
                     float* crow = args.C + (uint64_t)row * args.ldc + n0 + c0;
                     const float* rrow = EPI == TC_RESID ? args.R + (uint64_t)row * args.ldc + n0 + c0 : nullptr;
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj)
+                    if (args.vec4 && n0 + c0 + 32 <= args.N)
                     {
-                        if (n0 + c0 + jj < args.N)
+                        // whole 32-column slice, 16-byte aligned rows: float4
+                        // stores (and residual loads), a quarter of the
+                        // memory instructions of the scalar path
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj += 4)
                         {
-                            float x = v[jj];
-                            if constexpr (EPI == TC_GELU) x = gelu_exact(x);
-                            if constexpr (EPI == TC_RESID) x += rrow[jj];
-                            crow[jj] = x;
+                            float4 x = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
+                            if constexpr (EPI == TC_GELU)
+                            {
+                                x.x = gelu_exact(x.x); x.y = gelu_exact(x.y);
+                                x.z = gelu_exact(x.z); x.w = gelu_exact(x.w);
+                            }
+                            if constexpr (EPI == TC_RESID)
+                            {
+                                const float4 r = *reinterpret_cast<const float4*>(rrow + jj);
+                                x.x += r.x; x.y += r.y; x.z += r.z; x.w += r.w;
+                            }
+                            *reinterpret_cast<float4*>(crow + jj) = x;
+                        }
+                    }
+                    else
+                    {
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj)
+                        {
+                            if (n0 + c0 + jj < args.N)
+                            {
+                                float x = v[jj];
+                                if constexpr (EPI == TC_GELU) x = gelu_exact(x);
+                                if constexpr (EPI == TC_RESID) x += rrow[jj];
+                                crow[jj] = x;
+                            }
                         }
                     }
                 }
@@ -365,7 +391,7 @@ int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int l
     const bool blo = split3 && B_lo;
     if (blo) FML_RC(tc::make_map(&mblo, B_lo, N, K, ldb, tc::BN));
     else mblo = mb;
-    TcArgs args{M, N, K, C, ldc, R};
+    TcArgs args{M, N, K, C, ldc, R, aligned16(C) && (!R || aligned16(R)) && ldc % 4 == 0};
     if (blo)
     {
         if (epi == TC_GELU) return launch_tc<true, TC_GELU, true>(ma, mb, mblo, args, st);
@@ -399,7 +425,7 @@ int gemm_tc_nn(float* C, const float* A, const float* B, int M, int N, int K, in
     // B [K x N]: n is the contiguous (inner) dimension, 32 x 32 boxes in the
     // 32-byte-atom swizzle of an MN-major tf32 operand
     FML_RC(tc::make_map(&mb, B, K, N, ldb, (int)tc::MN_BOX, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
-    TcArgs args{M, N, K, C, ldc, nullptr};
+    TcArgs args{M, N, K, C, ldc, nullptr, aligned16(C) && ldc % 4 == 0};
     if (split3) return launch_tc<true, TC_STORE, false, true>(ma, mb, mb, args, st);
     return launch_tc<false, TC_STORE, false, true>(ma, mb, mb, args, st);
 }

@@ -677,12 +677,16 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
             if (!pp_wait(&bars[PB_KF + bf], ph, abort)) break;
             if constexpr (SPLIT3)
             {
-                float4* kb4 = reinterpret_cast<float4*>(k_op + bf * PP_KVOP);
-#pragma unroll 4
-                for (uint32_t i = ct; i < PP_KVT / 16; i += PP_CONV)
+                // 16 loads in flight per thread before the stores
+#pragma unroll
+                for (int c = 0; c < PP_HD / 32; ++c)
                 {
-                    float4* hi = kb4 + (i / 512) * 1024 + (i % 512);
-                    hi[512] = tf32_lo4(hi[0]);
+                    float4* box = reinterpret_cast<float4*>(k_op + bf * PP_KVOP + c * PP_KBOX);
+                    float4 v[16];
+#pragma unroll
+                    for (int n = 0; n < 16; ++n) v[n] = box[ct + 32 * n];
+#pragma unroll
+                    for (int n = 0; n < 16; ++n) box[512 + ct + 32 * n] = tf32_lo4(v[n]);
                 }
             }
             fence_async_smem();
@@ -694,21 +698,34 @@ __global__ void __launch_bounds__(PP_THREADS, 1) prefill_attention_pp_kernel(con
             {
                 const uint32_t k0 = t * PP_KT;
                 const uint32_t valid = nkeys - k0 < (uint32_t)PP_KT ? nkeys - k0 : (uint32_t)PP_KT;
-                if (SPLIT3 || valid < (uint32_t)PP_KT)
+#pragma unroll
+                for (int c = 0; c < PP_KT / 32; ++c)
                 {
-                    float4* vb4 = reinterpret_cast<float4*>(v_op + bf * PP_KVOP);
-#pragma unroll 4
-                    for (uint32_t i = ct; i < PP_KVT / 16; i += PP_CONV)
+                    float4* blk = reinterpret_cast<float4*>(v_op + bf * PP_KVOP + c * PP_VBLK);
+                    if (valid == (uint32_t)PP_KT)
                     {
-                        const uint32_t kb = i / 512, key = kb * 32 + (i % 256) / 8;
-                        float4* hi = vb4 + kb * 1024 + (i % 512);
-                        if (key >= valid)
+                        if constexpr (SPLIT3)
                         {
-                            hi[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if constexpr (SPLIT3) hi[512] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            float4 v[16];
+#pragma unroll
+                            for (int n = 0; n < 16; ++n) v[n] = blk[ct + 32 * n];
+#pragma unroll
+                            for (int n = 0; n < 16; ++n) blk[512 + ct + 32 * n] = tf32_lo4(v[n]);
                         }
-                        else if constexpr (SPLIT3)
-                            hi[512] = tf32_lo4(hi[0]);
+                    }
+                    else
+                    {
+                        for (int n = 0; n < 16; ++n)
+                        {
+                            const uint32_t i = ct + 32 * n, key = c * 32 + (i % 256) / 8;
+                            if (key >= valid)
+                            {
+                                blk[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                                if constexpr (SPLIT3) blk[512 + i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+                            else if constexpr (SPLIT3)
+                                blk[512 + i] = tf32_lo4(blk[i]);
+                        }
                     }
                 }
             }
