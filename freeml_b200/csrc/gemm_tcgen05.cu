@@ -6,14 +6,14 @@
 //   C[M x N]                = A[M x K] . B[K x N]          (BMN: B row-major)
 //
 // 128 x 128 output tiles, K staged 32 fp32 (one 128-byte row) at a time
-// through a 3-stage ring of TMA tensor loads (128-byte swizzle, each load into
+// through a 4-stage ring of TMA tensor loads (128-byte swizzle, each load into
 // this CTA only); a persistent CTA per SM walks the tiles with the
 // accumulator double-buffered in TMEM (2 x 128 lanes x 128 fp32 columns).
 // Warp roles (10 warps):
 //   warp 0      TMEM allocation; one thread issues the TMA loads
 //   warp 1      one thread issues tcgen05.mma and tcgen05.commit
-//   warps 2..5  TF32x3 split of each staged A tile (and of the B tile,
-//               unless B's lo part is given in memory)
+//   warps 2..5  TF32x3 split of each staged A tile into TMEM (and of the B
+//               tile into shared memory, unless B's lo part is given)
 //   warps 6..9  epilogue (tcgen05.ld of a finished accumulator, store to
 //               global with the fused GELU or residual add)
 //
@@ -22,7 +22,9 @@
 // cleared -- which is what the MMA reads from the staged tile itself, so hi
 // is never written -- and lo = x - hi (exact in fp32), then sums
 // hi*hi + hi*lo + lo*hi in the fp32 accumulator -- fp32-level results at
-// three MMAs per k-step.  TF32 (one MMA, hardware truncation) is the fast,
+// three MMAs per k-step.  A's lo part goes to TMEM (the lo.hi MMA reads its
+// A operand from there), which keeps a stage at three 16 KB tiles and the
+// ring four stages deep.  TF32 (one MMA, hardware truncation) is the fast,
 // looser mode.
 //
 // Every mbarrier wait is bounded; a wait that runs out sets the device error
@@ -39,9 +41,12 @@ __device__ int g_gemm_timeouts;
 namespace tc {
 
 constexpr int BM = 128, BN = 128;
-constexpr int STAGES = 3;
+constexpr int STAGES = 4;
 constexpr uint32_t TILE_BYTES = BM * BK * 4;  // 16 KB (A or B tile)
 constexpr uint32_t TMEM_COLS = 128;
+// TMEM: two 128-column accumulators, then A's TF32 lo part of each stage (32
+// columns: lane = A row, one column per k), the A operand of the lo.hi MMAs
+constexpr uint32_t ALO_COL = 2 * TMEM_COLS, TMEM_ALLOC = 512;
 constexpr uint32_t IDESC = idesc_tf32(BM, BN);
 constexpr uint32_t IDESC_BMN = IDESC | (1u << 16);  // B read MN-major (bit 16: "transpose B")
 constexpr uint32_t MN_BOX = 32;                      // n per 128-byte swizzle row of an MN-major B tile
@@ -69,6 +74,81 @@ __device__ __forceinline__ uint64_t smem_desc_mn(const void* tile, uint32_t kk)
     return start | (lbo << 16) | (sbo << 32) | (1ull << 46) | (1ull << 61);
 }
 
+// One stage's MMAs (BK / 8 = 4 K steps) and the commit that frees the stage,
+// in ONE asm block that first probes (mbarrier.test_wait, non-blocking) the
+// barrier of the next stage and reads the probe's answer only after the MMAs
+// are issued.  The tensor pipe's instruction queue is short, so a wait issued
+// between two stages -- even on a barrier already complete, ~170 cycles --
+// lets it drain; here the probe's latency overlaps the issue of the MMAs.
+// Descriptors advance per K step by a_step / b_step (16-byte units: 32 bytes
+// along a K-major row, 1 KB for the MN-major B).  Returns the probe's answer.
+// The lo.hi term reads A's lo part from TMEM (talo: 8 columns per K step).
+template <bool SPLIT3>
+__device__ __forceinline__ bool issue_stage_probe(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t talo,
+                                                  uint64_t dblo, uint32_t idesc, bool accumulate, uint64_t b_step,
+                                                  uint64_t* empty_bar, uint64_t* next_bar, uint32_t next_parity)
+{
+    uint32_t ready;
+    if constexpr (SPLIT3)
+    {
+        asm volatile(
+            "{\n\t"
+            ".reg .pred pr, pa, p1;\n\t"
+            ".reg .b64 a, b, bl;\n\t"
+            ".reg .b32 al;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 pr, [%1], %2;\n\t"
+            "setp.ne.b32 pa, %8, 0;\n\t"
+            "setp.eq.b32 p1, 0, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], %4, %5, %9, pa;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], %4, %7, %9, p1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], [%6], %5, %9, p1;\n\t"
+            "add.s64 a, %4, 2;\n\tadd.s64 b, %5, %10;\n\tadd.u32 al, %6, 8;\n\tadd.s64 bl, %7, %10;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, b, %9, p1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, bl, %9, p1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], [al], b, %9, p1;\n\t"
+            "add.s64 a, a, 2;\n\tadd.s64 b, b, %10;\n\tadd.u32 al, al, 8;\n\tadd.s64 bl, bl, %10;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, b, %9, p1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, bl, %9, p1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], [al], b, %9, p1;\n\t"
+            "add.s64 a, a, 2;\n\tadd.s64 b, b, %10;\n\tadd.u32 al, al, 8;\n\tadd.s64 bl, bl, %10;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, b, %9, p1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, bl, %9, p1;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], [al], b, %9, p1;\n\t"
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%11];\n\t"
+            "selp.u32 %0, 1, 0, pr;\n\t"
+            "}"
+            : "=r"(ready)
+            : "r"(smem_u32(next_bar)), "r"(next_parity), "r"(tmem_d), "l"(da), "l"(db), "r"(talo), "l"(dblo),
+              "r"((uint32_t)accumulate), "r"(idesc), "l"(b_step), "r"(smem_u32(empty_bar))
+            : "memory");
+    }
+    else
+    {
+        asm volatile(
+            "{\n\t"
+            ".reg .pred pr, pa, p1;\n\t"
+            ".reg .b64 a, b;\n\t"
+            "mbarrier.test_wait.parity.shared::cta.b64 pr, [%1], %2;\n\t"
+            "setp.ne.b32 pa, %6, 0;\n\t"
+            "setp.eq.b32 p1, 0, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], %4, %5, %7, pa;\n\t"
+            "add.s64 a, %4, 2;\n\tadd.s64 b, %5, %8;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, b, %7, p1;\n\t"
+            "add.s64 a, a, 2;\n\tadd.s64 b, b, %8;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, b, %7, p1;\n\t"
+            "add.s64 a, a, 2;\n\tadd.s64 b, b, %8;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%3], a, b, %7, p1;\n\t"
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%9];\n\t"
+            "selp.u32 %0, 1, 0, pr;\n\t"
+            "}"
+            : "=r"(ready)
+            : "r"(smem_u32(next_bar)), "r"(next_parity), "r"(tmem_d), "l"(da), "l"(db), "r"((uint32_t)accumulate),
+              "r"(idesc), "l"(b_step), "r"(smem_u32(empty_bar))
+            : "memory");
+    }
+    return ready != 0;
+}
+
 }  // namespace tc
 
 enum TcEpi { TC_STORE = 0, TC_GELU = 1, TC_RESID = 2 };
@@ -89,14 +169,16 @@ struct TcArgs
 // the MMAs of tile j + 1 run (measured against one CTA per tile, whose
 // tensor pipe idled while it filled its pipeline and drained its epilogue:
 // config 4 prefill 339 -> 320 ms).
-// Shared memory: STAGES x {A, B, A_lo, B_lo} tiles (1024-byte aligned), then
-// barriers and the TMEM base address.  BLO (TF32x3 only): B's lo part is
+// Shared memory: STAGES x {A, B, B_lo} tiles (1024-byte aligned), then
+// barriers and the TMEM base address.  TMEM: two accumulators and A_lo of
+// each stage.  BLO (TF32x3 only): B's lo part is
 // given in memory (map_blo, same geometry as map_b) and TMA-loaded into the
 // B_lo tile; the converters split A only.
 // Warp roles (10 warps):
 //   warp 0      TMEM allocation; one thread issues the TMA loads
 //   warp 1      one thread issues tcgen05.mma / tcgen05.commit
-//   warps 2..5  TF32x3 split of each staged A tile (relay only without split)
+//   warps 2..5  TF32x3 split of each staged A tile into TMEM, and of B
+//               without B_lo (relay only without split)
 //   warps 6..9  epilogue: tcgen05.ld of a finished accumulator, store
 // Barriers: full / conv / empty per stage (TMA landed / split done / MMAs have
 // read it), acc_full / acc_empty per accumulator (MMAs done / drained).
@@ -111,7 +193,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
     using namespace tc;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    constexpr int NT = SPLIT3 ? 4 : 2;  // tiles per stage
+    constexpr int NT = SPLIT3 ? 3 : 2;  // shared-memory tiles per stage: A, B (, B lo)
     unsigned char* tiles = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(tiles + STAGES * NT * TILE_BYTES);
     uint64_t* conv = full + STAGES;
@@ -145,7 +227,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
     if (warp == 0)
     {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(2 * TMEM_COLS)
+                     "r"(TMEM_ALLOC)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -180,7 +262,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
                     }
                     else
                         tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
-                    if constexpr (BLO) tma_load_2d(tile_ptr(s, 3), &map_blo, kb * BK, n0, &full[s]);
+                    if constexpr (BLO) tma_load_2d(tile_ptr(s, 2), &map_blo, kb * BK, n0, &full[s]);
                 }
             }
             // the last STAGES loads issued (all earlier ones were consumed):
@@ -193,7 +275,11 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
     {
         if (lane == 0)
         {
+            static_assert(BK == 32, "issue_stage_probe issues 4 K steps of 8");
             uint32_t it = 0, j = 0;  // k-blocks consumed, tiles accumulated
+            const uint32_t total = (uint32_t)kblocks * (uint32_t)((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) /
+                                                                  (int)gridDim.x);
+            bool ready = false;  // conv[it % STAGES] known complete (the previous stage's probe)
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++j)
             {
                 const uint32_t buf = j & 1u, use = j >> 1;
@@ -203,35 +289,27 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
                 for (int kb = 0; kb < kblocks; ++kb, ++it)
                 {
                     const int s = it % STAGES;
-                    if (!mbar_wait(&conv[s], (it / STAGES) & 1)) { ok = false; break; }
+                    if (!ready && !mbar_wait(&conv[s], (it / STAGES) & 1)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-                    for (int k = 0; k < BK / 8; ++k)  // K = 8 tf32 (32 bytes) per MMA
+                    // probe the next stage (the last one probes its own, already complete, barrier)
+                    const uint32_t nx = it + 1 < total ? it + 1 : it;
+                    const uint64_t da = smem_desc(tile_ptr(s, 0), 0);
+                    const uint32_t talo = tmem_base + ALO_COL + 32u * (uint32_t)s;
+                    uint64_t db, dblo;
+                    if constexpr (BMN)
                     {
-                        const uint32_t off = k * 32;
-                        const uint64_t da = smem_desc(tile_ptr(s, 0), off);
-                        if constexpr (BMN)
-                        {
-                            const uint64_t db = smem_desc_mn(tile_ptr(s, 1), k);
-                            tc::mma_tf32(acc_tmem, da, db, IDESC_BMN, kb > 0 || k > 0);
-                            if constexpr (SPLIT3)
-                            {
-                                tc::mma_tf32(acc_tmem, da, smem_desc_mn(tile_ptr(s, 3), k), IDESC_BMN, true);
-                                tc::mma_tf32(acc_tmem, smem_desc(tile_ptr(s, 2), off), db, IDESC_BMN, true);
-                            }
-                        }
-                        else
-                        {
-                            const uint64_t db = smem_desc(tile_ptr(s, 1), off);
-                            mma_tf32(acc_tmem, da, db, kb > 0 || k > 0);
-                            if constexpr (SPLIT3)
-                            {
-                                mma_tf32(acc_tmem, da, smem_desc(tile_ptr(s, 3), off), true);  // hi * lo
-                                mma_tf32(acc_tmem, smem_desc(tile_ptr(s, 2), off), db, true);  // lo * hi
-                            }
-                        }
+                        db = smem_desc_mn(tile_ptr(s, 1), 0);
+                        dblo = smem_desc_mn(tile_ptr(s, 2), 0);
                     }
-                    mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                    else
+                    {
+                        db = smem_desc(tile_ptr(s, 1), 0);
+                        dblo = smem_desc(tile_ptr(s, 2), 0);
+                    }
+                    ready = issue_stage_probe<SPLIT3>(acc_tmem, da, db, talo, dblo, BMN ? IDESC_BMN : IDESC, kb > 0,
+                                                      BMN ? 64u : 2u, &empty[s], &conv[nx % STAGES],
+                                                      (nx / STAGES) & 1);
+                    if (nx == it) ready = false;
                 }
                 if (!ok) break;
                 mma_commit(&acc_full[buf]);  // the accumulator is complete
@@ -241,8 +319,12 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
     }
     else if (warp < 6)
     {
-        // warps 2..5: split each staged A tile (and B's, without B_lo)
+        // warps 2..5: A's lo part into TMEM (thread = TMEM lane = A row: warp
+        // w may access lanes 32 (w % 4) ..), and B's into shared memory
+        // unless B_lo is given
         const int ct = threadIdx.x - 64;  // 0..127
+        const int r = 32 * (warp & 3) + lane;
+        const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
         uint32_t it = 0;
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
         {
@@ -252,23 +334,31 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
                 if (!__all_sync(FULL_MASK, mbar_wait(&full[s], (it / STAGES) & 1))) { ok = false; break; }
                 if constexpr (SPLIT3)
                 {
-                    for (int which = 0; which < (BLO ? 1 : 2); ++which)
+                    // row r of the A tile: logical 16-byte chunk c (k = 4c..)
+                    // at physical chunk c ^ (r % 8) (128-byte swizzle)
+                    const unsigned char* arow = tile_ptr(s, 0) + r * 128;
+                    uint32_t u[32];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
                     {
-                        const float4* x4 = reinterpret_cast<const float4*>(tile_ptr(s, which));
-                        float4* lo = reinterpret_cast<float4*>(tile_ptr(s, which + 2));
-                        for (int i = ct; i < (int)(TILE_BYTES / 16); i += 128)
-                        {
-                            const float4 x = x4[i];
-                            float4 l;
-                            l.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
-                            l.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
-                            l.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
-                            l.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
-                            lo[i] = l;
-                        }
+                        const float4 lo = tf32_lo4(*reinterpret_cast<const float4*>(arow + ((c ^ (r & 7)) * 16)));
+                        u[4 * c] = __float_as_uint(lo.x);
+                        u[4 * c + 1] = __float_as_uint(lo.y);
+                        u[4 * c + 2] = __float_as_uint(lo.z);
+                        u[4 * c + 3] = __float_as_uint(lo.w);
                     }
-                    // make these generic-proxy writes visible to the tensor core
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    tmem_st32(tmem_base + tlane + ALO_COL + 32u * (uint32_t)s, u);
+                    if constexpr (!BLO)
+                    {
+                        const float4* x4 = reinterpret_cast<const float4*>(tile_ptr(s, 1));
+                        float4* lo = reinterpret_cast<float4*>(tile_ptr(s, 2));
+#pragma unroll
+                        for (int i = ct; i < (int)(TILE_BYTES / 16); i += 128) lo[i] = tf32_lo4(x4[i]);
+                        // make these generic-proxy writes visible to the tensor core
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    }
+                    tmem_wait_st();
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&conv[s]);
@@ -349,7 +439,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
     if (warp == 0)
     {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_ALLOC)
                      : "memory");
     }
 }
@@ -360,7 +450,7 @@ template <bool SPLIT3, int EPI, bool BLO = false, bool BMN = false>
 static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo, const TcArgs& args,
                      cudaStream_t st)
 {
-    constexpr int NT = SPLIT3 ? 4 : 2;
+    constexpr int NT = SPLIT3 ? 3 : 2;
     const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 32 * 8;
     static uint64_t attr_devices = 0;
     FML_RC(smem_limit_once(reinterpret_cast<const void*>(gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN>), (int)smem,
