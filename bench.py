@@ -439,8 +439,7 @@ def main():
 
     def one_pass():
         lm.rewind(P, first)
-        for _ in range(steps_per_pass):
-            lm.step()
+        lm.steps(steps_per_pass)  # graphs of several engine steps each
 
     def barrier():
         if pg is not None:
@@ -547,8 +546,9 @@ def main():
             "config": dict(workload_config(ws, B, tp),
                            allreduce=("NCCL" if args.tp_nccl else "one-shot kernel over NVLink peer memory "
                                       "(decode; prefill: NCCL)") if tp else None,
-                           engine="per-operation kernels (CUDA graph, programmatic dependent launch); decode "
-                                  "contractions on tcgen05 (TF32x3) where the shape allows"),
+                           engine="per-operation kernels (CUDA graphs of 16 engine steps, programmatic "
+                                  "dependent launch between all kernels); decode contractions on the CUDA cores "
+                                  "(fp32), prefill contractions on tcgen05 (TF32x3)"),
             "gpu_launches": int(launches),
             "clocks": clocks,
             "roofline": {"bound": "hbm", "kernel": k_name,

@@ -94,6 +94,7 @@ SIGNATURES = {
     "fml_lm_load_checkpoint": (_I, [_P, ctypes.c_char_p, _P]),
     "fml_lm_prefill": (_I, [_P, _P, _U32, _U32, _P]),
     "fml_lm_step": (_I, [_P, _P, _P, _P]),
+    "fml_lm_steps": (_I, [_P, _U32, _P]),
     "fml_lm_step_host": (_I, [_P, _P, _P, _P]),
     "fml_lm_generate_host": (_I, [_P, _U32, _P, _P, _P]),
     "fml_lm_set_graph": (_I, [_P, _I]),

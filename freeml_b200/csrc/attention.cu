@@ -23,16 +23,18 @@ int timeline_bind_attention(TimelineRec* p, uint32_t cap) { return timeline_bind
 // (CausalSelfAttentionLayer.h:424-499: Q_h K_h^T, * 1/sqrt(hd) + causal
 // mask, Softmax, P V_h) as one pass with an online softmax.
 //
-// CTA = 4 warps on one (row, head, key split); grid = (heads, rows, splits).
+// CTA = NW warps (4 or 16) on one (row, head, key split); grid = (heads,
+// rows, splits).
 // Inside a warp, G = HD/4 lanes form a group that owns one key at a time,
 // each lane holding 4 dims (one float4 of the K row and of the V row), so a
 // score needs log2(G) shuffles and a warp covers 32/G keys per step.  Every
 // group keeps its own running max / sum / accumulator (no per-key
 // broadcast); U steps of K and V loads are issued before any is used, and a
-// thread stays under 64 registers so that 8 CTAs (32 warps) fit on an SM and
-// the loads of many warps overlap.  Groups, warps and then splits are merged
-// at the end; with S > 1 each CTA writes (m, l, acc) and the last CTA of the
-// (row, head) to finish merges the partials.
+// thread stays under 64 registers so that 32 warps (8 CTAs of 4, or 2 of 16)
+// fit on an SM and the loads of many warps overlap.  Groups, warps and then
+// splits are merged at the end; with S > 1 the splits of a (row, head) merge
+// through a cluster's shared memory, or each CTA writes (m, l, acc) and the
+// last CTA of the (row, head) to finish merges the partials.
 struct AttnUnit
 {
     uint32_t r, b, begin, end, nsplit;
@@ -80,16 +82,16 @@ __device__ __forceinline__ void softmax_merge(float& m, float& l, float4& acc, f
 // merged through distributed shared memory (cluster rank 0 reads every
 // split's (m, l, acc) after a cluster barrier) instead of through global
 // partials, a fence and a completion counter.
-template <int HD, bool CL>
-__global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
+template <int HD, int NW, bool CL>
+__global__ void __launch_bounds__(32 * NW, 32 / NW) attention_kernel(AttnArgs a)
 {
     FML_TIMELINE_SCOPE(20);
     const StampAtExit stamp_at_exit(a.stamp);
     constexpr int G = HD / 4;       // lanes per key
     constexpr int KPW = 32 / G;     // keys per warp step
     constexpr int U = 4;            // steps whose loads are in flight together
-    __shared__ float sm_m[4], sm_l[4];
-    __shared__ __align__(16) float sm_acc[4][HD];
+    __shared__ float sm_m[NW], sm_l[NW];
+    __shared__ __align__(16) float sm_acc[NW][HD];
     __shared__ int sm_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
     const AttnUnit cu = attention_unit(a, r, s);
     const float* K = a.kc + (uint64_t)cu.b * a.seq_stride + (uint64_t)h * a.C * HD + lig * 4;
     const float* V = a.vc + (uint64_t)cu.b * a.seq_stride + (uint64_t)h * a.C * HD + lig * 4;
-    constexpr uint32_t STEP = 4 * KPW;  // keys per CTA step (4 warps)
+    constexpr uint32_t STEP = NW * KPW;  // keys per CTA step (NW warps)
     const uint32_t last = cu.end > 0 ? cu.end - 1 : 0;
     const uint32_t kw0 = cu.begin + warp * KPW;
     const uint32_t newest = cu.newest;
@@ -216,18 +218,19 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
     if (grp == 0) *reinterpret_cast<float4*>(&sm_acc[warp][lig * 4]) = acc;
     __syncthreads();
 
-    // merge the 4 warps: thread e < HD owns output dim e
+    // merge the NW warps in warp order: thread e < HD owns output dim e
     const int e = tid;
-    const float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
-    float w4[4], L = 0.0f;
+    float M = sm_m[0];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 1; i < NW; ++i) M = fmaxf(M, sm_m[i]);
+    float L = 0.0f, A = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i)
     {
-        w4[i] = (sm_m[i] == -INFINITY) ? 0.0f : expf(sm_m[i] - M);
-        L += sm_l[i] * w4[i];
+        const float wi = (sm_m[i] == -INFINITY) ? 0.0f : expf(sm_m[i] - M);
+        L += sm_l[i] * wi;
+        if (e < HD) A += sm_acc[i][e] * wi;
     }
-    const float A = e < HD ? sm_acc[0][e] * w4[0] + sm_acc[1][e] * w4[1] + sm_acc[2][e] * w4[2] + sm_acc[3][e] * w4[3]
-                           : 0.0f;
     if constexpr (CL)
     {
         // every split pushes (acc, m, l) into cluster rank 0's shared memory;
@@ -298,6 +301,24 @@ __global__ void __launch_bounds__(128, 8) attention_kernel(AttnArgs a)
 template <int HD>
 static int launch_attention_hd(AttnArgs a, dim3 grid, cudaStream_t st, bool pdl)
 {
+    // warps per CTA: 16 with a quarter of the splits when that still gives
+    // every SM a CTA (one CTA then merges four splits' worth of warps in
+    // shared memory instead of four CTAs through a cluster), else 4.
+    // Measured on B200, config 3: 32 sequences (256 (row, head) pairs, 4
+    // splits) attention 10.1 -> 9.7 us per launch in the step graph; at 4
+    // and 1 sequences 16 warps lose (3.9 -> 5.4 us).  Tuning override:
+    // FML_ATTN_WARPS = 4 | 16.
+    int nw = (grid.z % 4 == 0 && (uint64_t)grid.x * grid.y * (grid.z / 4) >= 148) ? 16 : 4;
+    if (const char* e = getenv("FML_ATTN_WARPS"))
+    {
+        const long v = strtol(e, nullptr, 10);
+        if (v == 4 || (v == 16 && grid.z % 4 == 0)) nw = (int)v;
+    }
+    if (nw == 16)
+    {
+        grid.z /= 4;
+        a.S = grid.z;
+    }
     // 2..8 splits: one cluster per (row, head), merged on chip
     // (FML_ATTN_CLUSTER=0: global partials and a completion counter)
     const char* cl_env = getenv("FML_ATTN_CLUSTER");
@@ -306,7 +327,7 @@ static int launch_attention_hd(AttnArgs a, dim3 grid, cudaStream_t st, bool pdl)
     if (grid.x == 0 || grid.y == 0 || grid.z == 0) return FML_OK;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(32 * nw);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -327,8 +348,13 @@ static int launch_attention_hd(AttnArgs a, dim3 grid, cudaStream_t st, bool pdl)
     }
     cfg.attrs = attr;
     cfg.numAttrs = n;
-    const cudaError_t e = cl ? cudaLaunchKernelEx(&cfg, attention_kernel<HD, true>, a)
-                             : cudaLaunchKernelEx(&cfg, attention_kernel<HD, false>, a);
+    cudaError_t e;
+    if (nw == 16)
+        e = cl ? cudaLaunchKernelEx(&cfg, attention_kernel<HD, 16, true>, a)
+               : cudaLaunchKernelEx(&cfg, attention_kernel<HD, 16, false>, a);
+    else
+        e = cl ? cudaLaunchKernelEx(&cfg, attention_kernel<HD, 4, true>, a)
+               : cudaLaunchKernelEx(&cfg, attention_kernel<HD, 4, false>, a);
     if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
     FML_LAUNCH_CHECK();
     return FML_OK;

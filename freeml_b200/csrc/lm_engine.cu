@@ -28,6 +28,7 @@
 //   attention (split-KV, last CTA combines) -> proj gemv (+residual) ->
 //   layernorm -> fc gemv (+gelu) -> mlp gemv (+residual) } -> layernorm ->
 //   lm_head gemv (+argmax keys) -> finalize
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -754,6 +755,7 @@ __global__ void finalize_kernel(unsigned long long* keys, uint32_t* pending, uin
                                 uint32_t B, uint32_t set_pos, uint32_t* epoch, StepStamp stamp, uint32_t* stamp_ctr)
 {
     FML_TIMELINE_SCOPE(30);
+    griddep_launch_dependents();
     griddep_wait();
     FML_TIMELINE_MARK(1);
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -893,6 +895,12 @@ struct fml_lm
     // tokens) as one graph: one launch per step instead of three calls
     cudaGraphExec_t host_graph_exec = nullptr;
     uint32_t host_graph_batch = 0;
+    // several steps as one graph (fml_lm_steps): no launch gap between the
+    // steps it holds, and each step's embed overlaps the previous finalize
+    // (steps per graph, graph) for the current batch: the main size and the
+    // remainder of a call
+    std::vector<std::pair<uint32_t, cudaGraphExec_t>> multi_graphs;
+    uint32_t multi_graph_batch = 0;
 
     // profiling
     bool profiling = false;
@@ -918,6 +926,8 @@ void drop_graphs(fml_lm* lm)
     lm->graph_exec = nullptr;
     if (lm->host_graph_exec) cudaGraphExecDestroy(lm->host_graph_exec);
     lm->host_graph_exec = nullptr;
+    for (auto& g : lm->multi_graphs) cudaGraphExecDestroy(g.second);
+    lm->multi_graphs.clear();
 }
 
 void free_all(fml_lm* lm)
@@ -1229,7 +1239,11 @@ int gemv_allreduce(fml_lm* lm, GemvArgs a, float* y, const float* resid, uint32_
 // fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
 // finalize.  Every launch after the first uses programmatic dependent launch.
 // ids: the tokens the step consumes (default: the pending tokens).
-int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st, const uint32_t* ids = nullptr)
+// chained: the previous kernel on `st` is this engine's finalize of the
+// previous step (captured in the same graph), so the embed may launch under
+// programmatic dependent launch too.
+int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st, const uint32_t* ids = nullptr,
+                 bool chained = false)
 {
     const fml_lm_config& c = lm->cfg;
     const uint32_t B = lm->batch, d = c.d_model;
@@ -1239,7 +1253,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
     lm->stamp_class.clear();
     {
         ProfScope ps(lm, 0, st);
-        FML_RC(launch_k(embed_kernel, dim3(B), dim3(128), st, false, lm->x, (const float*)lm->tok,
+        FML_RC(launch_k(embed_kernel, dim3(B), dim3(128), st, chained && pdl && lm->tp_world == 1, lm->x,
+                        (const float*)lm->tok,
                         (const float*)lm->pos_emb, ids ? ids : (const uint32_t*)lm->pending, (const uint32_t*)lm->pos,
                         B, 1u, d, c.vocab, c.context, lm->grab, c.n_layer, next_stamp(lm, 0)));
     }
@@ -1912,6 +1927,28 @@ int record_step(fml_lm* lm, uint32_t* next_tokens, float* logits, bool host_io, 
     return FML_OK;
 }
 
+// Record `n` consecutive steps (no outputs: each step leaves its tokens
+// pending on the device) into one executable graph.
+int record_steps(fml_lm* lm, uint32_t n, cudaGraphExec_t* out)
+{
+    *out = nullptr;
+    cudaStream_t cap;
+    FML_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+    FML_CUDA_TRY(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
+    int rc = FML_OK;
+    for (uint32_t i = 0; i < n && rc == FML_OK; ++i) rc = enqueue_step(lm, nullptr, nullptr, cap, nullptr, i > 0);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(cap, &g);
+    cudaStreamDestroy(cap);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    launch_counter().fetch_sub((uint64_t)n * graph_nodes_per_step(lm), std::memory_order_relaxed);
+    return FML_OK;
+}
+
 // Enqueue one host-buffer step: tokens from host_io[0, B) in, the next
 // tokens to host_io[max_batch, max_batch + B) out (read after a sync).
 int enqueue_step_host(fml_lm* lm, cudaStream_t st)
@@ -1969,6 +2006,60 @@ int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t s
         if (lm->profiling) FML_RC(collect_profile(lm));
     }
     for (uint32_t b = 0; b < lm->batch; ++b) lm->hpos[b] += 1;
+    return FML_OK;
+}
+
+int fml_lm_steps(fml_lm* lm, uint32_t n, fml_stream_t stream)
+{
+    FML_REQUIRE(lm, "fml_lm_steps: null engine");
+    if (n == 0) return FML_OK;
+    FML_RC(check_step_state(lm, "fml_lm_steps"));
+    for (uint32_t b = 0; b < lm->batch; ++b)
+        if (lm->hpos[b] + n > lm->cfg.context)
+            return set_error(FML_ERR_STATE, "fml_lm_steps: %u steps take sequence %u past the context limit (%u)", n,
+                             b, lm->cfg.context);
+    cudaStream_t st = as_stream(stream);
+    if (!lm->use_graph || lm->profiling)
+    {
+        for (uint32_t i = 0; i < n; ++i) FML_RC(fml_lm_step(lm, nullptr, nullptr, stream));
+        return FML_OK;
+    }
+    // graphs of G steps (FML_LM_GRAPH_STEPS, default 16), then one graph of
+    // the remaining n mod G steps
+    uint32_t G = 16;
+    if (const char* e = getenv("FML_LM_GRAPH_STEPS"))
+    {
+        const long v = strtol(e, nullptr, 10);
+        if (v >= 1 && v <= 256) G = (uint32_t)v;
+    }
+    if (lm->multi_graph_batch != lm->batch)
+    {
+        for (auto& g : lm->multi_graphs) cudaGraphExecDestroy(g.second);
+        lm->multi_graphs.clear();
+        lm->multi_graph_batch = lm->batch;
+    }
+    auto graph_of = [&](uint32_t k, cudaGraphExec_t* out) -> int {
+        for (auto& g : lm->multi_graphs)
+            if (g.first == k) { *out = g.second; return FML_OK; }
+        if (lm->multi_graphs.size() >= 4)  // keep a few sizes only
+        {
+            cudaGraphExecDestroy(lm->multi_graphs.front().second);
+            lm->multi_graphs.erase(lm->multi_graphs.begin());
+        }
+        FML_RC(record_steps(lm, k, out));
+        lm->multi_graphs.emplace_back(k, *out);
+        return FML_OK;
+    };
+    for (uint32_t done = 0; done < n;)
+    {
+        const uint32_t k = std::min(G, n - done);
+        cudaGraphExec_t ge = nullptr;
+        FML_RC(graph_of(k, &ge));
+        FML_CUDA_TRY(cudaGraphLaunch(ge, st));
+        launch_counter().fetch_add((uint64_t)k * graph_nodes_per_step(lm), std::memory_order_relaxed);
+        for (uint32_t b = 0; b < lm->batch; ++b) lm->hpos[b] += k;
+        done += k;
+    }
     return FML_OK;
 }
 

@@ -113,6 +113,11 @@ class NanoLM:
         call("fml_lm_step", self._h, self._next.data_ptr(), logits_ptr, self._stream())
         return self._next[: self.batch], (self._logits[: self.batch] if want_logits else None)
 
+    def steps(self, n: int) -> None:
+        """n greedy steps on device (multi-step graphs); the last tokens stay
+        pending (pending_tokens())."""
+        call("fml_lm_steps", self._h, n, self._stream())
+
     def vocab_slice(self):
         """(first row, rows) of the vocabulary this engine's logits cover:
         all of it, or the rank's share under tensor parallelism."""

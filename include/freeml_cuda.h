@@ -408,6 +408,16 @@ FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
  * just computed.  All work is enqueued on `stream`; nothing synchronises. */
 FML_API int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t stream);
 
+/* `n` decode steps for every active sequence, each token left pending on the
+ * device for the next (read them with fml_lm_pending).  With graphs on, the
+ * steps replay as graphs of several steps each (FML_LM_GRAPH_STEPS, default
+ * 16): no launch gap between the steps a graph holds, and each step's first
+ * kernel starts under programmatic dependent launch while the previous
+ * step's last one finishes.  The decode loop of NanoLLM.cpp:189-204 run n
+ * times (one Model::Run and argmax per token there).  Fails before any work
+ * if a sequence would pass the context. */
+FML_API int fml_lm_steps(fml_lm* lm, uint32_t n, fml_stream_t stream);
+
 /* The same step through host memory, the way a host caller drives the loop:
  * `tokens_in` (host, [batch]) go to the device, the step runs, the next
  * tokens come back into `tokens_out` (host) and the call waits for them.

@@ -163,6 +163,42 @@ def test_graph_and_eager_steps_are_identical(golden):
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
 
 
+@pytest.mark.parametrize("graph_steps", ["16", "5"])
+def test_multi_step_graphs_match_single_steps(graph_steps, monkeypatch):
+    """fml_lm_steps (several decode steps per graph, each step's embed under
+    programmatic dependent launch behind the previous finalize) leaves the
+    same KV cache, positions and pending tokens as one fml_lm_step per token:
+    the step after them gives bit-identical tokens and logits.  37 steps =
+    graphs of 16 + 16 + 5 (or 5 x 7 + 2): full and remainder graphs."""
+    monkeypatch.setenv("FML_LM_GRAPH_STEPS", graph_steps)
+    from freeml_b200.lm import CONFIGS, NanoLM, prompt_tokens, random_params
+    c = CONFIGS[3]
+    s = c["shape"]
+    params = random_params(s, c["wseed"], 0)
+    prompts = prompt_tokens(c["pseed"], s.vocab, 8, c["prompt"])
+    lm = NanoLM(s, 8)
+    lm.bind(params)
+    lm.prefill(prompts)
+    first = lm.pending_tokens().clone()
+    outs = []
+    for multi in (True, False):
+        lm.rewind(c["prompt"], first)
+        if multi:
+            lm.steps(37)
+        else:
+            for _ in range(37):
+                lm.step()
+        pend = lm.pending_tokens().clone()
+        toks, logits = lm.step(want_logits=True)
+        outs.append((pend.cpu().numpy(), toks.cpu().numpy().copy(), logits.cpu().numpy().copy(),
+                     lm.position(0), lm.position(7)))
+    lm.close()
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    np.testing.assert_array_equal(outs[0][2].view(np.uint32), outs[1][2].view(np.uint32))
+    assert outs[0][3:] == outs[1][3:] == (c["prompt"] + 38, c["prompt"] + 38)
+
+
 def test_host_step_matches_device_step(golden):
     meta, g, _ = golden
     m = meta["greedy"]["cfg1"]
