@@ -45,6 +45,13 @@ def weight_bytes(d: int, L: int, vocab: int, tpw: int = 1) -> int:
     return 4 * (L * (4 * d * dl + 2 * d * fl) + vl * d + (2 * L + 1) * d)
 
 
+def weight_bytes_bf16(d: int, L: int, vocab: int, tpw: int = 1) -> int:
+    """weight_bytes with the decode GEMVs' matrices and the lm_head rows at
+    2 bytes (the bf16-weight mode); the LayerNorm gammas stay fp32."""
+    dl, fl, vl = d // tpw, 4 * d // tpw, -(-vocab // tpw)
+    return 2 * (L * (4 * d * dl + 2 * d * fl) + vl * d) + 4 * (2 * L + 1) * d
+
+
 def decode_pass_bytes(d: int, L: int, vocab: int, B: int, P: int, steps: int, tpw: int = 1) -> int:
     """Bytes of one decode pass of B sequences from key length P: every step
     reads the weights once, each sequence's cached K and V rows (p + 1 keys of
@@ -520,13 +527,31 @@ def main():
     e2e_s = max_over_ranks(time.perf_counter() - t0, pg, "cuda")
     e2e_value = dp * B * steps_per_pass * e2e_passes / e2e_s
 
+    # ---- the same decode passes with bf16 weights (fml_lm_set_weight_format):
+    # a separate figure with its own byte count, not the fp32 headline ----
+    d, L = s.d_model, s.n_layer
+    tpw = ws if tp else 1
+    bf_passes = max(1, min(args.steps, 5))
+    lm.set_weight_format("bf16")
+    one_pass()  # makes the bf16 copy and records the graphs
+    barrier()
+    torch.cuda.synchronize()
+    bf0, bf1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    bf0.record(stream)
+    for _ in range(bf_passes):
+        one_pass()
+    bf1.record(stream)
+    torch.cuda.synchronize()
+    bf_ms = max_over_ranks(bf0.elapsed_time(bf1), pg, "cuda") / bf_passes
+    lm.set_weight_format("fp32")
+    bf_bytes = decode_pass_bytes(d, L, s.vocab, B, P, steps_per_pass, tpw) - steps_per_pass * (
+        weight_bytes(d, L, s.vocab, tpw) - weight_bytes_bf16(d, L, s.vocab, tpw))
+
     # ---- per-kernel times inside the replayed step graph (the timed code
     # path, with programmatic dependent launch): one more pass with
     # completion stamps, every kernel's CTAs stamping the global timer ----
-    d, L = s.d_model, s.n_layer
     peak, peak_kind = hbm_peak()
-    tpw = ws if tp else 1  # this rank's share of the weights and heads
-    dl = d // tpw
+    dl = d // tpw  # this rank's share of the weights and heads
     step_bytes = decode_pass_bytes(d, L, s.vocab, B, P, steps_per_pass, tpw)
     pass_ms = ms_max / args.steps
     stamps, classes = lm.stamped_pass(one_pass, steps_per_pass)
@@ -573,6 +598,12 @@ def main():
                         "math": "TF32x3 on tcgen05 (three kind::tf32 MMAs per product, fp32 accumulate in TMEM)",
                         "frac_of_tf32x3_peak": prefill_flop / (prefill_ms / 1e3) / 1e12 / (tensor_peak() / 2 / 3),
                         "peak_note": "tf32 dense = half the measured bf16 peak, / 3 for the three-pass split"},
+            "bf16_weights": {"tokens_per_s": dp * B * steps_per_pass / (bf_ms / 1e3), "ms_per_pass": bf_ms,
+                             "algorithmic_bytes_per_pass": bf_bytes,
+                             "step_frac": bf_bytes / (bf_ms / 1e3) / 1e9 / peak,
+                             "note": "decode GEMVs stream bf16 copies of the weights (fp32 accumulate); prefill, "
+                                     "embedding, gammas and K/V cache fp32; a separate mode with a looser logits "
+                                     "bound, not the fp32 headline"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * B * dp * steps_per_pass,
                     "d2h_bytes_per_step": 4 * B * dp * steps_per_pass,
                     "path": "fml_lm_generate_host (host token buffers: every engine step copies its tokens "

@@ -17,6 +17,7 @@ STATUS_NAMES = {1: "FML_ERR_INVALID", 2: "FML_ERR_CUDA", 3: "FML_ERR_NOMEM", 4: 
                 5: "FML_ERR_STATE"}
 
 FML_MATH_FP32, FML_MATH_TF32X3, FML_MATH_TF32 = 0, 1, 2
+FML_WEIGHTS_FP32, FML_WEIGHTS_BF16 = 0, 1
 FML_LM_NCLASS = 10
 PROFILE_CLASSES = ["embed", "layernorm", "qkv", "attention", "proj", "fc", "mlp", "lm_head", "finalize",
                    "allreduce"]
@@ -95,6 +96,7 @@ SIGNATURES = {
     "fml_lm_prefill": (_I, [_P, _P, _U32, _U32, _P]),
     "fml_lm_step": (_I, [_P, _P, _P, _P]),
     "fml_lm_steps": (_I, [_P, _U32, _P]),
+    "fml_lm_set_weight_format": (_I, [_P, _I]),
     "fml_lm_step_host": (_I, [_P, _P, _P, _P]),
     "fml_lm_generate_host": (_I, [_P, _U32, _P, _P, _P]),
     "fml_lm_set_graph": (_I, [_P, _I]),

@@ -32,9 +32,11 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <utility>
 #include <vector>
 
+#include <cuda_bf16.h>
 #include <nccl.h>
 
 #include "attention.cuh"
@@ -139,10 +141,24 @@ __device__ __forceinline__ float4 ldw(const float* p)
     return v;
 }
 
+// Eight bf16 weights packed in a 16-byte load (element i in bits
+// [16 (i % 2), 16 (i % 2) + 16) of word i / 2), widened to fp32 exactly.
+__device__ __forceinline__ void bf16x8_to_f32(const float4& w, float (&f)[8])
+{
+    const uint32_t u[4] = {__float_as_uint(w.x), __float_as_uint(w.y), __float_as_uint(w.z), __float_as_uint(w.w)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        f[2 * i] = __uint_as_float(u[i] << 16);
+        f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+    }
+}
+
 struct GemvArgs
 {
     const float* x;  // [M x K], row stride ldx
     const float* w;  // [N x K]
+    const uint16_t* wb;  // the same weights as bf16 (read instead of w by the WB kernels)
     uint32_t M, N, K, ldx;
     float* y;        // [M x N], row stride ldy
     uint32_t ldy;
@@ -177,12 +193,14 @@ struct GemvArgs
 // finishes.  Partial sums are combined by a warp transpose-reduce (each lane
 // ends up owning distinct outputs) and a 4-way shared-memory sum; the
 // epilogue runs on one thread per output.
-template <int MT, int EPI, bool LN>
+template <int MT, int EPI, bool LN, bool WB>
 __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
 {
     FML_TIMELINE_SCOPE(10 + EPI);
     const StampAtExit stamp_at_exit(a.stamp);
     constexpr int NW = 4;
+    constexpr uint32_t KV = WB ? 8u : 4u;  // k values per 16-byte W load
+    constexpr uint32_t KSTEP = 128u * KV;  // k the CTA covers per iteration
     constexpr int CNT = MT * NW;
     constexpr int R = CNT >= 32 ? CNT / 32 : 1;
     constexpr int RM = MT >= 32 ? MT / 32 : 1;
@@ -193,21 +211,26 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t n0 = blockIdx.y * NW;
     const uint32_t m0 = blockIdx.x * MT;
-    const uint32_t k_first = (uint32_t)tid * 4u;
+    const uint32_t k_first = (uint32_t)tid * 4u;    // x rows (LayerNorm statistics; fp32 W slice)
+    const uint32_t kw_first = (uint32_t)tid * KV;   // this thread's W slice
+    // W rows: fp32 (a.w) or bf16 (a.wb) elements
+    using WT = std::conditional_t<WB, uint16_t, float>;
+    const WT* wbase = WB ? reinterpret_cast<const WT*>(a.wb) : reinterpret_cast<const WT*>(a.w);
+    auto wptr = [](const WT* row, uint32_t k) { return reinterpret_cast<const float*>(row + k); };
 
-    const float* wrow[NW];
+    const WT* wrow[NW];
 #pragma unroll
-    for (int j = 0; j < NW; ++j) wrow[j] = a.w + (uint64_t)min(blockIdx.y * NW + j, a.N - 1) * a.K;
+    for (int j = 0; j < NW; ++j) wrow[j] = wbase + (uint64_t)min(blockIdx.y * NW + j, a.N - 1) * a.K;
     // row pointers clamped into range: loads stay unconditional and in bounds
     const float* xrow[MT];
 #pragma unroll
     for (int m = 0; m < MT; ++m) xrow[m] = a.x + (uint64_t)min(m0 + m, a.M - 1) * a.ldx;
 
     float4 wv[NW];
-    const bool have_first = k_first < a.K;
+    const bool have_first = kw_first < a.K;
 #pragma unroll
     for (int j = 0; j < NW; ++j)
-        wv[j] = have_first ? ldw(wrow[j] + k_first) : make_float4(0, 0, 0, 0);
+        wv[j] = have_first ? ldw(wptr(wrow[j], kw_first)) : make_float4(0, 0, 0, 0);
 
     griddep_launch_dependents();
     griddep_wait();
@@ -281,42 +304,98 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
         for (int i = 0; i < CNT; ++i) acc[i] = 0.0f;
 
         // the W slice for the next k is requested as soon as this one is used
-        for (uint32_t k = k_first; k < a.K; k += 512u)
+        if constexpr (WB)
         {
-            float4 xv[MT];
-#pragma unroll
-            for (int m = 0; m < MT; ++m) xv[m] = *reinterpret_cast<const float4*>(xrow[m] + k);
-            if constexpr (LN)
+            for (uint32_t k = kw_first; k < a.K; k += KSTEP)
             {
-                const float4 gm = *reinterpret_cast<const float4*>(a.gamma + k);
+                float4 xv[MT][2];  // x[m][k .. k + 7]
 #pragma unroll
                 for (int m = 0; m < MT; ++m)
-                {
-                    const float mu = s_mean[m], rs = s_rstd[m];
-                    xv[m].x = (xv[m].x - mu) * rs * gm.x;
-                    xv[m].y = (xv[m].y - mu) * rs * gm.y;
-                    xv[m].z = (xv[m].z - mu) * rs * gm.z;
-                    xv[m].w = (xv[m].w - mu) * rs * gm.w;
-                }
-            }
 #pragma unroll
-            for (int m = 0; m < MT; ++m)
-            {
+                    for (int q = 0; q < 2; ++q) xv[m][q] = *reinterpret_cast<const float4*>(xrow[m] + k + 4 * q);
+                if constexpr (LN)
+                {
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+                    {
+                        const float4 gm = *reinterpret_cast<const float4*>(a.gamma + k + 4 * q);
+#pragma unroll
+                        for (int m = 0; m < MT; ++m)
+                        {
+                            const float mu = s_mean[m], rs = s_rstd[m];
+                            xv[m][q].x = (xv[m][q].x - mu) * rs * gm.x;
+                            xv[m][q].y = (xv[m][q].y - mu) * rs * gm.y;
+                            xv[m][q].z = (xv[m][q].z - mu) * rs * gm.z;
+                            xv[m][q].w = (xv[m][q].w - mu) * rs * gm.w;
+                        }
+                    }
+                }
 #pragma unroll
                 for (int j = 0; j < NW; ++j)
                 {
-                    float sacc = acc[m * NW + j];
-                    sacc = fmaf(xv[m].x, wv[j].x, sacc);
-                    sacc = fmaf(xv[m].y, wv[j].y, sacc);
-                    sacc = fmaf(xv[m].z, wv[j].z, sacc);
-                    sacc = fmaf(xv[m].w, wv[j].w, sacc);
-                    acc[m * NW + j] = sacc;
+                    float wf[8];
+                    bf16x8_to_f32(wv[j], wf);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                    {
+                        float sacc = acc[m * NW + j];
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+                        {
+                            sacc = fmaf(xv[m][q].x, wf[4 * q + 0], sacc);
+                            sacc = fmaf(xv[m][q].y, wf[4 * q + 1], sacc);
+                            sacc = fmaf(xv[m][q].z, wf[4 * q + 2], sacc);
+                            sacc = fmaf(xv[m][q].w, wf[4 * q + 3], sacc);
+                        }
+                        acc[m * NW + j] = sacc;
+                    }
+                }
+                if (k + KSTEP < a.K)
+                {
+#pragma unroll
+                    for (int j = 0; j < NW; ++j) wv[j] = ldw(wptr(wrow[j], k + KSTEP));
                 }
             }
-            if (k + 512u < a.K)
+        }
+        else
+        {
+            for (uint32_t k = k_first; k < a.K; k += 512u)
             {
+                float4 xv[MT];
 #pragma unroll
-                for (int j = 0; j < NW; ++j) wv[j] = ldw(wrow[j] + k + 512u);
+                for (int m = 0; m < MT; ++m) xv[m] = *reinterpret_cast<const float4*>(xrow[m] + k);
+                if constexpr (LN)
+                {
+                    const float4 gm = *reinterpret_cast<const float4*>(a.gamma + k);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                    {
+                        const float mu = s_mean[m], rs = s_rstd[m];
+                        xv[m].x = (xv[m].x - mu) * rs * gm.x;
+                        xv[m].y = (xv[m].y - mu) * rs * gm.y;
+                        xv[m].z = (xv[m].z - mu) * rs * gm.z;
+                        xv[m].w = (xv[m].w - mu) * rs * gm.w;
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < MT; ++m)
+                {
+#pragma unroll
+                    for (int j = 0; j < NW; ++j)
+                    {
+                        float sacc = acc[m * NW + j];
+                        sacc = fmaf(xv[m].x, wv[j].x, sacc);
+                        sacc = fmaf(xv[m].y, wv[j].y, sacc);
+                        sacc = fmaf(xv[m].z, wv[j].z, sacc);
+                        sacc = fmaf(xv[m].w, wv[j].w, sacc);
+                        acc[m * NW + j] = sacc;
+                    }
+                }
+                if (k + 512u < a.K)
+                {
+#pragma unroll
+                    for (int j = 0; j < NW; ++j) wv[j] = ldw(wptr(wrow[j], k + 512u));
+                }
             }
         }
 
@@ -326,8 +405,8 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a)
 #pragma unroll
             for (int j = 0; j < NW; ++j)
             {
-                wrow[j] = a.w + (uint64_t)min(gnext * NW + j, a.N - 1) * a.K;
-                wv[j] = have_first ? ldw(wrow[j] + k_first) : make_float4(0, 0, 0, 0);
+                wrow[j] = wbase + (uint64_t)min(gnext * NW + j, a.N - 1) * a.K;
+                wv[j] = have_first ? ldw(wptr(wrow[j], kw_first)) : make_float4(0, 0, 0, 0);
             }
         }
 
@@ -428,7 +507,7 @@ __device__ __forceinline__ void team_sync(uint32_t id, uint32_t n)
 // griddepcontrol.wait.  Measured against the one-group-per-CTA layout (every
 // output a 128-thread reduction, the LayerNorm redone per column group):
 // the per-group instruction count, not memory, bounded that kernel.
-template <int MT, int KW, int EPI, bool LN>
+template <int MT, int KW, int EPI, bool LN, bool WB>
 __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
 {
     FML_TIMELINE_SCOPE(10 + EPI);
@@ -437,7 +516,8 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
     constexpr int CNT = MT * NW;       // sums per lane (16 or 32)
     constexpr int TEAMS = 4 / KW;
     constexpr int SB = FML_GEMV_SB;    // W slices in flight per lane
-    constexpr uint32_t KSTEP = 128u * KW;  // K covered by one slice of the team
+    constexpr uint32_t KV = WB ? 8u : 4u;  // k values per 16-byte W slice (fp32 or bf16 weights)
+    constexpr uint32_t KSTEP = 32u * KV * KW;  // K covered by one slice of the team
     static_assert(CNT == 16 || CNT == 32, "MT must be 4 or 8");
     extern __shared__ __align__(16) float xs[];  // [MT][K] x rows, then (LN) gamma [K]
     __shared__ float red[2][TEAMS][KW][CNT];
@@ -446,7 +526,7 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
     const int team = warp / KW, kw = warp % KW;
     const uint32_t m0 = blockIdx.x * MT;
     const uint32_t K = a.K;
-    const uint32_t k_lane = 4u * (32u * kw + lane);
+    const uint32_t k_lane = KV * (32u * kw + lane);
     const uint32_t S = (K + KSTEP - 1) / KSTEP;          // slices per lane
     const uint32_t nchunk = (S + SB - 1) / SB;
     const uint32_t ngroups = (a.N + NW - 1) / NW;
@@ -461,7 +541,14 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
         const bool ok = gg < ngroups && s < S && k < K;
 #pragma unroll
         for (int j = 0; j < NW; ++j)
-            wv[b][j] = ok ? ldw(a.w + (uint64_t)min(gg * NW + j, a.N - 1) * K + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        {
+            if constexpr (WB)
+                wv[b][j] = ok ? ldw(reinterpret_cast<const float*>(a.wb + (uint64_t)min(gg * NW + j, a.N - 1) * K + k))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            else
+                wv[b][j] = ok ? ldw(a.w + (uint64_t)min(gg * NW + j, a.N - 1) * K + k)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     };
 #pragma unroll
     for (int b = 0; b < SB; ++b) load_slot(b, g, b);
@@ -572,7 +659,44 @@ __global__ void __launch_bounds__(128) gemv_team_kernel(GemvArgs a)
             {
                 const uint32_t s = c * SB + b;
                 const uint32_t k = k_lane + s * KSTEP;
-                if (s < S && k < K)
+                if constexpr (WB)
+                {
+                  if (s < S && k < K)
+                  {
+                    // eight bf16 weights per slot, widened to fp32 (exactly)
+                    float wf[NW][8];
+#pragma unroll
+                    for (int j = 0; j < NW; ++j) bf16x8_to_f32(wv[b][j], wf[j]);
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                    {
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+                        {
+                            const float4 xv = *reinterpret_cast<const float4*>(xs + (uint64_t)m * K + k + 4 * q);
+#pragma unroll
+                            for (int j = 0; j < NW; ++j)
+                            {
+#if FML_GEMV_F2
+                                float2 t = acc2[m * NW + j];
+                                t = __ffma2_rn(make_float2(xv.x, xv.y), make_float2(wf[j][4 * q], wf[j][4 * q + 1]), t);
+                                t = __ffma2_rn(make_float2(xv.z, xv.w), make_float2(wf[j][4 * q + 2], wf[j][4 * q + 3]),
+                                               t);
+                                acc2[m * NW + j] = t;
+#else
+                                float t = acc[m * NW + j];
+                                t = fmaf(xv.x, wf[j][4 * q], t);
+                                t = fmaf(xv.y, wf[j][4 * q + 1], t);
+                                t = fmaf(xv.z, wf[j][4 * q + 2], t);
+                                t = fmaf(xv.w, wf[j][4 * q + 3], t);
+                                acc[m * NW + j] = t;
+#endif
+                            }
+                        }
+                    }
+                  }
+                }
+                else if (s < S && k < K)
                 {
 #pragma unroll
                     for (int m = 0; m < MT; ++m)
@@ -792,6 +916,13 @@ __global__ void transpose_kernel(float* __restrict__ out, const float* __restric
     }
 }
 
+// bf16 copy of fp32 weights, rounded to nearest even.
+__global__ void to_bf16_kernel(uint16_t* __restrict__ out, const float* __restrict__ in, uint64_t n)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(in[i]));
+}
+
 __global__ void rewind_kernel(uint32_t* pos, uint32_t* pending, const uint32_t* src, uint32_t B, uint32_t p)
 {
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -835,6 +966,14 @@ struct fml_lm
     std::vector<float*> wqkv_lo, wproj_lo, wfc_lo, wmlp_lo;
     float *tok = nullptr, *pos_emb = nullptr, *lnf = nullptr;
     std::vector<float*> ln0, ln1, wqkv, wproj, wfc, wmlp;
+    // FML_WEIGHTS_BF16: the decode step's GEMVs stream a bf16 copy of their
+    // weights (layer matrices and the lm_head's vocabulary rows), made after
+    // each bind before the next step; the prefill keeps the fp32 weights
+    int weight_format = FML_WEIGHTS_FP32;
+    uint16_t* wb16 = nullptr;
+    bool wb16_valid = false;
+    std::vector<const uint16_t*> wqkv_b, wproj_b, wfc_b, wmlp_b;
+    const uint16_t* head_b = nullptr;
 
     // KV cache
     float *kc = nullptr, *vc = nullptr;
@@ -943,6 +1082,8 @@ void free_all(fml_lm* lm)
     for (cudaEvent_t e : lm->ev_pool) cudaEventDestroy(e);
     if (lm->wlo) cudaFree(lm->wlo);
     lm->wlo = nullptr;
+    if (lm->wb16) cudaFree(lm->wb16);
+    lm->wb16 = nullptr;
     void* ptrs[] = {lm->wbuf, lm->kc,  lm->vc,      lm->x,          lm->buf,  lm->ln,   lm->q,
                     lm->att,  lm->tmp, lm->hid,     lm->pending,    lm->pos,  lm->keys, lm->part,
                     lm->counters, lm->prompt_dev, lm->grab, lm->stamp_step};
@@ -1024,21 +1165,22 @@ int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, boo
 }
 
 // Resident CTAs per SM of a gemv instantiation (cached per instantiation).
-template <int MT, int EPI, bool LN>
+template <int MT, int EPI, bool LN, bool WB>
 int gemv_blocks_per_sm()
 {
     static int n = 0;
     if (!n)
     {
         int b = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, gemv_kernel<MT, EPI, LN>, 128, 0) != cudaSuccess || b < 1)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, gemv_kernel<MT, EPI, LN, WB>, 128, 0) != cudaSuccess ||
+            b < 1)
             b = 1;
         n = b;
     }
     return n;
 }
 
-template <int MT, int EPI, bool LN>
+template <int MT, int EPI, bool LN, bool WB>
 int launch_gemv_mt(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 {
     const unsigned gx = (a.M + MT - 1) / MT;
@@ -1046,20 +1188,20 @@ int launch_gemv_mt(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
     // one wave: every CTA resident at once, each walking several column groups
     // (measured: capping the CTAs per SM to leave room for the next kernel's
     // early-launched CTAs only slows the step)
-    const unsigned slots = (unsigned)(gemv_blocks_per_sm<MT, EPI, LN>() * sms);
+    const unsigned slots = (unsigned)(gemv_blocks_per_sm<MT, EPI, LN, WB>() * sms);
     unsigned gy = slots / gx;
     if (gy < 1) gy = 1;
     if (gy > ngroups) gy = ngroups;
     if (gy > 65535u) gy = 65535u;
-    return launch_k(gemv_kernel<MT, EPI, LN>, dim3(gx, gy), dim3(128), st, pdl, a);
+    return launch_k(gemv_kernel<MT, EPI, LN, WB>, dim3(gx, gy), dim3(128), st, pdl, a);
 }
 
 constexpr size_t GEMV_TEAM_MAX_SMEM = 64 * 1024;  // staged x rows per CTA
 
-template <int MT, int KW, int EPI, bool LN>
+template <int MT, int KW, int EPI, bool LN, bool WB>
 int launch_gemv_team(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 {
-    auto kern = gemv_team_kernel<MT, KW, EPI, LN>;
+    auto kern = gemv_team_kernel<MT, KW, EPI, LN, WB>;
     const size_t smem = (size_t)(MT + (LN ? 1 : 0)) * a.K * sizeof(float);
     static uint64_t attr_devices = 0;
     static size_t occ_smem = 0;
@@ -1093,7 +1235,7 @@ int launch_gemv_team(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 #ifndef FML_GEMV_KW2_MAX
 #define FML_GEMV_KW2_MAX 1024
 #endif
-template <int MT, int EPI, bool LN>
+template <int MT, int EPI, bool LN, bool WB>
 int launch_gemv_team_k(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
 {
     uint32_t kw = a.K <= FML_GEMV_KW1_MAX ? 1u : (a.K <= FML_GEMV_KW2_MAX ? 2u : 4u);
@@ -1102,15 +1244,16 @@ int launch_gemv_team_k(const GemvArgs& a, cudaStream_t st, bool pdl, int sms)
         const long v = strtol(e, nullptr, 10);
         if (v == 1 || v == 2 || v == 4) kw = (uint32_t)v;
     }
-    if (kw == 1) return launch_gemv_team<MT, 1, EPI, LN>(a, st, pdl, sms);
-    if (kw == 2) return launch_gemv_team<MT, 2, EPI, LN>(a, st, pdl, sms);
-    return launch_gemv_team<MT, 4, EPI, LN>(a, st, pdl, sms);
+    if (kw == 1) return launch_gemv_team<MT, 1, EPI, LN, WB>(a, st, pdl, sms);
+    if (kw == 2) return launch_gemv_team<MT, 2, EPI, LN, WB>(a, st, pdl, sms);
+    return launch_gemv_team<MT, 4, EPI, LN, WB>(a, st, pdl, sms);
 }
 
-template <int EPI, bool LN>
-int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
+template <int EPI, bool LN, bool WB>
+int launch_gemv_w(const GemvArgs& a, cudaStream_t st, bool pdl)
 {
     FML_REQUIRE(a.K % 4 == 0 && a.ldx % 4 == 0, "gemv: K and ldx must be multiples of 4");
+    FML_REQUIRE(!WB || (a.K % 8 == 0 && a.wb), "gemv: bf16 weights need K a multiple of 8");
     FML_REQUIRE(!LN || a.gamma, "gemv: LayerNorm prologue without gamma");
     static int sms = 0;
     if (!sms)
@@ -1137,12 +1280,20 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
     const uint32_t mt_team = a.M <= 4 || mt_cap == 4 ? 4u : 8u;
     if (team && (mt_team + (LN ? 1 : 0)) * a.K * sizeof(float) <= GEMV_TEAM_MAX_SMEM)
     {
-        if (mt_team == 4) return launch_gemv_team_k<4, EPI, LN>(a, st, pdl, sms);
-        return launch_gemv_team_k<8, EPI, LN>(a, st, pdl, sms);
+        if (mt_team == 4) return launch_gemv_team_k<4, EPI, LN, WB>(a, st, pdl, sms);
+        return launch_gemv_team_k<8, EPI, LN, WB>(a, st, pdl, sms);
     }
-    if (a.M <= 4 || mt_cap == 4) return launch_gemv_mt<4, EPI, LN>(a, st, pdl, sms);
-    if (a.M <= 8 || mt_cap == 8) return launch_gemv_mt<8, EPI, LN>(a, st, pdl, sms);
-    return launch_gemv_mt<16, EPI, LN>(a, st, pdl, sms);
+    if (a.M <= 4 || mt_cap == 4) return launch_gemv_mt<4, EPI, LN, WB>(a, st, pdl, sms);
+    if (a.M <= 8 || mt_cap == 8) return launch_gemv_mt<8, EPI, LN, WB>(a, st, pdl, sms);
+    return launch_gemv_mt<16, EPI, LN, WB>(a, st, pdl, sms);
+}
+
+// The decode GEMV: fp32 weights (a.w), or their bf16 copy when a.wb is set.
+template <int EPI, bool LN>
+int launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl)
+{
+    if (a.wb) return launch_gemv_w<EPI, LN, true>(a, st, pdl);
+    return launch_gemv_w<EPI, LN, false>(a, st, pdl);
 }
 
 int launch_attention(fml_lm* lm, uint32_t layer, uint32_t row0, uint32_t rows, const uint32_t* pos, uint32_t P,
@@ -1260,12 +1411,15 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
     }
     const bool tp = lm->tp_world > 1;
     const bool resid_here = lm->tp_rank == 0;  // row-parallel sums take the residual once
+    const bool wb = lm->weight_format == FML_WEIGHTS_BF16;
+    FML_REQUIRE(!wb || lm->wb16_valid, "decode step: the bf16 weight copy is not ready");
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         {
             ProfScope ps(lm, 2, st);
             GemvArgs a{};
             a.x = lm->x; a.ldx = d; a.w = lm->wqkv[l]; a.M = B; a.N = 3 * lm->dl; a.K = d; a.gamma = lm->ln0[l];
+            if (wb) a.wb = lm->wqkv_b[l];
             a.q = lm->q; a.kc = lm->kc + (uint64_t)l * lm->layer_stride; a.vc = lm->vc + (uint64_t)l * lm->layer_stride;
             a.pos = lm->pos; a.d = lm->dl; a.H = lm->hl; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
             FML_RC((decode_gemv<EPI_QKV, true>(lm, a, 2, st, pdl)));
@@ -1278,6 +1432,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             ProfScope ps(lm, 4, st);
             GemvArgs a{};
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
+            if (wb) a.wb = lm->wproj_b[l];
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
             if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, 4, st, pdl));
             else
@@ -1291,6 +1446,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             ProfScope ps(lm, 5, st);
             GemvArgs a{};
             a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = lm->fl; a.K = d; a.gamma = lm->ln1[l];
+            if (wb) a.wb = lm->wfc_b[l];
             a.y = lm->hid; a.ldy = lm->fl;
             FML_RC((decode_gemv<EPI_GELU, true>(lm, a, 5, st, pdl && (!tp || lm->ar_fused))));
         }
@@ -1298,6 +1454,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             ProfScope ps(lm, 6, st);
             GemvArgs a{};
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
+            if (wb) a.wb = lm->wmlp_b[l];
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
             if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, 6, st, pdl));
             else
@@ -1313,6 +1470,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
         GemvArgs a{};
         a.x = lm->x; a.ldx = d; a.w = lm->tok + (uint64_t)lm->v0 * d; a.M = B; a.N = lm->vl; a.K = d;
         a.gamma = lm->lnf; a.y = logits; a.ldy = lm->vl; a.keys = lm->keys; a.n_off = lm->v0;
+        if (wb) a.wb = lm->head_b;
         FML_RC((decode_gemv<EPI_ARGMAX, true>(lm, a, 7, st, pdl && !tp)));
         if (tp) FML_RC(all_reduce_max_keys(lm, B, st));
     }
@@ -1363,6 +1521,53 @@ int ensure_weight_lo(fml_lm* lm, cudaStream_t st)
         FML_RC(tf32_lo(lm->wmlp_lo[l], lm->wmlp[l], d * fl, st));
     }
     lm->wlo_valid = true;
+    return FML_OK;
+}
+
+// The bf16 copy of the decode weights (FML_WEIGHTS_BF16): allocated once,
+// refilled after every bind.  Called before a step is enqueued or recorded
+// (never inside a stream capture).
+int ensure_weight_bf16(fml_lm* lm, cudaStream_t st)
+{
+    if (lm->weight_format != FML_WEIGHTS_BF16 || lm->wb16_valid) return FML_OK;
+    const fml_lm_config& c = lm->cfg;
+    const uint64_t d = c.d_model, dl = lm->dl, fl = lm->fl;
+    const uint64_t per_layer = 3 * dl * d + d * dl + fl * d + d * fl;
+    const uint64_t head = (uint64_t)lm->vl * d;
+    if (!lm->wb16)
+    {
+        if (cudaMalloc(&lm->wb16, (per_layer * c.n_layer + head) * sizeof(uint16_t)) != cudaSuccess)
+        {
+            cudaGetLastError();
+            lm->wb16 = nullptr;
+            return set_error(FML_ERR_NOMEM, "bf16 weight copy: cudaMalloc of %llu bytes failed",
+                             (unsigned long long)((per_layer * c.n_layer + head) * sizeof(uint16_t)));
+        }
+        uint16_t* p = lm->wb16;
+        lm->wqkv_b.clear(); lm->wproj_b.clear(); lm->wfc_b.clear(); lm->wmlp_b.clear();
+        for (uint32_t l = 0; l < c.n_layer; ++l)
+        {
+            lm->wqkv_b.push_back(p); p += 3 * dl * d;
+            lm->wproj_b.push_back(p); p += d * dl;
+            lm->wfc_b.push_back(p); p += fl * d;
+            lm->wmlp_b.push_back(p); p += d * fl;
+        }
+        lm->head_b = p;
+    }
+    auto conv = [&](const uint16_t* dst, const float* src, uint64_t n) -> int {
+        to_bf16_kernel<<<grid_for(n, 256), 256, 0, st>>>(const_cast<uint16_t*>(dst), src, n);
+        FML_LAUNCH_CHECK();
+        return FML_OK;
+    };
+    for (uint32_t l = 0; l < c.n_layer; ++l)
+    {
+        FML_RC(conv(lm->wqkv_b[l], lm->wqkv[l], 3 * dl * d));
+        FML_RC(conv(lm->wproj_b[l], lm->wproj[l], d * dl));
+        FML_RC(conv(lm->wfc_b[l], lm->wfc[l], fl * d));
+        FML_RC(conv(lm->wmlp_b[l], lm->wmlp[l], d * fl));
+    }
+    FML_RC(conv(lm->head_b, lm->tok + (uint64_t)lm->v0 * d, head));
+    lm->wb16_valid = true;
     return FML_OK;
 }
 
@@ -1542,6 +1747,7 @@ int fml_lm_bind_weights(fml_lm* lm, const fml_lm_weights* w, fml_stream_t stream
     const fml_lm_config& c = lm->cfg;
     const uint64_t d = c.d_model, f = sizeof(float);
     lm->wlo_valid = false;  // the lo parts follow the new weights at the next prefill
+    lm->wb16_valid = false;  // and the bf16 copy at the next step
     FML_CUDA_TRY(cudaMemcpyAsync(lm->tok, w->tok_emb, (uint64_t)c.vocab * d * f, cudaMemcpyDeviceToDevice, st));
     FML_CUDA_TRY(cudaMemcpyAsync(lm->pos_emb, w->pos_emb, (uint64_t)c.context * d * f, cudaMemcpyDeviceToDevice, st));
     FML_CUDA_TRY(cudaMemcpyAsync(lm->lnf, w->lnf, d * f, cudaMemcpyDeviceToDevice, st));
@@ -1721,6 +1927,22 @@ int fml_lm_set_prefill_math(fml_lm* lm, int mode)
     FML_REQUIRE(mode == FML_MATH_FP32 || mode == FML_MATH_TF32X3 || mode == FML_MATH_TF32, "unknown math mode %d",
                 mode);
     lm->prefill_math = mode;
+    return FML_OK;
+}
+
+int fml_lm_set_weight_format(fml_lm* lm, int format)
+{
+    FML_REQUIRE(lm, "fml_lm_set_weight_format: null engine");
+    FML_REQUIRE(format == FML_WEIGHTS_FP32 || format == FML_WEIGHTS_BF16, "unknown weight format %d", format);
+    if (lm->weight_format == format) return FML_OK;
+    lm->weight_format = format;
+    lm->wb16_valid = false;
+    drop_graphs(lm);  // the recorded steps read the other weights
+    if (format == FML_WEIGHTS_FP32 && lm->wb16)
+    {
+        cudaFree(lm->wb16);
+        lm->wb16 = nullptr;
+    }
     return FML_OK;
 }
 
@@ -1954,6 +2176,7 @@ int record_steps(fml_lm* lm, uint32_t n, cudaGraphExec_t* out)
 int enqueue_step_host(fml_lm* lm, cudaStream_t st)
 {
     FML_RC(check_step_state(lm, "fml_lm_step_host"));
+    FML_RC(ensure_weight_bf16(lm, st));
     const uint32_t B = lm->batch;
     uint32_t* dev_next = lm->prompt_dev;  // scratch slot for the step's output tokens
     if (lm->use_graph && !lm->profiling)
@@ -1985,6 +2208,7 @@ int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t s
     FML_REQUIRE(lm, "fml_lm_step: null engine");
     FML_RC(check_step_state(lm, "fml_lm_step"));
     cudaStream_t st = as_stream(stream);
+    FML_RC(ensure_weight_bf16(lm, st));
     if (lm->use_graph && !lm->profiling)
     {
         if (!lm->graph_exec || lm->graph_next != next_tokens || lm->graph_logits != logits ||
@@ -2019,6 +2243,7 @@ int fml_lm_steps(fml_lm* lm, uint32_t n, fml_stream_t stream)
             return set_error(FML_ERR_STATE, "fml_lm_steps: %u steps take sequence %u past the context limit (%u)", n,
                              b, lm->cfg.context);
     cudaStream_t st = as_stream(stream);
+    FML_RC(ensure_weight_bf16(lm, st));
     if (!lm->use_graph || lm->profiling)
     {
         for (uint32_t i = 0; i < n; ++i) FML_RC(fml_lm_step(lm, nullptr, nullptr, stream));

@@ -215,6 +215,11 @@ class NanoLM:
         """FML_MATH_TF32X3 (default, tensor cores), FML_MATH_TF32 or FML_MATH_FP32."""
         call("fml_lm_set_prefill_math", self._h, int(mode))
 
+    def set_weight_format(self, fmt: str) -> None:
+        """'fp32' (default) or 'bf16': the storage of the weights the decode
+        step streams (fml_lm_set_weight_format)."""
+        call("fml_lm_set_weight_format", self._h, {"fp32": 0, "bf16": 1}[fmt])
+
     def set_graph(self, on: bool) -> None:
         call("fml_lm_set_graph", self._h, int(on))
 

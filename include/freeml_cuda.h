@@ -402,6 +402,19 @@ FML_API int fml_tp_flag_check(uint32_t epoch, uint32_t slot, uint32_t nslot, uin
 FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
 
 
+/* Storage of the weights the decode step streams.  FML_WEIGHTS_FP32 (the
+ * default): the fp32 weights, as the reference holds them.  FML_WEIGHTS_BF16:
+ * the decode GEMVs (QKV, projection, fc, mlp and the tied lm_head) read a
+ * bf16 copy, rounded to nearest even, and accumulate in fp32 -- half the
+ * weight bytes per step.  The copy is made after each bind, before the next
+ * step (2 bytes per weight of extra device memory); the prefill, the
+ * embedding gathers, LayerNorm gammas and the K/V cache stay fp32.  Logits
+ * then differ from the fp32 reference by more than the fp32 bound (tests
+ * state the bf16 bound).  No counterpart in the reference, which holds fp32
+ * (PRECISION=float) weights only. */
+enum fml_weight_format { FML_WEIGHTS_FP32 = 0, FML_WEIGHTS_BF16 = 1 };
+FML_API int fml_lm_set_weight_format(fml_lm* lm, int format);
+
 /* One decode step for every active sequence: consume each sequence's pending
  * token, append its K/V, and produce the next token (greedy).  Optional
  * outputs (device): next tokens [batch] and logits [batch x V] of the row

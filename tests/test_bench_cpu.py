@@ -18,6 +18,15 @@ def test_weight_bytes_per_step():
         assert abs(want / 1e6 - mb) < 0.1
 
 
+def test_bf16_weight_bytes_per_step():
+    # the bf16-weight mode streams the 12 d^2 per layer and the lm_head rows
+    # at 2 bytes; the gammas stay fp32
+    for d, L, V in (CFG3, CFG4, CFG5):
+        want = 2 * (12 * d * d * L + V * d) + 4 * (2 * L + 1) * d
+        assert bench.weight_bytes_bf16(d, L, V) == want
+        assert abs(bench.weight_bytes_bf16(d, L, V) / bench.weight_bytes(d, L, V) - 0.5) < 1e-3
+
+
 def test_tensor_parallel_weight_share():
     d, L, V = CFG5
     full = bench.weight_bytes(d, L, V)

@@ -59,14 +59,14 @@ def _check_teacher_forced(name, ref_rows_fn, toks, logits, seqs, P, N):
     return rows
 
 
-def first_divergence(ref_logits, gpu_tokens_next):
-    """Index of the first row whose reference argmax (with a clear top-2 gap)
-    differs from the GPU's token, or -1."""
+def first_divergence(ref_logits, gpu_tokens_next, gap=GAP):
+    """Index of the first row whose reference argmax (with a top-2 gap above
+    `gap`) differs from the GPU's token, or -1."""
     for t in range(ref_logits.shape[0]):
         row = ref_logits[t]
         top2 = np.sort(row)[-2:]
         if O.argmax_first(row) != gpu_tokens_next[t]:
-            if top2[1] - top2[0] > GAP:
+            if top2[1] - top2[0] > gap:
                 return t
             return -2 - t  # a near-tie: acceptable, stop comparing here
     return -1

@@ -24,8 +24,15 @@ def _layernorm(x, g):
     return (x - mean) / torch.sqrt(var + 1e-5) * g
 
 
-def forward(params: torch.Tensor, V: int, C: int, d: int, H: int, L: int, tokens, row0: int, nrows: int):
-    """Logits rows [row0, row0 + nrows) of a forward over `tokens` (T <= C)."""
+def forward(params: torch.Tensor, V: int, C: int, d: int, H: int, L: int, tokens, row0: int, nrows: int,
+            bf16_from_row=None):
+    """Logits rows [row0, row0 + nrows) of a forward over `tokens` (T <= C).
+
+    bf16_from_row = r: rows >= r multiply by the Dense weights and the tied
+    lm_head rounded to bf16 (nearest even) -- what the decode engine's
+    bf16-weight mode computes for the rows it generates after an fp32
+    prefill of rows < r (a row's K/V come from its own QKV, so the rule is
+    exact per row)."""
     p = params.to(torch.float32)
     dev = p.device
     tokens = torch.as_tensor(tokens, dtype=torch.long, device=dev)
@@ -42,6 +49,14 @@ def forward(params: torch.Tensor, V: int, C: int, d: int, H: int, L: int, tokens
     tok = take(V * d, V, d)
     pos = take(C * d, C, d)
     x = tok[tokens] + pos[:T]
+    r0 = T if bf16_from_row is None else bf16_from_row
+
+    def lin(inp, w):
+        out = inp @ w
+        if r0 < inp.shape[0]:
+            out[r0:] = inp[r0:] @ w.to(torch.bfloat16).to(torch.float32)
+        return out
+
     causal = torch.triu(torch.ones(T, T, dtype=torch.bool, device=dev), diagonal=1)
     for _ in range(L):
         g0 = take(d, d)
@@ -50,13 +65,19 @@ def forward(params: torch.Tensor, V: int, C: int, d: int, H: int, L: int, tokens
         g1 = take(d, d)
         wfc = take(4 * d * d, d, 4 * d)
         wmlp = take(4 * d * d, 4 * d, d)
-        qkv = _layernorm(x, g0) @ wqkv
+        qkv = lin(_layernorm(x, g0), wqkv)
         q, k, v = (t.view(T, H, hd).transpose(0, 1) for t in qkv.split(d, dim=1))
         s = (q @ k.transpose(-1, -2)) * (1.0 / math.sqrt(hd))
         s = s.masked_fill(causal, float("-inf"))
         y = (torch.softmax(s, dim=-1) @ v).transpose(0, 1).reshape(T, d)
-        buf = x + y @ wprj.t()
-        h = torch.nn.functional.gelu(_layernorm(buf, g1) @ wfc)
-        x = buf + h @ wmlp
+        buf = x + lin(y, wprj.t())
+        h = torch.nn.functional.gelu(lin(_layernorm(buf, g1), wfc))
+        x = buf + lin(h, wmlp)
     gf = take(d, d)
-    return _layernorm(x[row0:row0 + nrows], gf) @ tok.t()
+    xf = _layernorm(x[row0:row0 + nrows], gf)
+    if r0 >= row0 + nrows:
+        return xf @ tok.t()
+    out = xf @ tok.t()
+    lo = max(r0 - row0, 0)
+    out[lo:] = xf[lo:] @ tok.t().to(torch.bfloat16).to(torch.float32)
+    return out
