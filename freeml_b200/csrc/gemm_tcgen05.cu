@@ -151,7 +151,7 @@ __device__ __forceinline__ bool issue_stage_probe(uint32_t tmem_d, uint64_t da, 
 
 }  // namespace tc
 
-enum TcEpi { TC_STORE = 0, TC_GELU = 1, TC_RESID = 2 };
+enum TcEpi { TC_STORE = 0, TC_GELU = 1, TC_RESID = 2, TC_QKV = 3 };
 
 struct TcArgs
 {
@@ -160,6 +160,14 @@ struct TcArgs
     int ldc;
     const float* R;   // TC_RESID: C = R + A.B^T (row stride ldc)
     bool vec4;        // C (and R) 16-byte aligned with ldc a multiple of 4
+    // TC_QKV (the prefill's packed QKV rows, row = b * P + t): columns
+    // [0, dq) go to C (row stride ldc), [dq, 2 dq) to the K cache and
+    // [2 dq, 3 dq) to the V cache at cache + b * seq_stride +
+    // (h * ctx + t) * hd + e for column h * hd + e of the part
+    float* kc;
+    float* vc;
+    int P, hd, dq, ctx;
+    uint64_t seq_stride;
 };
 
 // One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x +
@@ -385,6 +393,22 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
                 if (row < args.M)
                 {
                     float* crow = args.C + (uint64_t)row * args.ldc + n0 + c0;
+                    if constexpr (EPI == TC_QKV)
+                    {
+                        // a 32-column slice lies inside one head of one part
+                        // (dq and hd are multiples of 32): one base address
+                        const int n = n0 + c0;
+                        if (n >= args.dq)
+                        {
+                            const bool isk = n < 2 * args.dq;
+                            const int c = isk ? n - args.dq : n - 2 * args.dq;
+                            const int b = row / args.P, tq = row - b * args.P;
+                            crow = (isk ? args.kc : args.vc) + (uint64_t)b * args.seq_stride +
+                                   ((uint64_t)(c / args.hd) * args.ctx + tq) * args.hd + c % args.hd;
+                        }
+                        else
+                            crow = args.C + (uint64_t)row * args.ldc + n;
+                    }
                     const float* rrow = EPI == TC_RESID ? args.R + (uint64_t)row * args.ldc + n0 + c0 : nullptr;
                     if (args.vec4 && n0 + c0 + 32 <= args.N)
                     {
@@ -497,6 +521,33 @@ int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int l
     if (epi == TC_GELU) return launch_tc<false, TC_GELU>(ma, mb, mblo, args, st);
     if (epi == TC_RESID) return launch_tc<false, TC_RESID>(ma, mb, mblo, args, st);
     return launch_tc<false, TC_STORE>(ma, mb, mblo, args, st);
+}
+
+// The prefill's QKV contraction with its scatter fused into the epilogue:
+// qkv = A . B^T (B [3 dq x K]) written as q [M x dq] (row stride ldq) and as
+// the rows t of the K and V caches of sequence b = row / P (layout of
+// TcArgs::kc).  dq and hd must be multiples of 32, q and the caches 16-byte
+// aligned.
+int gemm_tc_qkv(float* q, int ldq, float* kc, float* vc, uint64_t seq_stride, int P, int hd, int ctx,
+                const float* A, const float* B, int M, int dq, int K, bool split3, cudaStream_t st, const float* B_lo)
+{
+    if (M <= 0 || dq <= 0) return FML_OK;
+    FML_REQUIRE(K > 0 && P > 0, "gemm_tc_qkv: K and P must be positive");
+    FML_REQUIRE(dq % 32 == 0 && hd % 32 == 0 && dq % hd == 0 && ldq % 4 == 0,
+                "gemm_tc_qkv: dq and hd must be multiples of 32 (dq %d, hd %d)", dq, hd);
+    FML_REQUIRE(aligned16(A) && aligned16(B) && aligned16(q) && aligned16(kc) && aligned16(vc) && K % 4 == 0 &&
+                    (!B_lo || aligned16(B_lo)) && seq_stride % 4 == 0,
+                "gemm_tc_qkv: operands must be 16-byte aligned with row strides that are multiples of 4");
+    CUtensorMap ma, mb, mblo;
+    FML_RC(tc::make_map(&ma, A, M, K, K, tc::BM));
+    FML_RC(tc::make_map(&mb, B, 3 * dq, K, K, tc::BN));
+    const bool blo = split3 && B_lo;
+    if (blo) FML_RC(tc::make_map(&mblo, B_lo, 3 * dq, K, K, tc::BN));
+    else mblo = mb;
+    TcArgs args{M, 3 * dq, K, q, ldq, nullptr, true, kc, vc, P, hd, dq, ctx, seq_stride};
+    if (blo) return launch_tc<true, TC_QKV, true>(ma, mb, mblo, args, st);
+    if (split3) return launch_tc<true, TC_QKV>(ma, mb, mblo, args, st);
+    return launch_tc<false, TC_QKV>(ma, mb, mblo, args, st);
 }
 
 // C = A . B on the tensor cores with B [K x N] row-major (row stride ldb):

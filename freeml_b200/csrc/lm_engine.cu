@@ -62,6 +62,9 @@ int gemm_f32(float* C, const float* A, const float* B, int M, int N, int K, int 
              int batch, uint64_t pa, uint64_t pb, uint64_t pc, cudaStream_t st);
 int gemm_tc(float* C, const float* A, const float* B, int M, int N, int K, int lda, int ldb, int ldc, bool split3,
             int epi, const float* R, cudaStream_t st, const float* B_lo = nullptr);
+int gemm_tc_qkv(float* q, int ldq, float* kc, float* vc, uint64_t seq_stride, int P, int hd, int ctx,
+                const float* A, const float* B, int M, int dq, int K, bool split3, cudaStream_t st,
+                const float* B_lo = nullptr);
 int tf32_lo(float* lo, const float* x, uint64_t n, cudaStream_t st);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
@@ -1877,17 +1880,28 @@ int fml_lm_prefill(fml_lm* lm, const uint32_t* prompts, uint32_t batch, uint32_t
         float* vc = lm->vc + (uint64_t)l * lm->layer_stride;
         const uint32_t dl = lm->dl, fl = lm->fl;
         FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, R, d, d, d, 1e-5f, st));
-        FML_RC(prefill_gemm(lm, lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * dl), (int)d, 0, nullptr, st,
-                            lm->wlo_valid ? lm->wqkv_lo[l] : nullptr));
-        qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * dl, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, dl, lm->hd,
-                                                                               c.context, lm->seq_stride);
-        FML_LAUNCH_CHECK();
+        // QKV: on the tensor cores the epilogue writes q and the cached K/V
+        // rows directly (measured on config 3's prefill: the separate scatter
+        // took 26.5 us of every layer's ~250); otherwise packed rows + scatter
+        if (lm->prefill_math != FML_MATH_FP32 && d % 4 == 0 && dl % 32 == 0 && lm->hd % 32 == 0)
+            FML_RC(gemm_tc_qkv(lm->q, (int)dl, kc, vc, lm->seq_stride, (int)P, (int)lm->hd, (int)c.context, lm->ln,
+                               lm->wqkv[l], (int)R, (int)dl, (int)d, lm->prefill_math == FML_MATH_TF32X3, st,
+                               lm->wlo_valid ? lm->wqkv_lo[l] : nullptr));
+        else
+        {
+            FML_RC(prefill_gemm(lm, lm->tmp, lm->ln, lm->wqkv[l], (int)R, (int)(3 * dl), (int)d, 0, nullptr, st,
+                                lm->wlo_valid ? lm->wqkv_lo[l] : nullptr));
+            qkv_scatter_kernel<<<grid_for((uint64_t)R * 3 * dl, 256), 256, 0, st>>>(lm->tmp, lm->q, kc, vc, R, P, dl,
+                                                                                   lm->hd, c.context, lm->seq_stride);
+            FML_LAUNCH_CHECK();
+        }
         // prefill attention: tensor cores in the TF32 modes (128-query tiles),
         // else (or for a layout that kernel does not take) the CUDA-core kernel
         {
             const float scale = 1.0f / sqrtf((float)lm->hd);
             int rc = FML_ERR_UNSUPPORTED;
-            if (lm->prefill_math != FML_MATH_FP32)
+            const char* pa_env = getenv("FML_PREFILL_ATTN_SIMT");  // tuning: 1 = the CUDA-core kernel
+            if (lm->prefill_math != FML_MATH_FP32 && !(pa_env && pa_env[0] == '1'))
                 rc = launch_prefill_attention_tc(lm->q, dl, kc, vc, lm->seq_stride, c.context, lm->att, dl, batch,
                                                  lm->hl, P, lm->hd, scale, lm->prefill_math == FML_MATH_TF32X3, st);
             if (rc == FML_ERR_UNSUPPORTED)

@@ -197,11 +197,79 @@ __global__ void softmax_kernel(float* __restrict__ out, const float* in, uint32_
     }
 }
 
+// The same LayerNormOp for rows of up to 2048 columns in multiples of 128:
+// one warp per row holds the row in registers (NV float4 per lane, requested
+// together), so the row is read from memory once and the two statistics
+// passes and the output pass run on registers.
+template <int NV>
+__global__ void layernorm_rows_kernel(float* __restrict__ out, const float* __restrict__ in,
+                                      const float* __restrict__ gamma, const float* __restrict__ beta,
+                                      float* __restrict__ xhat, uint32_t rows, uint32_t cols, uint64_t in_stride,
+                                      uint64_t out_stride, float eps)
+{
+    const int lane = threadIdx.x & 31;
+    const uint32_t warps = blockDim.x >> 5;
+    const uint32_t c4 = cols / 4;  // float4 per row: 32 * nv, nv <= NV
+    const float invCols = 1.0f / (float)cols;
+    for (uint32_t r = blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += gridDim.x * warps)
+    {
+        const float4* x = reinterpret_cast<const float4*>(in + r * in_stride);
+        float4 v[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            if ((uint32_t)(lane + 32 * i) < c4) v[i] = x[lane + 32 * i];
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            if ((uint32_t)(lane + 32 * i) < c4) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        const float mean = warp_sum(s) * invCols;
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            if ((uint32_t)(lane + 32 * i) < c4)
+            {
+                const float d0 = v[i].x - mean, d1 = v[i].y - mean, d2 = v[i].z - mean, d3 = v[i].w - mean;
+                q = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, fmaf(d3, d3, q))));
+            }
+        const float invStd = 1.0f / sqrtf(fmaf(warp_sum(q), invCols, eps));
+        float4* y = reinterpret_cast<float4*>(out + r * out_stride);
+        const float4* g4 = reinterpret_cast<const float4*>(gamma);
+        const float4* b4 = reinterpret_cast<const float4*>(beta);
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+        {
+            const uint32_t c = lane + 32 * i;
+            if (c >= c4) continue;
+            const float4 g = g4[c];
+            const float4 b = beta ? b4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 n;
+            n.x = (v[i].x - mean) * invStd; n.y = (v[i].y - mean) * invStd;
+            n.z = (v[i].z - mean) * invStd; n.w = (v[i].w - mean) * invStd;
+            if (xhat) reinterpret_cast<float4*>(xhat + r * (uint64_t)cols)[c] = n;
+            y[c] = make_float4(fmaf(n.x, g.x, b.x), fmaf(n.y, g.y, b.y), fmaf(n.z, g.z, b.z), fmaf(n.w, g.w, b.w));
+        }
+    }
+}
+
 int launch_layernorm(float* out, const float* in, const float* gamma, const float* beta, float* xhat, uint32_t rows,
                      uint32_t cols, uint64_t in_stride, uint64_t out_stride, float eps, cudaStream_t st)
 {
     if (rows == 0) return FML_OK;
     const unsigned block = 128;
+    if (cols % 128 == 0 && cols <= 2048 && in_stride % 4 == 0 && out_stride % 4 == 0 && aligned16(in) &&
+        aligned16(out) && aligned16(gamma) && (!beta || aligned16(beta)) && (!xhat || aligned16(xhat)))
+    {
+        const unsigned grid = (unsigned)((rows + 3) / 4);
+        const unsigned g = grid < 65535u * 8 ? grid : 65535u * 8;
+        if (cols <= 512)
+            layernorm_rows_kernel<4><<<g, block, 0, st>>>(out, in, gamma, beta, xhat, rows, cols, in_stride, out_stride,
+                                                           eps);
+        else
+            layernorm_rows_kernel<16><<<g, block, 0, st>>>(out, in, gamma, beta, xhat, rows, cols, in_stride,
+                                                            out_stride, eps);
+        FML_LAUNCH_CHECK();
+        return FML_OK;
+    }
     const unsigned grid = (unsigned)((rows + 3) / 4);
     layernorm_kernel<<<grid < 65535u * 8 ? grid : 65535u * 8, block, 0, st>>>(out, in, gamma, beta, xhat, rows, cols,
                                                                                in_stride, out_stride, eps);

@@ -110,7 +110,7 @@ def test_matmul_vs_oracle(M, N, K, mode):
     gemm_close(host(out), ref, A, B.T if mode else B)
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 1), (7, 33), (64, 512), (3, 4096)])
+@pytest.mark.parametrize("rows,cols", [(1, 1), (7, 33), (64, 512), (3, 4096), (17, 128), (9, 640), (5, 2048)])
 def test_row_ops_vs_oracle(rows, cols):
     from freeml_b200 import matrix_ops as F
     rs = np.random.RandomState(rows + cols)
