@@ -456,14 +456,16 @@ def main():
         one_pass()
     torch.cuda.synchronize()
 
-    # ---- one timed prefill of this rank's prompts (tensor-core contractions);
-    # it leaves the same KV rows and first tokens behind ----
+    # ---- timed prefills of this rank's prompts (tensor-core contractions);
+    # each leaves the same KV rows and first tokens behind ----
     pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_prefill = 3  # back-to-back prefills of the same prompts, averaged
     pe0.record()
-    lm.prefill(prompts)
+    for _ in range(n_prefill):
+        lm.prefill(prompts)
     pe1.record()
     torch.cuda.synchronize()
-    prefill_ms = max_over_ranks(pe0.elapsed_time(pe1), pg, "cuda")
+    prefill_ms = max_over_ranks(pe0.elapsed_time(pe1) / n_prefill, pg, "cuda")
     dm, Lm = s.d_model, s.n_layer
     prefill_flop = dp * prefill_flops(dm, Lm, s.vocab, B, P)
 
@@ -592,7 +594,7 @@ def main():
                               "frac": step_bytes / (pass_ms / 1e3) / 1e9 / peak},
             "kernel_us_per_step": {k: v / 1e3 / max(kt["steps"], 1) for k, v in kt["by_class_ns"].items()},
             "stamped_step_us": kt["total_ns"] / 1e3 / max(kt["steps"], 1),
-            "prefill": {"ms": prefill_ms, "tokens_per_s": dp * B * P / (prefill_ms / 1e3),
+            "prefill": {"ms": prefill_ms, "prefills_timed": n_prefill, "tokens_per_s": dp * B * P / (prefill_ms / 1e3),
                         "algorithmic_tflop": prefill_flop / 1e12,
                         "tflops": prefill_flop / (prefill_ms / 1e3) / 1e12,
                         "math": "TF32x3 on tcgen05 (three kind::tf32 MMAs per product, fp32 accumulate in TMEM)",
