@@ -49,6 +49,12 @@ def _rank(rank, world, q_id, q_out, fused, q_h):
             lm.tp_connect([got[r] for r in range(world)])
         lm.bind(w)
         toks, logits = lm.generate(prompts, N, want_logits=True)
+        # the same steps again as multi-step graphs (fml_lm_steps, with the
+        # all-reduces captured inside): the last pending token must match
+        lm.rewind(c["prompt"], np.ascontiguousarray(toks[:, c["prompt"]], np.uint32))
+        lm.steps(N - 1)
+        again = lm.pending_tokens().cpu().numpy().view(np.uint32)[:NSEQ]
+        assert np.array_equal(again, toks[:, c["prompt"] + N - 1]), "multi-step graphs gave another stream"
         v0, vl = lm.vocab_slice()
         import ctypes
         from freeml_b200 import _lib
