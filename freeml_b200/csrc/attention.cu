@@ -301,22 +301,23 @@ __global__ void __launch_bounds__(32 * NW, 32 / NW) attention_kernel(AttnArgs a)
 template <int HD>
 static int launch_attention_hd(AttnArgs a, dim3 grid, cudaStream_t st, bool pdl)
 {
-    // warps per CTA: 16 with a quarter of the splits when that still gives
-    // every SM a CTA (one CTA then merges four splits' worth of warps in
-    // shared memory instead of four CTAs through a cluster), else 4.
-    // Measured on B200, config 3: 32 sequences (256 (row, head) pairs, 4
-    // splits) attention 10.1 -> 9.7 us per launch in the step graph; at 4
-    // and 1 sequences 16 warps lose (3.9 -> 5.4 us).  Tuning override:
-    // FML_ATTN_WARPS = 4 | 16.
-    int nw = (grid.z % 4 == 0 && (uint64_t)grid.x * grid.y * (grid.z / 4) >= 148) ? 16 : 4;
+    // warps per CTA: 16 in place of exactly 4 splits when the (row, head)
+    // pairs alone give every SM a CTA (one CTA then merges four splits'
+    // worth of warps in shared memory instead of four CTAs through a
+    // cluster), else 4.  Measured on B200, config 3 decode, attention per
+    // step (8 launches) at 4 / 8 / 16 warps: 32 sequences (256 pairs, 4
+    // splits) 68.3 / 70.9 / 65.1 us; 16 sequences (8 splits) 56.9 / 56.6 /
+    // 62.1; 8 sequences 39.3 / 41.8 / 47.3.  Tuning override:
+    // FML_ATTN_WARPS = 4 | 8 | 16.
+    int nw = (grid.z == 4 && (uint64_t)grid.x * grid.y >= 148) ? 16 : 4;
     if (const char* e = getenv("FML_ATTN_WARPS"))
     {
         const long v = strtol(e, nullptr, 10);
-        if (v == 4 || (v == 16 && grid.z % 4 == 0)) nw = (int)v;
+        if (v == 4 || (v == 8 && grid.z % 2 == 0) || (v == 16 && grid.z % 4 == 0)) nw = (int)v;
     }
-    if (nw == 16)
+    if (nw > 4)
     {
-        grid.z /= 4;
+        grid.z /= (uint32_t)(nw / 4);
         a.S = grid.z;
     }
     // 2..8 splits: one cluster per (row, head), merged on chip
@@ -352,6 +353,9 @@ static int launch_attention_hd(AttnArgs a, dim3 grid, cudaStream_t st, bool pdl)
     if (nw == 16)
         e = cl ? cudaLaunchKernelEx(&cfg, attention_kernel<HD, 16, true>, a)
                : cudaLaunchKernelEx(&cfg, attention_kernel<HD, 16, false>, a);
+    else if (nw == 8)
+        e = cl ? cudaLaunchKernelEx(&cfg, attention_kernel<HD, 8, true>, a)
+               : cudaLaunchKernelEx(&cfg, attention_kernel<HD, 8, false>, a);
     else
         e = cl ? cudaLaunchKernelEx(&cfg, attention_kernel<HD, 4, true>, a)
                : cudaLaunchKernelEx(&cfg, attention_kernel<HD, 4, false>, a);
