@@ -1271,7 +1271,7 @@ int launch_gemv_w(const GemvArgs& a, cudaStream_t st, bool pdl)
     // tokens/s against 16 rows per CTA): +13 % at 32 sequences (config 3),
     // +10 % at 8 (config 5); at 64 (config 4) 8 rows beat 4 and 16.
     // Tuning override: FML_GEMV_MT = 4, 8 or 16.
-    const char* mt_env = getenv("FML_GEMV_MT");
+    const char* mt_env = getenv(EPI == EPI_ARGMAX && getenv("FML_GEMV_MT_HEAD") ? "FML_GEMV_MT_HEAD" : "FML_GEMV_MT");
     const long mt_v = mt_env ? strtol(mt_env, nullptr, 10) : (a.M > 32 ? 8 : 4);
     const uint32_t mt_cap = (uint32_t)(mt_v == 4 || mt_v == 8 ? mt_v : 16);
     // team layout for K <= 2048 when the CTA's x rows fit in shared memory;

@@ -192,6 +192,11 @@ def test_multi_step_graphs_match_single_steps(graph_steps, monkeypatch):
         toks, logits = lm.step(want_logits=True)
         outs.append((pend.cpu().numpy(), toks.cpu().numpy().copy(), logits.cpu().numpy().copy(),
                      lm.position(0), lm.position(7)))
+    # a call that would take a sequence past the context fails before any work
+    from freeml_b200._lib import FmlError
+    with pytest.raises(FmlError):
+        lm.steps(s.context)
+    assert lm.position(0) == c["prompt"] + 38
     lm.close()
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
