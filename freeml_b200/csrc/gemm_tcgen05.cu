@@ -470,15 +470,27 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
 
 // ---- host side ---------------------------------------------------------------
 
+template <bool SPLIT3>
+constexpr size_t tc_smem_bytes()
+{
+    return 1024 + (size_t)tc::STAGES * (SPLIT3 ? 3 : 2) * tc::TILE_BYTES + 32 * 8;
+}
+
+// The kernel's dynamic shared-memory limit, raised once per device.
+template <bool SPLIT3, int EPI, bool BLO, bool BMN>
+static int tc_smem_setup()
+{
+    static uint64_t attr_devices = 0;
+    return smem_limit_once(reinterpret_cast<const void*>(gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN>),
+                           (int)tc_smem_bytes<SPLIT3>(), attr_devices);
+}
+
 template <bool SPLIT3, int EPI, bool BLO = false, bool BMN = false>
 static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mblo, const TcArgs& args,
                      cudaStream_t st)
 {
-    constexpr int NT = SPLIT3 ? 3 : 2;
-    const size_t smem = 1024 + (size_t)tc::STAGES * NT * tc::TILE_BYTES + 32 * 8;
-    static uint64_t attr_devices = 0;
-    FML_RC(smem_limit_once(reinterpret_cast<const void*>(gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN>), (int)smem,
-                           attr_devices));
+    const size_t smem = tc_smem_bytes<SPLIT3>();
+    FML_RC((tc_smem_setup<SPLIT3, EPI, BLO, BMN>()));
     int dev = 0, sms = 0;
     FML_CUDA_TRY(cudaGetDevice(&dev));
     FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -486,6 +498,22 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN><<<std::min(ntiles, sms), 320, smem, st>>>(ma, mb, mblo, args);
     FML_LAUNCH_CHECK();
     return FML_OK;
+}
+
+// Raise the dynamic shared-memory limit of gemm_tc's kernel for (split3,
+// epi, no B_lo) on the current device, so that a later launch inside a
+// stream capture makes no attribute call.
+int gemm_tc_prepare(bool split3, int epi)
+{
+    if (split3)
+    {
+        if (epi == TC_GELU) return tc_smem_setup<true, TC_GELU, false, false>();
+        if (epi == TC_RESID) return tc_smem_setup<true, TC_RESID, false, false>();
+        return tc_smem_setup<true, TC_STORE, false, false>();
+    }
+    if (epi == TC_GELU) return tc_smem_setup<false, TC_GELU, false, false>();
+    if (epi == TC_RESID) return tc_smem_setup<false, TC_RESID, false, false>();
+    return tc_smem_setup<false, TC_STORE, false, false>();
 }
 
 // C = A . B^T (+ epilogue) on the tensor cores.  A [M x K] (row stride lda),

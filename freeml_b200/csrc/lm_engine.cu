@@ -66,6 +66,7 @@ int gemm_tc_qkv(float* q, int ldq, float* kc, float* vc, uint64_t seq_stride, in
                 const float* A, const float* B, int M, int dq, int K, bool split3, cudaStream_t st,
                 const float* B_lo = nullptr);
 int tf32_lo(float* lo, const float* x, uint64_t n, cudaStream_t st);
+int gemm_tc_prepare(bool split3, int epi);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
                              uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
@@ -875,6 +876,38 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
     }
 }
 
+// Argmax keys of logits rows (the tensor-core lm_head): keys[m] = max over
+// this CTA's columns n of argmax_key(logits[m][n], n + n_off), folded into
+// the row's key with one atomicMax per CTA (keys start at zero: finalize
+// resets them).  grid = (column chunks, rows).
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ logits, uint32_t ld, uint32_t N,
+                                                          uint32_t n_off, unsigned long long* keys, StepStamp stamp)
+{
+    const StampAtExit stamp_at_exit(stamp);
+    __shared__ unsigned long long wbest[8];
+    const uint32_t m = blockIdx.y;
+    unsigned long long best = 0ull;
+    for (uint32_t n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x)
+    {
+        const unsigned long long k = argmax_key(logits[(uint64_t)m * ld + n], n + n_off);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const unsigned long long other = __shfl_xor_sync(FULL_MASK, best, o);
+        best = other > best ? other : best;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) wbest[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0)
+    {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = wbest[w] > best ? wbest[w] : best;
+        atomicMax(keys + m, best);
+    }
+}
+
 // After lm_head: pending token = argmax, advance the position, reset keys.
 // With stamps on, thread 0 stamps the step's last slot and then advances the
 // stamp step counter (every other kernel of the step has finished by then).
@@ -1271,7 +1304,7 @@ int launch_gemv_w(const GemvArgs& a, cudaStream_t st, bool pdl)
     // tokens/s against 16 rows per CTA): +13 % at 32 sequences (config 3),
     // +10 % at 8 (config 5); at 64 (config 4) 8 rows beat 4 and 16.
     // Tuning override: FML_GEMV_MT = 4, 8 or 16.
-    const char* mt_env = getenv(EPI == EPI_ARGMAX && getenv("FML_GEMV_MT_HEAD") ? "FML_GEMV_MT_HEAD" : "FML_GEMV_MT");
+    const char* mt_env = getenv("FML_GEMV_MT");
     const long mt_v = mt_env ? strtol(mt_env, nullptr, 10) : (a.M > 32 ? 8 : 4);
     const uint32_t mt_cap = (uint32_t)(mt_v == 4 || mt_v == 8 ? mt_v : 16);
     // team layout for K <= 2048 when the CTA's x rows fit in shared memory;
@@ -1388,6 +1421,17 @@ int gemv_allreduce(fml_lm* lm, GemvArgs a, float* y, const float* resid, uint32_
                     (uint32_t)lm->tp_world, (uint32_t)lm->tp_rank, n, next_stamp(lm, 9));
 }
 
+// The decode lm_head on the tcgen05 GEMM instead of the GEMV: TF32x3 math,
+// fp32 weights, at least 32 rows and 148 column tiles of 128 (one per SM),
+// and room for the logits in the engine's scratch rows.
+bool lm_head_on_tensor_cores(const fml_lm* lm)
+{
+    const uint64_t d = lm->cfg.d_model;
+    return lm->prefill_math == FML_MATH_TF32X3 && lm->weight_format == FML_WEIGHTS_FP32 && lm->batch >= 32 &&
+           (lm->vl + 127) / 128 >= 148 && d % 4 == 0 &&
+           (uint64_t)lm->batch * lm->vl <= (uint64_t)lm->cfg.max_batch * lm->cfg.context * 3 * lm->dl;
+}
+
 // Enqueue one decode step for the active batch: embed, per layer
 // {qkv (LayerNorm fused) -> attention -> proj + residual -> fc (LayerNorm
 // fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
@@ -1474,7 +1518,22 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
         a.x = lm->x; a.ldx = d; a.w = lm->tok + (uint64_t)lm->v0 * d; a.M = B; a.N = lm->vl; a.K = d;
         a.gamma = lm->lnf; a.y = logits; a.ldy = lm->vl; a.keys = lm->keys; a.n_off = lm->v0;
         if (wb) a.wb = lm->head_b;
-        FML_RC((decode_gemv<EPI_ARGMAX, true>(lm, a, 7, st, pdl && !tp)));
+        if (lm_head_on_tensor_cores(lm))
+        {
+            // at >= 32 rows and a vocabulary of >= 148 column tiles (config
+            // 4: 64 rows x 32000) the GEMV's row chunks re-read the table
+            // (131 MB, past L2): LayerNorm rows, then the tcgen05 GEMM (TF32x3)
+            // streams the table once, then the argmax keys
+            float* lg = logits ? logits : lm->tmp;
+            FML_RC(launch_layernorm(lm->ln, lm->x, lm->lnf, nullptr, nullptr, B, d, d, d, 1e-5f, st));
+            FML_RC(gemm_tc(lg, lm->ln, lm->tok + (uint64_t)lm->v0 * d, (int)B, (int)lm->vl, (int)d, (int)d, (int)d,
+                           (int)lm->vl, true, 0, nullptr, st));
+            const uint32_t chunks = std::min<uint32_t>(64u, (lm->vl + 2047u) / 2048u);
+            FML_RC(launch_k(argmax_rows_kernel, dim3(chunks, B), dim3(256), st, false, (const float*)lg, lm->vl,
+                            lm->vl, lm->v0, lm->keys, next_stamp(lm, 7)));
+        }
+        else
+            FML_RC((decode_gemv<EPI_ARGMAX, true>(lm, a, 7, st, pdl && !tp)));
         if (tp) FML_RC(all_reduce_max_keys(lm, B, st));
     }
     {
@@ -2191,6 +2250,7 @@ int enqueue_step_host(fml_lm* lm, cudaStream_t st)
 {
     FML_RC(check_step_state(lm, "fml_lm_step_host"));
     FML_RC(ensure_weight_bf16(lm, st));
+    if (lm_head_on_tensor_cores(lm)) FML_RC(gemm_tc_prepare(true, 0));
     const uint32_t B = lm->batch;
     uint32_t* dev_next = lm->prompt_dev;  // scratch slot for the step's output tokens
     if (lm->use_graph && !lm->profiling)
@@ -2223,6 +2283,7 @@ int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t s
     FML_RC(check_step_state(lm, "fml_lm_step"));
     cudaStream_t st = as_stream(stream);
     FML_RC(ensure_weight_bf16(lm, st));
+    if (lm_head_on_tensor_cores(lm)) FML_RC(gemm_tc_prepare(true, 0));  // no attribute call inside a capture
     if (lm->use_graph && !lm->profiling)
     {
         if (!lm->graph_exec || lm->graph_next != next_tokens || lm->graph_logits != logits ||
@@ -2258,6 +2319,7 @@ int fml_lm_steps(fml_lm* lm, uint32_t n, fml_stream_t stream)
                              b, lm->cfg.context);
     cudaStream_t st = as_stream(stream);
     FML_RC(ensure_weight_bf16(lm, st));
+    if (lm_head_on_tensor_cores(lm)) FML_RC(gemm_tc_prepare(true, 0));
     if (!lm->use_graph || lm->profiling)
     {
         for (uint32_t i = 0; i < n; ++i) FML_RC(fml_lm_step(lm, nullptr, nullptr, stream));
