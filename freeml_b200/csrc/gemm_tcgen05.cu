@@ -168,6 +168,10 @@ struct TcArgs
     float* vc;
     int P, hd, dq, ctx;
     uint64_t seq_stride;
+    // split K (TC_STORE only): tile t covers k-blocks [ks kbs, (ks + 1) kbs)
+    // of K with ks = t / (M and N tiles), and stores its partial product to
+    // C + ks * M * ldc; 0 or 1 = no split
+    int ksplit;
 };
 
 // One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x +
@@ -212,9 +216,11 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kblocks = (args.K + BK - 1) / BK;
+    const int ksplit = args.ksplit > 1 ? args.ksplit : 1;
+    const int kblocks = (args.K + BK - 1) / BK / ksplit;  // k-blocks per tile (host: divisible)
     const int tiles_n = (args.N + BN - 1) / BN;
-    const int ntiles = tiles_n * ((args.M + BM - 1) / BM);
+    const int tiles_mn = tiles_n * ((args.M + BM - 1) / BM);
+    const int ntiles = tiles_mn * ksplit;
 
     if (threadIdx.x == 0)
     {
@@ -254,23 +260,24 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
             uint32_t it = 0;  // k-blocks issued over all tiles
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
             {
-                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+                const int tmn = t % tiles_mn, k0 = (t / tiles_mn) * kblocks * BK;
+                const int m0 = (tmn / tiles_n) * BM, n0 = (tmn % tiles_n) * BN;
                 for (int kb = 0; kb < kblocks; ++kb, ++it)
                 {
                     const int s = it % STAGES;
                     if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { ok = false; break; }
                     mbar_arrive_expect_tx(&full[s], (BLO ? 3 : 2) * TILE_BYTES);
-                    tma_load_2d(tile_ptr(s, 0), &map_a, kb * BK, m0, &full[s]);
+                    tma_load_2d(tile_ptr(s, 0), &map_a, k0 + kb * BK, m0, &full[s]);
                     if constexpr (BMN)
                     {
 #pragma unroll
                         for (int j = 0; j < BN / (int)MN_BOX; ++j)
                             tma_load_2d(tile_ptr(s, 1) + j * (MN_BOX * BK * 4), &map_b, n0 + j * (int)MN_BOX,
-                                        kb * BK, &full[s]);
+                                        k0 + kb * BK, &full[s]);
                     }
                     else
-                        tma_load_2d(tile_ptr(s, 1), &map_b, kb * BK, n0, &full[s]);
-                    if constexpr (BLO) tma_load_2d(tile_ptr(s, 2), &map_blo, kb * BK, n0, &full[s]);
+                        tma_load_2d(tile_ptr(s, 1), &map_b, k0 + kb * BK, n0, &full[s]);
+                    if constexpr (BLO) tma_load_2d(tile_ptr(s, 2), &map_blo, k0 + kb * BK, n0, &full[s]);
                 }
             }
             // the last STAGES loads issued (all earlier ones were consumed):
@@ -384,15 +391,17 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
             const uint32_t buf = j & 1u, use = j >> 1;
             if (!__all_sync(FULL_MASK, mbar_wait(&acc_full[buf], use & 1))) { ok = false; break; }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+            const int tmn = t % tiles_mn;
+            const int m0 = (tmn / tiles_n) * BM, n0 = (tmn % tiles_n) * BN;
             const int row = m0 + lg * 32 + lane;
+            float* const cbase = args.C + (uint64_t)(t / tiles_mn) * args.M * args.ldc;  // split-K plane
             for (int c0 = 0; c0 < BN; c0 += 32)
             {
                 float v[32];
                 tc::tmem_ld32(tmem_base + ((uint32_t)(lg * 32) << 16) + buf * TMEM_COLS + (uint32_t)c0, v);
                 if (row < args.M)
                 {
-                    float* crow = args.C + (uint64_t)row * args.ldc + n0 + c0;
+                    float* crow = cbase + (uint64_t)row * args.ldc + n0 + c0;
                     if constexpr (EPI == TC_QKV)
                     {
                         // a 32-column slice lies inside one head of one part
@@ -494,17 +503,23 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     int dev = 0, sms = 0;
     FML_CUDA_TRY(cudaGetDevice(&dev));
     FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int ntiles = ((args.N + tc::BN - 1) / tc::BN) * ((args.M + tc::BM - 1) / tc::BM);
+    const int ntiles = ((args.N + tc::BN - 1) / tc::BN) * ((args.M + tc::BM - 1) / tc::BM) * std::max(1, args.ksplit);
     gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN><<<std::min(ntiles, sms), 320, smem, st>>>(ma, mb, mblo, args);
     FML_LAUNCH_CHECK();
     return FML_OK;
 }
 
 // Raise the dynamic shared-memory limit of gemm_tc's kernel for (split3,
-// epi, no B_lo) on the current device, so that a later launch inside a
+// epi, B_lo given) on the current device, so that a later launch inside a
 // stream capture makes no attribute call.
-int gemm_tc_prepare(bool split3, int epi)
+int gemm_tc_prepare(bool split3, int epi, bool blo)
 {
+    if (split3 && blo)
+    {
+        if (epi == TC_GELU) return tc_smem_setup<true, TC_GELU, true, false>();
+        if (epi == TC_RESID) return tc_smem_setup<true, TC_RESID, true, false>();
+        return tc_smem_setup<true, TC_STORE, true, false>();
+    }
     if (split3)
     {
         if (epi == TC_GELU) return tc_smem_setup<true, TC_GELU, false, false>();
@@ -576,6 +591,32 @@ int gemm_tc_qkv(float* q, int ldq, float* kc, float* vc, uint64_t seq_stride, in
     if (blo) return launch_tc<true, TC_QKV, true>(ma, mb, mblo, args, st);
     if (split3) return launch_tc<true, TC_QKV>(ma, mb, mblo, args, st);
     return launch_tc<false, TC_QKV>(ma, mb, mblo, args, st);
+}
+
+// Split-K partial products for few rows (the decode contractions at 33-64
+// rows): part[s] = A[:, s Ks:(s+1) Ks] . B[:, s Ks:(s+1) Ks]^T for s <
+// ksplit (Ks = K / ksplit, a multiple of 32), each [M x N] (row stride N)
+// at part + s M N.  The caller sums the planes in order.
+int gemm_tc_splitk(float* part, const float* A, const float* B, int M, int N, int K, int lda, int ldb, bool split3,
+                   int ksplit, cudaStream_t st, const float* B_lo)
+{
+    if (M <= 0 || N <= 0) return FML_OK;
+    FML_REQUIRE(K > 0 && ksplit >= 1 && K % (32 * ksplit) == 0,
+                "gemm_tc_splitk: K %d must be a multiple of 32 x ksplit (%d)", K, ksplit);
+    FML_REQUIRE(aligned16(A) && aligned16(B) && aligned16(part) && lda % 4 == 0 && ldb % 4 == 0 && N % 4 == 0 &&
+                    (!B_lo || aligned16(B_lo)),
+                "gemm_tc_splitk: operands must be 16-byte aligned with row strides that are multiples of 4");
+    CUtensorMap ma, mb, mblo;
+    FML_RC(tc::make_map(&ma, A, M, K, lda, tc::BM));
+    FML_RC(tc::make_map(&mb, B, N, K, ldb, tc::BN));
+    const bool blo = split3 && B_lo;
+    if (blo) FML_RC(tc::make_map(&mblo, B_lo, N, K, ldb, tc::BN));
+    else mblo = mb;
+    TcArgs args{M, N, K, part, N, nullptr, true};
+    args.ksplit = ksplit;
+    if (blo) return launch_tc<true, TC_STORE, true>(ma, mb, mblo, args, st);
+    if (split3) return launch_tc<true, TC_STORE>(ma, mb, mblo, args, st);
+    return launch_tc<false, TC_STORE>(ma, mb, mblo, args, st);
 }
 
 // C = A . B on the tensor cores with B [K x N] row-major (row stride ldb):

@@ -66,7 +66,9 @@ int gemm_tc_qkv(float* q, int ldq, float* kc, float* vc, uint64_t seq_stride, in
                 const float* A, const float* B, int M, int dq, int K, bool split3, cudaStream_t st,
                 const float* B_lo = nullptr);
 int tf32_lo(float* lo, const float* x, uint64_t n, cudaStream_t st);
-int gemm_tc_prepare(bool split3, int epi);
+int gemm_tc_prepare(bool split3, int epi, bool blo = false);
+int gemm_tc_splitk(float* part, const float* A, const float* B, int M, int N, int K, int lda, int ldb, bool split3,
+                   int ksplit, cudaStream_t st, const float* B_lo = nullptr);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
                              uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
@@ -876,6 +878,53 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
     }
 }
 
+// The decode rows' split-K tensor-core contractions: v = sum of the S
+// partial planes part[s] [M x N] in plane order (deterministic), then the
+// GEMV's epilogue (a.y / a.r / a.q / K/V cache at a.pos, as in
+// gemv_team_kernel), four consecutive columns per thread (N, the row
+// strides and hd are multiples of 4, so the four share a head).
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, uint32_t S, GemvArgs a)
+{
+    const StampAtExit stamp_at_exit(a.stamp);
+    griddep_launch_dependents();
+    const uint32_t N = a.N;
+    const uint64_t plane = (uint64_t)a.M * N, n4 = plane / 4;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x)
+    {
+        float4 v = reinterpret_cast<const float4*>(part)[i];
+        for (uint32_t s = 1; s < S; ++s)
+        {
+            const float4 w = reinterpret_cast<const float4*>(part + s * plane)[i];
+            v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+        }
+        const uint32_t m = (uint32_t)(4 * i / N), n = (uint32_t)(4 * i - (uint64_t)m * N);
+        if constexpr (EPI == EPI_STORE)
+            *reinterpret_cast<float4*>(a.y + (uint64_t)m * a.ldy + n) = v;
+        else if constexpr (EPI == EPI_GELU)
+            *reinterpret_cast<float4*>(a.y + (uint64_t)m * a.ldy + n) =
+                make_float4(gelu_exact(v.x), gelu_exact(v.y), gelu_exact(v.z), gelu_exact(v.w));
+        else if constexpr (EPI == EPI_RESID)
+        {
+            const float4 r = *reinterpret_cast<const float4*>(a.r + (uint64_t)m * a.ldr + n);
+            *reinterpret_cast<float4*>(a.y + (uint64_t)m * a.ldy + n) =
+                make_float4(r.x + v.x, r.y + v.y, r.z + v.z, r.w + v.w);
+        }
+        else if constexpr (EPI == EPI_QKV)
+        {
+            float* dst;
+            if (n < a.d) dst = a.q + (uint64_t)m * a.d + n;
+            else
+            {
+                const uint32_t cc = n < 2 * a.d ? n - a.d : n - 2 * a.d;
+                dst = (n < 2 * a.d ? a.kc : a.vc) + (uint64_t)m * a.seq_stride +
+                      ((uint64_t)(cc / a.hd) * a.C + a.pos[m]) * a.hd + cc % a.hd;
+            }
+            *reinterpret_cast<float4*>(dst) = v;
+        }
+    }
+}
+
 // Argmax keys of logits rows (the tensor-core lm_head): keys[m] = max over
 // this CTA's columns n of argmax_key(logits[m][n], n + n_off), folded into
 // the row's key with one atomicMax per CTA (keys start at zero: finalize
@@ -1432,6 +1481,48 @@ bool lm_head_on_tensor_cores(const fml_lm* lm)
            (uint64_t)lm->batch * lm->vl <= (uint64_t)lm->cfg.max_batch * lm->cfg.context * 3 * lm->dl;
 }
 
+// The decode contractions on the tcgen05 GEMM (split K, then a reduction
+// with the GEMV's epilogue): TF32x3 math, fp32 weights, one rank, more than
+// 32 rows and d >= 1024 (config 4: 64 rows) -- there the CUDA-core GEMV's 8
+// row chunks re-read each weight 8 times and walk 5-54 column-group rounds
+// per warp.
+bool decode_on_tensor_cores(const fml_lm* lm)
+{
+    return lm->prefill_math == FML_MATH_TF32X3 && lm->weight_format == FML_WEIGHTS_FP32 && lm->tp_world == 1 &&
+           lm->batch > 32 && lm->cfg.d_model >= 1024 && lm->cfg.d_model % 128 == 0;
+}
+
+// One decode contraction y = epilogue(A . W^T) on the tensor cores: the K
+// split doubles (K / 32 divisible) while the tiles still fit one wave.
+template <int EPI>
+int decode_tc_gemm(fml_lm* lm, GemvArgs a, const float* W_lo, int cls, cudaStream_t st)
+{
+    const uint32_t tiles = (a.N + 127) / 128 * ((a.M + 127) / 128);
+    uint32_t ks = 1;
+    while (ks < 16 && tiles * ks * 2 <= 148 && (a.K / 32) % (ks * 2) == 0) ks *= 2;
+    float* part = lm->tmp;
+    FML_REQUIRE((uint64_t)ks * a.M * a.N <= (uint64_t)lm->cfg.max_batch * lm->cfg.context * 3 * lm->dl,
+                "decode_tc_gemm: split-K partials exceed the scratch rows");
+    FML_RC(gemm_tc_splitk(part, a.x, a.w, (int)a.M, (int)a.N, (int)a.K, (int)a.ldx, (int)a.K, true, (int)ks, st,
+                          lm->wlo_valid ? W_lo : nullptr));
+    a.stamp = next_stamp(lm, cls);
+    const uint64_t n4 = (uint64_t)a.M * a.N / 4;
+    return launch_k(splitk_reduce_kernel<EPI>, dim3((unsigned)std::min<uint64_t>((n4 + 255) / 256, 148u * 8u)),
+                    dim3(256), st, false, (const float*)part, ks, a);
+}
+
+// The tcgen05 kernels a decode step may launch get their shared-memory
+// limit before any capture records the step.
+int prepare_tc_decode(const fml_lm* lm)
+{
+    if (lm_head_on_tensor_cores(lm) || decode_on_tensor_cores(lm))
+    {
+        FML_RC(gemm_tc_prepare(true, 0, false));
+        FML_RC(gemm_tc_prepare(true, 0, true));
+    }
+    return FML_OK;
+}
+
 // Enqueue one decode step for the active batch: embed, per layer
 // {qkv (LayerNorm fused) -> attention -> proj + residual -> fc (LayerNorm
 // fused) + GELU -> mlp + residual}, lm_head (final LayerNorm fused) + argmax,
@@ -1460,6 +1551,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
     const bool resid_here = lm->tp_rank == 0;  // row-parallel sums take the residual once
     const bool wb = lm->weight_format == FML_WEIGHTS_BF16;
     FML_REQUIRE(!wb || lm->wb16_valid, "decode step: the bf16 weight copy is not ready");
+    const bool dtc = decode_on_tensor_cores(lm);  // rows of LayerNorm, tcgen05 split-K, reduction
+    auto lo = [&](const std::vector<float*>& v, uint32_t l) { return lm->wlo_valid ? v[l] : nullptr; };
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         {
@@ -1469,7 +1562,14 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             if (wb) a.wb = lm->wqkv_b[l];
             a.q = lm->q; a.kc = lm->kc + (uint64_t)l * lm->layer_stride; a.vc = lm->vc + (uint64_t)l * lm->layer_stride;
             a.pos = lm->pos; a.d = lm->dl; a.H = lm->hl; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
-            FML_RC((decode_gemv<EPI_QKV, true>(lm, a, 2, st, pdl)));
+            if (dtc)
+            {
+                FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
+                a.x = lm->ln;
+                FML_RC(decode_tc_gemm<EPI_QKV>(lm, a, lo(lm->wqkv_lo, l), 2, st));
+            }
+            else
+                FML_RC((decode_gemv<EPI_QKV, true>(lm, a, 2, st, pdl)));
         }
         {
             ProfScope ps(lm, 3, st);
@@ -1481,7 +1581,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             if (wb) a.wb = lm->wproj_b[l];
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, 4, st, pdl));
+            if (dtc) FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wproj_lo, l), 4, st));
+            else if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, 4, st, pdl));
             else
             {
                 if (resid_here) FML_RC((decode_gemv<EPI_RESID, false>(lm, a, 4, st, pdl)));
@@ -1495,7 +1596,14 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.x = lm->buf; a.ldx = d; a.w = lm->wfc[l]; a.M = B; a.N = lm->fl; a.K = d; a.gamma = lm->ln1[l];
             if (wb) a.wb = lm->wfc_b[l];
             a.y = lm->hid; a.ldy = lm->fl;
-            FML_RC((decode_gemv<EPI_GELU, true>(lm, a, 5, st, pdl && (!tp || lm->ar_fused))));
+            if (dtc)
+            {
+                FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
+                a.x = lm->ln;
+                FML_RC(decode_tc_gemm<EPI_GELU>(lm, a, lo(lm->wfc_lo, l), 5, st));
+            }
+            else
+                FML_RC((decode_gemv<EPI_GELU, true>(lm, a, 5, st, pdl && (!tp || lm->ar_fused))));
         }
         {
             ProfScope ps(lm, 6, st);
@@ -1503,7 +1611,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             if (wb) a.wb = lm->wmlp_b[l];
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, 6, st, pdl));
+            if (dtc) FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wmlp_lo, l), 6, st));
+            else if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, 6, st, pdl));
             else
             {
                 if (resid_here) FML_RC((decode_gemv<EPI_RESID, false>(lm, a, 6, st, pdl)));
@@ -2250,7 +2359,7 @@ int enqueue_step_host(fml_lm* lm, cudaStream_t st)
 {
     FML_RC(check_step_state(lm, "fml_lm_step_host"));
     FML_RC(ensure_weight_bf16(lm, st));
-    if (lm_head_on_tensor_cores(lm)) FML_RC(gemm_tc_prepare(true, 0));
+    FML_RC(prepare_tc_decode(lm));
     const uint32_t B = lm->batch;
     uint32_t* dev_next = lm->prompt_dev;  // scratch slot for the step's output tokens
     if (lm->use_graph && !lm->profiling)
@@ -2283,7 +2392,7 @@ int fml_lm_step(fml_lm* lm, uint32_t* next_tokens, float* logits, fml_stream_t s
     FML_RC(check_step_state(lm, "fml_lm_step"));
     cudaStream_t st = as_stream(stream);
     FML_RC(ensure_weight_bf16(lm, st));
-    if (lm_head_on_tensor_cores(lm)) FML_RC(gemm_tc_prepare(true, 0));  // no attribute call inside a capture
+    FML_RC(prepare_tc_decode(lm));  // no attribute call inside a capture
     if (lm->use_graph && !lm->profiling)
     {
         if (!lm->graph_exec || lm->graph_next != next_tokens || lm->graph_logits != logits ||
@@ -2319,7 +2428,7 @@ int fml_lm_steps(fml_lm* lm, uint32_t n, fml_stream_t stream)
                              b, lm->cfg.context);
     cudaStream_t st = as_stream(stream);
     FML_RC(ensure_weight_bf16(lm, st));
-    if (lm_head_on_tensor_cores(lm)) FML_RC(gemm_tc_prepare(true, 0));
+    FML_RC(prepare_tc_decode(lm));
     if (!lm->use_graph || lm->profiling)
     {
         for (uint32_t i = 0; i < n; ++i) FML_RC(fml_lm_step(lm, nullptr, nullptr, stream));
