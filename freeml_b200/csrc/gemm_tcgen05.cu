@@ -172,6 +172,7 @@ struct TcArgs
     // of K with ks = t / (M and N tiles), and stores its partial product to
     // C + ks * M * ldc; 0 or 1 = no split
     int ksplit;
+    bool pdl;  // launch under programmatic dependent launch
 };
 
 // One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x +
@@ -253,32 +254,64 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
 
     auto tile_ptr = [&](int stage, int which) { return tiles + (stage * NT + which) * TILE_BYTES; };
 
+    // Programmatic dependent launch (the decode contractions): the weight
+    // operand B does not depend on the previous kernel, so the first STAGES
+    // stages' B tiles are requested before griddepcontrol.wait and their A
+    // tiles after it; every role that touches global memory the previous
+    // kernel writes (the A loads, the epilogue's residual reads and its
+    // stores into buffers that kernel may still read) waits first.  Without
+    // the launch attribute the wait returns at once.
+    griddep_launch_dependents();
     if (warp == 0)
     {
         if (lane == 0)
         {
-            uint32_t it = 0;  // k-blocks issued over all tiles
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x)
-            {
-                const int tmn = t % tiles_mn, k0 = (t / tiles_mn) * kblocks * BK;
-                const int m0 = (tmn / tiles_n) * BM, n0 = (tmn % tiles_n) * BN;
-                for (int kb = 0; kb < kblocks; ++kb, ++it)
+            // iteration it of this CTA: its (it / kblocks)-th tile, k-block it % kblocks
+            auto coords = [&](uint32_t i, int& k, int& m0, int& n0) {
+                const int t = (int)blockIdx.x + (int)(i / (uint32_t)kblocks) * (int)gridDim.x;
+                const int tmn = t % tiles_mn;
+                k = (t / tiles_mn) * kblocks * BK + (int)(i % (uint32_t)kblocks) * BK;
+                m0 = (tmn / tiles_n) * BM;
+                n0 = (tmn % tiles_n) * BN;
+            };
+            auto load_b = [&](int s, int k, int n0) {
+                if constexpr (BMN)
                 {
-                    const int s = it % STAGES;
-                    if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], (BLO ? 3 : 2) * TILE_BYTES);
-                    tma_load_2d(tile_ptr(s, 0), &map_a, k0 + kb * BK, m0, &full[s]);
-                    if constexpr (BMN)
-                    {
 #pragma unroll
-                        for (int j = 0; j < BN / (int)MN_BOX; ++j)
-                            tma_load_2d(tile_ptr(s, 1) + j * (MN_BOX * BK * 4), &map_b, n0 + j * (int)MN_BOX,
-                                        k0 + kb * BK, &full[s]);
-                    }
-                    else
-                        tma_load_2d(tile_ptr(s, 1), &map_b, k0 + kb * BK, n0, &full[s]);
-                    if constexpr (BLO) tma_load_2d(tile_ptr(s, 2), &map_blo, k0 + kb * BK, n0, &full[s]);
+                    for (int j = 0; j < BN / (int)MN_BOX; ++j)
+                        tma_load_2d(tile_ptr(s, 1) + j * (MN_BOX * BK * 4), &map_b, n0 + j * (int)MN_BOX, k, &full[s]);
                 }
+                else
+                    tma_load_2d(tile_ptr(s, 1), &map_b, k, n0, &full[s]);
+                if constexpr (BLO) tma_load_2d(tile_ptr(s, 2), &map_blo, k, n0, &full[s]);
+            };
+            const uint32_t mytiles = (uint32_t)((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+            const uint32_t total = (uint32_t)kblocks * (blockIdx.x < (unsigned)ntiles ? mytiles : 0u);
+            const uint32_t pre = total < (uint32_t)STAGES ? total : (uint32_t)STAGES;
+            for (uint32_t i = 0; i < pre; ++i)
+            {
+                int k, m0, n0;
+                coords(i, k, m0, n0);
+                mbar_arrive_expect_tx(&full[i], (BLO ? 3 : 2) * TILE_BYTES);
+                load_b((int)i, k, n0);
+            }
+            griddep_wait();
+            for (uint32_t i = 0; i < pre; ++i)
+            {
+                int k, m0, n0;
+                coords(i, k, m0, n0);
+                tma_load_2d(tile_ptr((int)i, 0), &map_a, k, m0, &full[i]);
+            }
+            uint32_t it = pre;  // k-blocks issued over all tiles
+            for (; it < total && ok; ++it)
+            {
+                const int s = it % STAGES;
+                if (!mbar_wait(&empty[s], ((it / STAGES) - 1) & 1)) { ok = false; break; }
+                int k, m0, n0;
+                coords(it, k, m0, n0);
+                mbar_arrive_expect_tx(&full[s], (BLO ? 3 : 2) * TILE_BYTES);
+                tma_load_2d(tile_ptr(s, 0), &map_a, k, m0, &full[s]);
+                load_b(s, k, n0);
             }
             // the last STAGES loads issued (all earlier ones were consumed):
             // none may still be landing when the CTA exits
@@ -385,6 +418,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tcgen05_kernel(const __grid_const
         // warps 6..9: drain the accumulators; warp w reads TMEM lanes
         // 32 (w % 4) .. 32 (w % 4) + 31
         const int lg = warp & 3;
+        griddep_wait();  // residual reads and output stores follow the previous kernel
         uint32_t j = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++j)
         {
@@ -504,7 +538,18 @@ static int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
     FML_CUDA_TRY(cudaGetDevice(&dev));
     FML_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int ntiles = ((args.N + tc::BN - 1) / tc::BN) * ((args.M + tc::BM - 1) / tc::BM) * std::max(1, args.ksplit);
-    gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN><<<std::min(ntiles, sms), 320, smem, st>>>(ma, mb, mblo, args);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min(ntiles, sms));
+    cfg.blockDim = dim3(320);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = args.pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05_kernel<SPLIT3, EPI, BLO, BMN>, ma, mb, mblo, args);
+    if (e != cudaSuccess) return set_error(FML_ERR_CUDA, "gemm_tcgen05 launch: %s", cudaGetErrorString(e));
     FML_LAUNCH_CHECK();
     return FML_OK;
 }
@@ -596,9 +641,11 @@ int gemm_tc_qkv(float* q, int ldq, float* kc, float* vc, uint64_t seq_stride, in
 // Split-K partial products for few rows (the decode contractions at 33-64
 // rows): part[s] = A[:, s Ks:(s+1) Ks] . B[:, s Ks:(s+1) Ks]^T for s <
 // ksplit (Ks = K / ksplit, a multiple of 32), each [M x N] (row stride N)
-// at part + s M N.  The caller sums the planes in order.
+// at part + s M N.  The caller sums the planes in order.  pdl: launch under
+// programmatic dependent launch (the B tiles of the first stages load
+// while the previous kernel finishes).
 int gemm_tc_splitk(float* part, const float* A, const float* B, int M, int N, int K, int lda, int ldb, bool split3,
-                   int ksplit, cudaStream_t st, const float* B_lo)
+                   int ksplit, cudaStream_t st, const float* B_lo, bool pdl)
 {
     if (M <= 0 || N <= 0) return FML_OK;
     FML_REQUIRE(K > 0 && ksplit >= 1 && K % (32 * ksplit) == 0,
@@ -614,6 +661,7 @@ int gemm_tc_splitk(float* part, const float* A, const float* B, int M, int N, in
     else mblo = mb;
     TcArgs args{M, N, K, part, N, nullptr, true};
     args.ksplit = ksplit;
+    args.pdl = pdl;
     if (blo) return launch_tc<true, TC_STORE, true>(ma, mb, mblo, args, st);
     if (split3) return launch_tc<true, TC_STORE>(ma, mb, mblo, args, st);
     return launch_tc<false, TC_STORE>(ma, mb, mblo, args, st);

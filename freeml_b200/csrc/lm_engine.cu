@@ -68,7 +68,7 @@ int gemm_tc_qkv(float* q, int ldq, float* kc, float* vc, uint64_t seq_stride, in
 int tf32_lo(float* lo, const float* x, uint64_t n, cudaStream_t st);
 int gemm_tc_prepare(bool split3, int epi, bool blo = false);
 int gemm_tc_splitk(float* part, const float* A, const float* B, int M, int N, int K, int lda, int ldb, bool split3,
-                   int ksplit, cudaStream_t st, const float* B_lo = nullptr);
+                   int ksplit, cudaStream_t st, const float* B_lo = nullptr, bool pdl = false);
 int gemv_nt(float* y, const float* x, const float* w, uint32_t M, uint32_t N, uint32_t K, cudaStream_t st);
 int launch_prefill_attention(const float* q, uint32_t ldq, const float* kc, const float* vc, uint64_t seq_stride,
                              uint32_t C, float* out, uint32_t ldo, uint32_t B, uint32_t H, uint32_t P, uint32_t hd,
@@ -183,6 +183,10 @@ struct GemvArgs
 
     // LN prologue: gamma [K] (beta absent, NanoLLM's use_bias = false)
     const float* gamma;
+    // split-K reduction with a LayerNorm of the finished rows: ln_out [M x N]
+    // (row stride N) = LayerNormOp(y) with ln_gamma
+    float* ln_out;
+    const float* ln_gamma;
     StepStamp stamp;  // optional completion stamp
 };
 
@@ -888,6 +892,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 {
     const StampAtExit stamp_at_exit(a.stamp);
     griddep_launch_dependents();
+    griddep_wait();  // the partials come from the previous kernel
     const uint32_t N = a.N;
     const uint64_t plane = (uint64_t)a.M * N, n4 = plane / 4;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x)
@@ -922,6 +927,70 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
             }
             *reinterpret_cast<float4*>(dst) = v;
         }
+    }
+}
+
+// The same reduction for a residual output, y = r + sum of the planes, one
+// CTA per row, followed by the LayerNorm the next contraction needs
+// (LayerNorm.h:148-165: two-pass mean and biased variance over the row held
+// in registers): ln_out = LayerNormOp(y) with ln_gamma.  N = 1024 NV.
+template <int NV>
+__global__ void __launch_bounds__(256) splitk_reduce_ln_kernel(const float* __restrict__ part, uint32_t S, GemvArgs a)
+{
+    const StampAtExit stamp_at_exit(a.stamp);
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ float red[8];
+    const uint32_t m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t N = a.N;
+    const uint64_t plane = (uint64_t)a.M * N;
+    float4 v[NV];
+    float s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+    {
+        const uint32_t n = 4 * (tid + 256 * i);
+        const uint64_t off = (uint64_t)m * N + n;
+        float4 x = *reinterpret_cast<const float4*>(part + off);
+        for (uint32_t s = 1; s < S; ++s)
+        {
+            const float4 w = *reinterpret_cast<const float4*>(part + s * plane + off);
+            x.x += w.x; x.y += w.y; x.z += w.z; x.w += w.w;
+        }
+        const float4 r = *reinterpret_cast<const float4*>(a.r + (uint64_t)m * a.ldr + n);
+        x = make_float4(r.x + x.x, r.y + x.y, r.z + x.z, r.w + x.w);
+        *reinterpret_cast<float4*>(a.y + (uint64_t)m * a.ldy + n) = x;
+        v[i] = x;
+        s1 += (x.x + x.y) + (x.z + x.w);
+    }
+    auto block_sum = [&](float t) {
+        t = warp_sum(t);
+        __syncthreads();  // red[] of a previous sum has been read
+        if (lane == 0) red[warp] = t;
+        __syncthreads();
+        float u = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) u += red[w];
+        return u;
+    };
+    const float invN = 1.0f / (float)N;
+    const float mean = block_sum(s1) * invN;
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+    {
+        const float d0 = v[i].x - mean, d1 = v[i].y - mean, d2 = v[i].z - mean, d3 = v[i].w - mean;
+        s2 = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, fmaf(d3, d3, s2))));
+    }
+    const float rstd = 1.0f / sqrtf(fmaf(block_sum(s2), invN, 1e-5f));
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+    {
+        const uint32_t n = 4 * (tid + 256 * i);
+        const float4 g = *reinterpret_cast<const float4*>(a.ln_gamma + n);
+        *reinterpret_cast<float4*>(a.ln_out + (uint64_t)m * N + n) =
+            make_float4((v[i].x - mean) * rstd * g.x, (v[i].y - mean) * rstd * g.y, (v[i].z - mean) * rstd * g.z,
+                        (v[i].w - mean) * rstd * g.w);
     }
 }
 
@@ -1489,13 +1558,13 @@ bool lm_head_on_tensor_cores(const fml_lm* lm)
 bool decode_on_tensor_cores(const fml_lm* lm)
 {
     return lm->prefill_math == FML_MATH_TF32X3 && lm->weight_format == FML_WEIGHTS_FP32 && lm->tp_world == 1 &&
-           lm->batch > 32 && lm->cfg.d_model >= 1024 && lm->cfg.d_model % 128 == 0;
+           lm->batch > 32 && lm->cfg.d_model % 1024 == 0 && lm->cfg.d_model <= 4096;
 }
 
 // One decode contraction y = epilogue(A . W^T) on the tensor cores: the K
 // split doubles (K / 32 divisible) while the tiles still fit one wave.
 template <int EPI>
-int decode_tc_gemm(fml_lm* lm, GemvArgs a, const float* W_lo, int cls, cudaStream_t st)
+int decode_tc_gemm(fml_lm* lm, GemvArgs a, const float* W_lo, int cls, cudaStream_t st, bool pdl)
 {
     const uint32_t tiles = (a.N + 127) / 128 * ((a.M + 127) / 128);
     uint32_t ks = 1;
@@ -1504,11 +1573,17 @@ int decode_tc_gemm(fml_lm* lm, GemvArgs a, const float* W_lo, int cls, cudaStrea
     FML_REQUIRE((uint64_t)ks * a.M * a.N <= (uint64_t)lm->cfg.max_batch * lm->cfg.context * 3 * lm->dl,
                 "decode_tc_gemm: split-K partials exceed the scratch rows");
     FML_RC(gemm_tc_splitk(part, a.x, a.w, (int)a.M, (int)a.N, (int)a.K, (int)a.ldx, (int)a.K, true, (int)ks, st,
-                          lm->wlo_valid ? W_lo : nullptr));
+                          lm->wlo_valid ? W_lo : nullptr, pdl));
     a.stamp = next_stamp(lm, cls);
+    if (EPI == EPI_RESID && a.ln_out)
+    {
+        const uint32_t nv = a.N / 1024;
+        auto k = nv == 1 ? splitk_reduce_ln_kernel<1> : (nv == 2 ? splitk_reduce_ln_kernel<2> : splitk_reduce_ln_kernel<4>);
+        return launch_k(k, dim3(a.M), dim3(256), st, pdl, (const float*)part, ks, a);
+    }
     const uint64_t n4 = (uint64_t)a.M * a.N / 4;
     return launch_k(splitk_reduce_kernel<EPI>, dim3((unsigned)std::min<uint64_t>((n4 + 255) / 256, 148u * 8u)),
-                    dim3(256), st, false, (const float*)part, ks, a);
+                    dim3(256), st, pdl, (const float*)part, ks, a);
 }
 
 // The tcgen05 kernels a decode step may launch get their shared-memory
@@ -1564,9 +1639,11 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.pos = lm->pos; a.d = lm->dl; a.H = lm->hl; a.hd = lm->hd; a.C = c.context; a.seq_stride = lm->seq_stride;
             if (dtc)
             {
-                FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
+                // lm->ln holds LN0(x): the previous layer's mlp reduction (or,
+                // for layer 0, the LayerNorm after the embedding) made it
+                if (l == 0) FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[0], nullptr, nullptr, B, d, d, d, 1e-5f, st));
                 a.x = lm->ln;
-                FML_RC(decode_tc_gemm<EPI_QKV>(lm, a, lo(lm->wqkv_lo, l), 2, st));
+                FML_RC(decode_tc_gemm<EPI_QKV>(lm, a, lo(lm->wqkv_lo, l), 2, st, pdl && l > 0));
             }
             else
                 FML_RC((decode_gemv<EPI_QKV, true>(lm, a, 2, st, pdl)));
@@ -1581,7 +1658,12 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.x = lm->att; a.ldx = lm->dl; a.w = lm->wproj[l]; a.M = B; a.N = d; a.K = lm->dl;
             if (wb) a.wb = lm->wproj_b[l];
             a.y = lm->buf; a.ldy = d; a.r = lm->x; a.ldr = d;
-            if (dtc) FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wproj_lo, l), 4, st));
+            if (dtc)
+            {
+                a.ln_out = lm->ln;  // LN1(buf) for fc
+                a.ln_gamma = lm->ln1[l];
+                FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wproj_lo, l), 4, st, pdl));
+            }
             else if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, 4, st, pdl));
             else
             {
@@ -1598,9 +1680,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.y = lm->hid; a.ldy = lm->fl;
             if (dtc)
             {
-                FML_RC(launch_layernorm(lm->ln, lm->buf, lm->ln1[l], nullptr, nullptr, B, d, d, d, 1e-5f, st));
-                a.x = lm->ln;
-                FML_RC(decode_tc_gemm<EPI_GELU>(lm, a, lo(lm->wfc_lo, l), 5, st));
+                a.x = lm->ln;  // LN1(buf), made by the projection's reduction
+                FML_RC(decode_tc_gemm<EPI_GELU>(lm, a, lo(lm->wfc_lo, l), 5, st, pdl));
             }
             else
                 FML_RC((decode_gemv<EPI_GELU, true>(lm, a, 5, st, pdl && (!tp || lm->ar_fused))));
@@ -1611,7 +1692,13 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             a.x = lm->hid; a.ldx = lm->fl; a.w = lm->wmlp[l]; a.M = B; a.N = d; a.K = lm->fl;
             if (wb) a.wb = lm->wmlp_b[l];
             a.y = lm->x; a.ldy = d; a.r = lm->buf; a.ldr = d;
-            if (dtc) FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wmlp_lo, l), 6, st));
+            if (dtc)
+            {
+                // LN0 of the next layer, or ln_f after the last, for the lm_head
+                a.ln_out = lm->ln;
+                a.ln_gamma = l + 1 < c.n_layer ? lm->ln0[l + 1] : lm->lnf;
+                FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wmlp_lo, l), 6, st, pdl));
+            }
             else if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, 6, st, pdl));
             else
             {
@@ -1634,7 +1721,8 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             // (131 MB, past L2): LayerNorm rows, then the tcgen05 GEMM (TF32x3)
             // streams the table once, then the argmax keys
             float* lg = logits ? logits : lm->tmp;
-            FML_RC(launch_layernorm(lm->ln, lm->x, lm->lnf, nullptr, nullptr, B, d, d, d, 1e-5f, st));
+            // ln_f(x): made by the last mlp reduction on the tensor-core decode path
+            if (!dtc) FML_RC(launch_layernorm(lm->ln, lm->x, lm->lnf, nullptr, nullptr, B, d, d, d, 1e-5f, st));
             FML_RC(gemm_tc(lg, lm->ln, lm->tok + (uint64_t)lm->v0 * d, (int)B, (int)lm->vl, (int)d, (int)d, (int)d,
                            (int)lm->vl, true, 0, nullptr, st));
             const uint32_t chunks = std::min<uint32_t>(64u, (lm->vl + 2047u) / 2048u);
