@@ -882,6 +882,34 @@ __global__ void qkv_scatter_kernel(const float* __restrict__ qkv, float* __restr
     }
 }
 
+// Sum of the S partial planes at float4 offset i (plane stride `plane`
+// floats), added in plane order; the loads of four planes are requested
+// before any is added (one L2 round trip per four planes, not per plane).
+__device__ __forceinline__ float4 sum_planes(const float* __restrict__ part, uint64_t plane, uint64_t i, uint32_t S)
+{
+    const float4* p4 = reinterpret_cast<const float4*>(part);
+    const uint64_t pl4 = plane / 4;
+    float4 v = p4[i];
+    uint32_t s = 1;
+    for (; s + 4 <= S; s += 4)
+    {
+        float4 w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) w[u] = p4[(s + u) * pl4 + i];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+        {
+            v.x += w[u].x; v.y += w[u].y; v.z += w[u].z; v.w += w[u].w;
+        }
+    }
+    for (; s < S; ++s)
+    {
+        const float4 w = p4[s * pl4 + i];
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+    }
+    return v;
+}
+
 // The decode rows' split-K tensor-core contractions: v = sum of the S
 // partial planes part[s] [M x N] in plane order (deterministic), then the
 // GEMV's epilogue (a.y / a.r / a.q / K/V cache at a.pos, as in
@@ -897,12 +925,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     const uint64_t plane = (uint64_t)a.M * N, n4 = plane / 4;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x)
     {
-        float4 v = reinterpret_cast<const float4*>(part)[i];
-        for (uint32_t s = 1; s < S; ++s)
-        {
-            const float4 w = reinterpret_cast<const float4*>(part + s * plane)[i];
-            v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-        }
+        const float4 v = sum_planes(part, plane, i, S);
         const uint32_t m = (uint32_t)(4 * i / N), n = (uint32_t)(4 * i - (uint64_t)m * N);
         if constexpr (EPI == EPI_STORE)
             *reinterpret_cast<float4*>(a.y + (uint64_t)m * a.ldy + n) = v;
@@ -951,12 +974,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_ln_kernel(const float* __re
     {
         const uint32_t n = 4 * (tid + 256 * i);
         const uint64_t off = (uint64_t)m * N + n;
-        float4 x = *reinterpret_cast<const float4*>(part + off);
-        for (uint32_t s = 1; s < S; ++s)
-        {
-            const float4 w = *reinterpret_cast<const float4*>(part + s * plane + off);
-            x.x += w.x; x.y += w.y; x.z += w.z; x.w += w.w;
-        }
+        float4 x = sum_planes(part, plane, off / 4, S);
         const float4 r = *reinterpret_cast<const float4*>(a.r + (uint64_t)m * a.ldr + n);
         x = make_float4(r.x + x.x, r.y + x.y, r.z + x.z, r.w + x.w);
         *reinterpret_cast<float4*>(a.y + (uint64_t)m * a.ldy + n) = x;
@@ -1564,7 +1582,7 @@ bool decode_on_tensor_cores(const fml_lm* lm)
 // One decode contraction y = epilogue(A . W^T) on the tensor cores: the K
 // split doubles (K / 32 divisible) while the tiles still fit one wave.
 template <int EPI>
-int decode_tc_gemm(fml_lm* lm, GemvArgs a, const float* W_lo, int cls, cudaStream_t st, bool pdl)
+int decode_tc_gemm(fml_lm* lm, GemvArgs a, int cls, cudaStream_t st, bool pdl)
 {
     const uint32_t tiles = (a.N + 127) / 128 * ((a.M + 127) / 128);
     uint32_t ks = 1;
@@ -1572,8 +1590,11 @@ int decode_tc_gemm(fml_lm* lm, GemvArgs a, const float* W_lo, int cls, cudaStrea
     float* part = lm->tmp;
     FML_REQUIRE((uint64_t)ks * a.M * a.N <= (uint64_t)lm->cfg.max_batch * lm->cfg.context * 3 * lm->dl,
                 "decode_tc_gemm: split-K partials exceed the scratch rows");
+    // the weights' stored lo parts (the prefill's) would double the bytes a
+    // decode step streams: the converter warps split the weight tiles
+    // instead (measured on config 4: 2 192 -> 2 168 us per step)
     FML_RC(gemm_tc_splitk(part, a.x, a.w, (int)a.M, (int)a.N, (int)a.K, (int)a.ldx, (int)a.K, true, (int)ks, st,
-                          lm->wlo_valid ? W_lo : nullptr, pdl));
+                          nullptr, pdl));
     a.stamp = next_stamp(lm, cls);
     if (EPI == EPI_RESID && a.ln_out)
     {
@@ -1593,7 +1614,6 @@ int prepare_tc_decode(const fml_lm* lm)
     if (lm_head_on_tensor_cores(lm) || decode_on_tensor_cores(lm))
     {
         FML_RC(gemm_tc_prepare(true, 0, false));
-        FML_RC(gemm_tc_prepare(true, 0, true));
     }
     return FML_OK;
 }
@@ -1627,7 +1647,6 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
     const bool wb = lm->weight_format == FML_WEIGHTS_BF16;
     FML_REQUIRE(!wb || lm->wb16_valid, "decode step: the bf16 weight copy is not ready");
     const bool dtc = decode_on_tensor_cores(lm);  // rows of LayerNorm, tcgen05 split-K, reduction
-    auto lo = [&](const std::vector<float*>& v, uint32_t l) { return lm->wlo_valid ? v[l] : nullptr; };
     for (uint32_t l = 0; l < c.n_layer; ++l)
     {
         {
@@ -1643,7 +1662,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
                 // for layer 0, the LayerNorm after the embedding) made it
                 if (l == 0) FML_RC(launch_layernorm(lm->ln, lm->x, lm->ln0[0], nullptr, nullptr, B, d, d, d, 1e-5f, st));
                 a.x = lm->ln;
-                FML_RC(decode_tc_gemm<EPI_QKV>(lm, a, lo(lm->wqkv_lo, l), 2, st, pdl && l > 0));
+                FML_RC(decode_tc_gemm<EPI_QKV>(lm, a, 2, st, pdl && l > 0));
             }
             else
                 FML_RC((decode_gemv<EPI_QKV, true>(lm, a, 2, st, pdl)));
@@ -1662,7 +1681,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             {
                 a.ln_out = lm->ln;  // LN1(buf) for fc
                 a.ln_gamma = lm->ln1[l];
-                FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wproj_lo, l), 4, st, pdl));
+                FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, 4, st, pdl));
             }
             else if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->buf, lm->x, 2 * l, 4, st, pdl));
             else
@@ -1681,7 +1700,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
             if (dtc)
             {
                 a.x = lm->ln;  // LN1(buf), made by the projection's reduction
-                FML_RC(decode_tc_gemm<EPI_GELU>(lm, a, lo(lm->wfc_lo, l), 5, st, pdl));
+                FML_RC(decode_tc_gemm<EPI_GELU>(lm, a, 5, st, pdl));
             }
             else
                 FML_RC((decode_gemv<EPI_GELU, true>(lm, a, 5, st, pdl && (!tp || lm->ar_fused))));
@@ -1697,7 +1716,7 @@ int enqueue_step(fml_lm* lm, uint32_t* next_out, float* logits, cudaStream_t st,
                 // LN0 of the next layer, or ln_f after the last, for the lm_head
                 a.ln_out = lm->ln;
                 a.ln_gamma = l + 1 < c.n_layer ? lm->ln0[l + 1] : lm->lnf;
-                FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, lo(lm->wmlp_lo, l), 6, st, pdl));
+                FML_RC(decode_tc_gemm<EPI_RESID>(lm, a, 6, st, pdl));
             }
             else if (lm->ar_fused) FML_RC(gemv_allreduce(lm, a, lm->x, lm->buf, 2 * l + 1, 6, st, pdl));
             else
