@@ -1569,14 +1569,19 @@ bool lm_head_on_tensor_cores(const fml_lm* lm)
 }
 
 // The decode contractions on the tcgen05 GEMM (split K, then a reduction
-// with the GEMV's epilogue): TF32x3 math, fp32 weights, one rank, more than
-// 32 rows and d >= 1024 (config 4: 64 rows) -- there the CUDA-core GEMV's 8
-// row chunks re-read each weight 8 times and walk 5-54 column-group rounds
-// per warp.
+// with the GEMV's epilogue): TF32x3 math, fp32 weights, one rank, at least
+// 32 rows and d a multiple of 1024 -- there the CUDA-core GEMV's row chunks
+// re-read each weight and walk many column-group rounds per warp.  Measured
+// on config 4's shape (us per step, GEMV / tensor cores): 64 rows 2 620 /
+// 2 170, 32 rows 1 469 / 1 387, 16 rows 838 / 989, 8 rows 584 / 828.
 bool decode_on_tensor_cores(const fml_lm* lm)
 {
-    return lm->prefill_math == FML_MATH_TF32X3 && lm->weight_format == FML_WEIGHTS_FP32 && lm->tp_world == 1 &&
-           lm->batch > 32 && lm->cfg.d_model % 1024 == 0 && lm->cfg.d_model <= 4096;
+    const bool able = lm->prefill_math == FML_MATH_TF32X3 && lm->weight_format == FML_WEIGHTS_FP32 &&
+                      lm->tp_world == 1 && lm->cfg.d_model % 1024 == 0 && lm->cfg.d_model <= 4096;
+    const char* e = getenv("FML_DECODE_TC");  // tuning override: 0 never, 1 at any batch
+    if (e && e[0] == '0') return false;
+    if (e && e[0] == '1') return able;
+    return able && lm->batch >= 32;
 }
 
 // One decode contraction y = epilogue(A . W^T) on the tensor cores: the K
