@@ -432,6 +432,28 @@ def test_config4_all_sequences_teacher_forced(fp32_matmul):
                           list(range(c["batch"])), P, N)
 
 
+@pytest.mark.parametrize("batch", [32, 16])
+def test_config4_one_gpu_share_teacher_forced(batch, fp32_matmul):
+    """Config 4's sequences as one GPU holds them at 2 and 4 GPUs: the first
+    32 (the tensor-core decode contractions, split K, from 32 rows) or 16
+    (the CUDA-core GEMVs), every generated row teacher-forced against the
+    PyTorch fp32 restatement."""
+    from freeml_b200.lm import CONFIGS, prompt_tokens
+    c = CONFIGS[4]
+    sh = c["shape"]
+    s = O.LMShape(sh.vocab, sh.context, sh.d_model, sh.n_head, sh.n_layer)
+    w = O.init_weights(s, c["wseed"])
+    prompts = prompt_tokens(c["pseed"], sh.vocab, c["batch"], c["prompt"])[:batch]
+    lm = _lm(s, batch)
+    lm.bind(w)
+    toks, logits = lm.generate(prompts, c["new"], want_logits=True)
+    lm.close()
+    P, N = c["prompt"], c["new"]
+    params = torch.from_numpy(w).cuda()
+    _check_teacher_forced(f"config4_{batch}seq_torch", _torch_rows(params, sh, toks, P, N), toks, logits,
+                          list(range(batch)), P, N)
+
+
 def test_config5_teacher_forced_vs_torch_fp32(fp32_matmul):
     """BASELINE config 5 on one GPU: V32000 C4096 d4096 H32 L32 (6.6e9 fp32
     parameters, seeded N(0, 0.02) on the device), 8 sequences of 1024 prompt
