@@ -398,7 +398,13 @@ FML_API int fml_lm_tp_error_count(uint64_t* count);
 FML_API int fml_tp_flag_check(uint32_t epoch, uint32_t slot, uint32_t nslot, uint32_t flag, int* reached);
 
 /* Precision of the prefill contractions (FML_MATH_*; default
- * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy). */
+ * FML_MATH_TF32X3: tcgen05 tensor cores at fp32-level accuracy).  Under
+ * FML_MATH_TF32X3 with fp32 weights on one rank, the decode step's
+ * contractions also run on tcgen05 from 32 rows when d_model is a multiple
+ * of 1024, and the logits head from 32 rows when the vocabulary spans at
+ * least 148 column tiles of 128; fewer rows stay on the CUDA-core GEMVs.
+ * FML_MATH_FP32 keeps every contraction on CUDA cores; FML_MATH_TF32 runs
+ * the prefill as one tf32 pass and the decode step on CUDA cores. */
 FML_API int fml_lm_set_prefill_math(fml_lm* lm, int mode);
 
 
