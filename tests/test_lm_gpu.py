@@ -163,20 +163,23 @@ def test_graph_and_eager_steps_are_identical(golden):
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
 
 
+@pytest.mark.parametrize("batch", [8, 32])
 @pytest.mark.parametrize("graph_steps", ["16", "5"])
-def test_multi_step_graphs_match_single_steps(graph_steps, monkeypatch):
+def test_multi_step_graphs_match_single_steps(graph_steps, batch, monkeypatch):
     """fml_lm_steps (several decode steps per graph, each step's embed under
     programmatic dependent launch behind the previous finalize) leaves the
     same KV cache, positions and pending tokens as one fml_lm_step per token:
     the step after them gives bit-identical tokens and logits.  37 steps =
-    graphs of 16 + 16 + 5 (or 5 x 7 + 2): full and remainder graphs."""
+    graphs of 16 + 16 + 5 (or 5 x 7 + 2): full and remainder graphs; at 8
+    sequences attention_kernel runs 4-warp CTAs in split clusters, at 32 the
+    16-warp CTAs of the bench's shape."""
     monkeypatch.setenv("FML_LM_GRAPH_STEPS", graph_steps)
     from freeml_b200.lm import CONFIGS, NanoLM, prompt_tokens, random_params
     c = CONFIGS[3]
     s = c["shape"]
     params = random_params(s, c["wseed"], 0)
-    prompts = prompt_tokens(c["pseed"], s.vocab, 8, c["prompt"])
-    lm = NanoLM(s, 8)
+    prompts = prompt_tokens(c["pseed"], s.vocab, batch, c["prompt"])
+    lm = NanoLM(s, batch)
     lm.bind(params)
     lm.prefill(prompts)
     first = lm.pending_tokens().clone()
@@ -191,7 +194,7 @@ def test_multi_step_graphs_match_single_steps(graph_steps, monkeypatch):
         pend = lm.pending_tokens().clone()
         toks, logits = lm.step(want_logits=True)
         outs.append((pend.cpu().numpy(), toks.cpu().numpy().copy(), logits.cpu().numpy().copy(),
-                     lm.position(0), lm.position(7)))
+                     lm.position(0), lm.position(batch - 1)))
     # a call that would take a sequence past the context fails before any work
     from freeml_b200._lib import FmlError
     with pytest.raises(FmlError):
