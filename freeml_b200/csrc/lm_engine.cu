@@ -2535,7 +2535,7 @@ int fml_lm_steps(fml_lm* lm, uint32_t n, fml_stream_t stream)
     if (n == 0) return FML_OK;
     FML_RC(check_step_state(lm, "fml_lm_steps"));
     for (uint32_t b = 0; b < lm->batch; ++b)
-        if (lm->hpos[b] + n > lm->cfg.context)
+        if ((uint64_t)lm->hpos[b] + n > lm->cfg.context)  // 64-bit: no wrap for any n
             return set_error(FML_ERR_STATE, "fml_lm_steps: %u steps take sequence %u past the context limit (%u)", n,
                              b, lm->cfg.context);
     cudaStream_t st = as_stream(stream);

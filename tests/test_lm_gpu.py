@@ -199,6 +199,8 @@ def test_multi_step_graphs_match_single_steps(graph_steps, batch, monkeypatch):
     from freeml_b200._lib import FmlError
     with pytest.raises(FmlError):
         lm.steps(s.context)
+    with pytest.raises(FmlError):  # a count whose sum with the position wraps 32 bits
+        lm.steps(2**32 - 1)
     assert lm.position(0) == c["prompt"] + 38
     lm.close()
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
