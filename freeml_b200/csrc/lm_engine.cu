@@ -2637,6 +2637,9 @@ int fml_lm_rewind(fml_lm* lm, uint32_t pos, const uint32_t* pending, int pending
     FML_REQUIRE(lm->batch > 0 && pos >= 1 && pos < lm->cfg.context, "fml_lm_rewind: bad position %u", pos);
     cudaStream_t st = as_stream(stream);
     const uint32_t B = lm->batch;
+    for (uint32_t b = 0; b < B; ++b)  // rows past a sequence's position were never written
+        FML_REQUIRE(pos <= lm->hpos[b], "fml_lm_rewind: position %u is past sequence %u's %u cached rows", pos, b,
+                    lm->hpos[b]);
     if (pending_on_host)
     {
         FML_CUDA_TRY(cudaStreamSynchronize(st));  // host_io may still feed an earlier copy

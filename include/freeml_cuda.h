@@ -464,9 +464,10 @@ FML_API int fml_lm_set_graph(fml_lm* lm, int use_graph);
 FML_API int fml_lm_pending(fml_lm* lm, uint32_t* out, fml_stream_t stream);
 
 /* Position (tokens held in the cache) of sequence b, and rewinding every
- * active sequence to `pos` (cache rows [0, pos) are kept) with the given
- * pending tokens ([batch], host or device memory).  The device form is
- * stream-ordered and does not synchronise. */
+ * active sequence to `pos` (cache rows [0, pos) are kept; pos must not pass
+ * any sequence's position) with the given pending tokens ([batch], host or
+ * device memory).  The device form is stream-ordered and does not
+ * synchronise. */
 FML_API int fml_lm_get_position(fml_lm* lm, uint32_t b, uint32_t* pos);
 FML_API int fml_lm_rewind(fml_lm* lm, uint32_t pos, const uint32_t* pending, int pending_on_host,
                           fml_stream_t stream);

@@ -270,6 +270,11 @@ def test_rewind_replays_the_same_stream(golden):
     lm.rewind(16 + 5, toks[:, 16 + 5])
     again = [lm.step()[0].cpu().numpy().view(np.uint32)[0] for _ in range(10)]
     np.testing.assert_array_equal(np.array(again, np.uint32), toks[0, 16 + 6:16 + 16])
+    # forward past the cached rows is refused (those rows were never written)
+    from freeml_b200._lib import FmlError
+    with pytest.raises(FmlError):
+        lm.rewind(lm.position(0) + 1, toks[:, 16 + 5])
+    assert lm.position(0) == 16 + 15
     lm.close()
 
 
