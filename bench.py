@@ -123,6 +123,20 @@ def dist_env():
     return ws, rank, local
 
 
+def decode_contraction_path(d: int, vocab: int, b_local: int, tp: bool) -> str:
+    """Where the engine runs one rank's decode contractions (default math
+    mode TF32x3, fp32 weights; vocab = the rank's vocabulary rows): the
+    rule of lm_engine.cu's
+    decode_on_tensor_cores (one rank, d a multiple of 1024 up to 4096, at
+    least 32 rows) and lm_head_on_tensor_cores (at least 32 rows and 148
+    column tiles of 128 in the vocabulary)."""
+    dense = not tp and d % 1024 == 0 and d <= 4096 and b_local >= 32
+    head = b_local >= 32 and -(-vocab // 128) >= 148
+    where = "tcgen05 (TF32x3, K split + reduction)" if dense else "the CUDA cores (fp32 GEMVs)"
+    head_where = "tcgen05 (TF32x3)" if head else "a CUDA-core GEMV with fused argmax"
+    return f"decode contractions on {where}, logits head on {head_where}"
+
+
 def workload_config(n_gpus, b_local, tp=False):
     from freeml_b200.lm import CONFIGS
     c = CONFIGS[CONFIG]
@@ -574,8 +588,9 @@ def main():
                            allreduce=("NCCL" if args.tp_nccl else "one-shot kernel over NVLink peer memory "
                                       "(decode; prefill: NCCL)") if tp else None,
                            engine="per-operation kernels (CUDA graphs of 16 engine steps, programmatic "
-                                  "dependent launch between all kernels); decode contractions on the CUDA cores "
-                                  "(fp32), prefill contractions on tcgen05 (TF32x3)"),
+                                  "dependent launch between all kernels); "
+                                  + decode_contraction_path(s.d_model, -(-s.vocab // (ws if tp else 1)), B, tp)
+                                  + "; prefill contractions on tcgen05 (TF32x3)"),
             "gpu_launches": int(launches),
             "clocks": clocks,
             "roofline": {"bound": "hbm", "kernel": k_name,

@@ -101,3 +101,21 @@ def test_kernel_times_from_stamps():
     assert kt["by_class_ns"] == {"embed": 10, "qkv": 15, "attention": 50, "finalize": 5}
     assert kt["launches"] == {"embed": 1, "qkv": 1, "attention": 1, "finalize": 1}
     assert kt["total_ns"] == 80 == sum(kt["by_class_ns"].values())
+
+
+def test_decode_contraction_path_follows_the_engine_rule():
+    """The bench line names where the decode contractions ran: tensor cores
+    from 32 rows with d a multiple of 1024 on one rank (config 4 at one and
+    two GPUs), CUDA-core GEMVs otherwise (config 3, config 4 at 16 rows per
+    GPU, config 5 with or without tensor parallelism); the logits head on
+    tensor cores from 32 rows and 148 column tiles of the rank's vocabulary."""
+    p = bench.decode_contraction_path
+    assert p(512, 4096, 32, False).startswith("decode contractions on the CUDA cores")
+    assert "logits head on a CUDA-core GEMV" in p(512, 4096, 32, False)  # 32 column tiles
+    assert p(1024, 32000, 64, False) == ("decode contractions on tcgen05 (TF32x3, K split + reduction), "
+                                         "logits head on tcgen05 (TF32x3)")
+    assert p(1024, 32000, 32, False).startswith("decode contractions on tcgen05")
+    assert p(1024, 32000, 16, False).startswith("decode contractions on the CUDA cores")
+    assert "logits head on a CUDA-core GEMV" in p(1024, 32000, 16, False)
+    assert p(4096, 32000, 8, False).startswith("decode contractions on the CUDA cores")
+    assert p(4096, 16000, 8, True).startswith("decode contractions on the CUDA cores")
